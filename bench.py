@@ -1,0 +1,431 @@
+"""Benchmark of the B200 depthwise Conv1D training path (FWD + dX + dK, FP32).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one FWD + dX + dK pass (dK deterministic two-pass, written, not
+accumulated, so no zero-fill exists) over one batch of the primary workload,
+B=16384 per GPU, H=128, L=48, K=48 (weak scaling: at N=8 the job is the
+batch-sharded x[131072,128,48] configuration; for N>1 each step also
+all-reduces dK[128,48] over NCCL).  Inputs are resident in HBM and each of
+x, dy, y, dX is 402 MB, larger than the 126 MB L2, so no L2 flush is needed.
+
+Printed (rank 0, one JSON line): ``value`` = whole-job algorithmic GB/s of
+FWD+dX+dK (bytes per phase (2*B*H*L + H*K)*4, the reference's formula) over
+the device-timed step (CUDA events, max over ranks); ``aggregate_ms`` = sum of
+the three phases' separately timed mean latencies (the reference's headline
+protocol); ``roofline`` for the dominant kernel; ``cpu_baseline`` = the
+reference's PyTorch CPU path timed on this host; ``e2e`` = the same pass
+through the host-buffer API (pinned host tensors, copies inside the timed
+region); ``clocks`` sampled by NVML during the timed region.
+
+``--impl reference`` times the reference's own CPU implementation (its PyTorch
+path F.pad + grouped conv1d with autograd, restated in oracle/) on this host's
+cores, on a bounded sample of the same workload, and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "FWD+dX+dK aggregate ms & GB/s at B=16384,H=128,L=48,K=48 FP32; % roofline"
+B_PER_GPU, H, L, K = 16384, 128, 48, 48
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        d["source"] = "measured"
+        return d
+    return dict(FALLBACK_PEAKS)
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling (NVML) during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.01) -> None:
+        self.idx, self.period = device_index, period_s
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thr = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+        except Exception as exc:  # NVML missing: report no samples, never guess
+            self._nv = None
+            self.error = repr(exc)
+
+    def _run(self) -> None:
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(int(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)))
+                mask = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thr is not None:
+            self._thr.join()
+        return False
+
+    def summary(self) -> dict:
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": sorted(self.reasons - {"gpu_idle"})}
+
+
+# ---------------------------------------------------------------------------
+# Device-resident timing
+# ---------------------------------------------------------------------------
+def phase_bytes(B: int) -> int:
+    return (2 * B * H * L + H * K) * 4
+
+
+def time_loop(fn, iters: int, stream) -> float:
+    """Mean ms of fn() over iters, CUDA events on `stream`, synchronised on both sides."""
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(iters):
+        fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def cpu_baseline(seconds_per_phase: float = 3.0, B_sample: int = 512) -> dict:
+    """The reference's PyTorch CPU path (restated in oracle/reference_torch.py) on
+    this host's cores: FWD, dX, dK timed separately (graph built outside the
+    timed region, as benchmark/benchmark_pytorch.py:97-144 does)."""
+    from oracle import reference_torch as ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, k, dy = ref.make_inputs(B_sample, H, L, K, seed=42)
+    xr = x.clone().requires_grad_(True)
+    kr = k.clone().requires_grad_(True)
+
+    def run_fwd():
+        with torch.no_grad():
+            ref.depthwise_same(x, k)
+
+    def run_dx():
+        y = ref.depthwise_same(xr, k)
+        torch.autograd.grad(y, xr, dy)
+
+    def run_dk():
+        y = ref.depthwise_same(x, kr)
+        torch.autograd.grad(y, kr, dy)
+
+    means = {}
+    for name, fn in (("fwd", run_fwd), ("bwd_input", run_dx), ("bwd_weight", run_dk)):
+        for _ in range(3):
+            fn()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds_per_phase and n >= 5:
+                break
+        means[name] = 1e3 * el / n
+    agg = sum(means.values())
+    return {
+        "value": 3 * phase_bytes(B_sample) / (agg / 1e3) / 1e9,
+        "unit": "GB/s",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "aggregate_ms": agg,
+        "phase_ms": means,
+        "sample": (f"B={B_sample} of the primary shape (H=128,L=48,K=48); reference PyTorch CPU path "
+                   f"F.pad + conv1d(groups=H) with autograd for dX/dK, 3 warm-up + >= {seconds_per_phase:.0f} s "
+                   "per phase; restated in oracle/reference_torch.py (the reference module needs pycuda to import)"),
+    }
+
+
+def load_traffic() -> dict | None:
+    p = ROOT / "profiles" / "dram_traffic_primary.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return None
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
+    from pathtile_b200 import build, ops, runtime
+    from pathtile_b200.host import HostPipeline
+
+    build.build()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    B = B_PER_GPU
+    g = torch.Generator(device=dev).manual_seed(42 + rank)
+    x = torch.randn(B, H, L, device=dev, generator=g)
+    k = torch.randn(H, K, device=dev, generator=torch.Generator(device=dev).manual_seed(42)) / (K ** 0.5)
+    dy = torch.randn(B, H, L, device=dev, generator=g)
+    y = torch.empty_like(x)
+    gx = torch.empty_like(x)
+    gk = torch.empty_like(k)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        ops.fwd(x, k, y)
+        ops.dx(dy, k, gx)
+        ops.dk(dy, x, gk, mode="deterministic")
+        if dist is not None:
+            dist.all_reduce(gk)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        step_ms = time_loop(step, args.steps, stream)
+    if dist is not None:
+        t = torch.tensor([step_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms = float(t.item())
+
+    # Per-phase means, each phase timed separately (reference protocol).
+    iters = max(20, min(200, args.steps))
+    phase_ms = {
+        "fwd": time_loop(lambda: ops.fwd(x, k, y), iters, stream),
+        "bwd_input": time_loop(lambda: ops.dx(dy, k, gx), iters, stream),
+        "bwd_weight": time_loop(lambda: ops.dk(dy, x, gk, mode="deterministic"), iters, stream),
+    }
+    if dist is not None:
+        t = torch.tensor(list(phase_ms.values()), device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        phase_ms = dict(zip(phase_ms, map(float, t.tolist())))
+
+    # End to end through the host-buffer API: pinned host inputs in, host outputs back.
+    pin = dict(device="cpu", pin_memory=True)
+    x_h = torch.empty(B, H, L, **pin)
+    dy_h = torch.empty(B, H, L, **pin)
+    k_h = torch.empty(H, K, **pin)
+    x_h.copy_(x)
+    dy_h.copy_(dy)
+    k_h.copy_(k)
+    y_h = torch.empty(B, H, L, **pin)
+    gx_h = torch.empty(B, H, L, **pin)
+    gk_h = torch.empty(H, K, **pin)
+    pipe = HostPipeline(H, L, K, chunk_b=args.e2e_chunk, device=local_rank)
+
+    def e2e_step():
+        pipe.run(x_h, k_h, dy_h, y_h, gx_h, gk_h)
+        if dist is not None:
+            dist.all_reduce(pipe.gk)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e2e_iters = max(3, min(args.e2e_steps, args.steps))
+    e2e_ms = time_loop(e2e_step, e2e_iters, stream)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d, d2h = pipe.bytes_per_call(B)
+    err = ops.device_error()
+
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    hbm = float(peaks["hbm_gbs"])
+    pb = phase_bytes(B)
+    total_bytes = 3 * pb * world
+    dominant = max(phase_ms, key=phase_ms.get)
+    achieved = pb / (phase_ms[dominant] / 1e3) / 1e9
+    sm_mhz = clocks.summary()["sm_mhz"] or 1965.0
+    fma_peak = runtime.fp32_fma_peak_tflops(torch.cuda.get_device_properties(dev).multi_processor_count,
+                                            float(sm_mhz))
+    roof_ms = runtime.roofline_ms(B, H, L, K, hbm, fma_peak)
+    traffic = load_traffic()
+    kernel_names = {"fwd": "conv_rows_kernel<48,48,FWD,TMA3D>", "bwd_input": "conv_rows_kernel<48,48,DX,TMA3D>",
+                    "bwd_weight": "dk_rows_kernel<48,48,TMA3D> + dk_reduce_kernel"}
+    result = {
+        "metric": METRIC,
+        "value": total_bytes / (step_ms / 1e3) / 1e9,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: x, dy ~ N(0,1), k ~ N(0,1)/sqrt(K), seeded, generated on device",
+        "config": {
+            "workload": "primary: B=16384 per GPU, H=128, L=48, K=48 (N=8: batch-sharded x[131072,128,48])",
+            "B_per_gpu": B, "global_batch": B * world, "H": H, "L": L, "K": K,
+            "parallelism": f"dp{world}" + (" + NCCL all_reduce(dK)" if world > 1 else ""),
+            "dk_mode": "deterministic two-pass",
+            "l2": "inputs larger than L2 (402,653,184 B per activation tensor vs 126 MB L2)",
+        },
+        "aggregate_ms": sum(phase_ms.values()),
+        "phases": {p: {"ms": ms, "GB/s": pb / (ms / 1e3) / 1e9,
+                       "frac_of_roofline": roof_ms / ms} for p, ms in phase_ms.items()},
+        "aggregate_frac_of_roofline": 3 * roof_ms / sum(phase_ms.values()),
+        "roofline": {
+            "bound": "hbm",
+            "kernel": kernel_names[dominant],
+            "achieved": achieved,
+            "peak": hbm,
+            "unit": "GB/s",
+            "frac": achieved / hbm,
+            "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured" else "fallback",
+            "algorithmic_bytes_per_launch": pb,
+            "traffic": (traffic or {}).get(dominant),
+            "fp32_fma_peak_tflops_at_sampled_clock": fma_peak,
+        },
+        "e2e": {
+            "value": total_bytes / (e2e_ms / 1e3) / 1e9,
+            "unit": "GB/s",
+            "ms_per_step": e2e_ms,
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "api": "pathtile_b200.host.HostPipeline.run (pinned host tensors)",
+        },
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks.summary(),
+        "device_error_word": err,
+    }
+    if not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    return result
+
+
+def run_reference(args, rank: int) -> dict | None:
+    """The reference's CPU path on this host, same metric and unit."""
+    if rank != 0:
+        return None
+    from oracle import reference_torch as ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    Bs = args.ref_sample_b
+    x, k, dy = ref.make_inputs(Bs, H, L, K, seed=42)
+
+    def step():
+        xr = x.clone().requires_grad_(True)
+        kr = k.clone().requires_grad_(True)
+        with torch.no_grad():
+            ref.depthwise_same(x, k)
+        y = ref.depthwise_same(xr, kr)
+        torch.autograd.grad(y, (xr, kr), dy)
+
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(times)
+    val = 3 * phase_bytes(Bs) / (ms / 1e3) / 1e9
+    sample = (f"B={Bs} of the primary shape (H=128,L=48,K=48) per step: FWD under no_grad, then one "
+              "forward + autograd for dX and dK; reference PyTorch CPU path restated in oracle/reference_torch.py")
+    return {
+        "metric": METRIC, "impl": "reference", "value": val, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: x, dy ~ N(0,1), k ~ N(0,1)/sqrt(K), seeded",
+        "config": {"workload": "primary: B=16384 per GPU, H=128, L=48, K=48 (bounded CPU sample per step)",
+                   "B_sample": Bs, "H": H, "L": L, "K": K, "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--e2e-chunk", type=int, default=2048)
+    ap.add_argument("--cpu-seconds", type=float, default=3.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-sample-b", type=int, default=256)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        res = run_ours(args, rank, world, local_rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

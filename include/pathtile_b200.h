@@ -1,0 +1,152 @@
+/*
+ * pathtile_b200.h -- C ABI of the B200 (sm_100a) short depthwise Conv1D
+ * training path: forward (FWD), input gradient (dX) and weight gradient (dK),
+ * FP32, for sequence length L <= 48 and filter length K <= 48.
+ *
+ * Layout: activations are contiguous float32 [B, H, L] (one contiguous row of
+ * L floats per (batch b, channel h) sequence); filters and filter gradients
+ * are contiguous float32 [H, K].  All pointers are DEVICE pointers of the
+ * calling thread's current CUDA device and must be 16-byte aligned (every
+ * cudaMalloc / PyTorch allocation is).  `stream` is a cudaStream_t (NULL is
+ * the legacy default stream).  Every call is asynchronous with respect to the
+ * host; errors found before launch are reported synchronously.
+ *
+ * Padding convention ("same" output length, as the reference PyTorch path
+ * F.pad(x, (K//2, K-1-K//2)) + grouped conv1d,
+ * benchmark/benchmark_shape_sweep_ampere.py:220-239):
+ *   y [b,h,t] = sum_{j<K} x [b,h,t+j-K/2] * k[h,j]         (zero outside 0..L-1)
+ *   dx[b,h,t] = sum_{j<K} dy[b,h,t-j+K/2] * k[h,j]
+ *   dk[h,j]   = sum_{b,t} dy[b,h,t] * x[b,h,t+j-K/2]
+ *
+ * Status codes follow the external-kernel bridge convention of the reference
+ * (benchmark/flashdwc_fp32_bridge.cu:15-20: 0 = ok, -2 = bad arguments);
+ * the other negative values are specific to this library.
+ */
+#ifndef PATHTILE_B200_H_
+#define PATHTILE_B200_H_
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define PT_API __attribute__((visibility("default")))
+#else
+#define PT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PT_OK 0
+#define PT_ERR_ARGS (-2)        /* null pointer, non-positive or mismatched dims */
+#define PT_ERR_UNSUPPORTED (-3) /* L > 48 or K > 48 (kernels are specialised) */
+#define PT_ERR_ALIGN (-4)       /* a pointer is not 16-byte aligned */
+#define PT_ERR_WORKSPACE (-5)   /* deterministic dK workspace missing or too small */
+#define PT_ERR_CUDA (-6)        /* a CUDA runtime/driver call or launch failed */
+#define PT_ERR_DEVICE (-7)      /* current device is not compute capability 10.x */
+
+#define PT_MAX_L 48
+#define PT_MAX_K 48
+
+/* dK reduction modes (pt_dk `mode`). */
+#define PT_DK_ATOMIC 0          /* one float atomicAdd per (CTA, h, j): dk += dK (dk pre-zeroed by caller) */
+#define PT_DK_DETERMINISTIC 1   /* two passes through a [CTA][K][h] workspace: dk = dK, bit-reproducible */
+#define PT_DK_DETERMINISTIC_ACCUMULATE 2 /* as 1, but dk += dK */
+
+/* Paths for pt_config / pt_set_config. */
+#define PT_PATH_FWD 0
+#define PT_PATH_DX 1
+#define PT_PATH_DK 2
+
+/*
+ * Forward pass.  Replaces the reference launch of dwconv1d_warptile_fwd via
+ * AmpereWarpRuntime.launch_fwd (kernels/warp_tiled_ampere.py:723-747, kernel
+ * :372-434) and, behind the legacy name surface, dwconv1d_fwd_shared
+ * (kernels/warp_tiled.py:151, launched at :853-885).
+ */
+PT_API int pt_fwd(const float* x, const float* k, float* y, int B, int H, int L, int K,
+           void* stream);
+
+/*
+ * Input gradient.  Replaces AmpereWarpRuntime.launch_bwd_input
+ * (kernels/warp_tiled_ampere.py:749-773, kernel :440-502) and
+ * dwconv1d_bwd_input_shared (kernels/warp_tiled.py:297, launched at :926-963).
+ */
+PT_API int pt_dx(const float* dy, const float* k, float* dx, int B, int H, int L, int K,
+          void* stream);
+
+/*
+ * Weight gradient.  Replaces AmpereWarpRuntime.launch_bwd_weight
+ * (kernels/warp_tiled_ampere.py:775-812, kernel :509-619; atomic semantics:
+ * dk must be zeroed by the caller, :890-893) and the deterministic two-pass
+ * path dwconv1d_warptile_bwd_weight_partials + dwconv1d_warptile_reduce_partials
+ * (kernels/warp_tiled_noatomic_optimized.py:881-1150, launched at :1473-1550).
+ * `ws`/`ws_bytes` is the caller-owned workspace of the deterministic modes
+ * (ignored by PT_DK_ATOMIC); its size is pt_dk_workspace_bytes(B,H,L,K).
+ */
+PT_API int pt_dk(const float* dy, const float* x, float* dk, int B, int H, int L, int K,
+          int mode, void* ws, size_t ws_bytes, void* stream);
+
+/*
+ * Bytes of deterministic-dK workspace for this shape under the active launch
+ * configuration on the current device (the reference sizes its cached
+ * [H,K,num_btiles] buffer at kernels/warp_tiled_noatomic_optimized.py:1448-1471).
+ * Returns 0 for invalid shapes.
+ */
+PT_API size_t pt_dk_workspace_bytes(int B, int H, int L, int K);
+
+/*
+ * Launch configuration that the frozen PathTile table selects for `path`
+ * (PT_PATH_*) at this shape.  out[0] = rows per tile, out[1] = pipeline
+ * stages, out[2] = CTAs per SM, out[3] = 1 if an (L,K)-specialised kernel
+ * exists, else 0 (generic kernel).  `n` is the capacity of `out` (>= 4).
+ * Mirrors the frozen constants that the reference bakes into CUDA_TEMPLATE
+ * (WARPS_PER_BLOCK / BWDK_BLOCK, kernels/warp_tiled_ampere.py:668-672,
+ * selected by scripts/aggregate_pathtile_results.py:222-240).
+ */
+PT_API int pt_config(int path, int B, int H, int L, int K, int* out, int n);
+
+/*
+ * Override the launch configuration of `path` for all shapes (rows_per_tile in
+ * {32,64,128,256}, stages in {2,3,4}, ctas_per_sm in {1,2,3,4}); passing
+ * rows_per_tile = 0 restores the frozen table.  Used by the offline PathTile
+ * candidate sweep, the counterpart of recompiling CUDA_TEMPLATE per candidate
+ * (benchmark/benchmark_pathtile_candidate_sweep.py:493-560).  Not thread-safe
+ * with concurrent launches.
+ */
+PT_API int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm);
+
+/*
+ * Resources of the kernel `path` would launch for this shape: out[0] registers
+ * per thread, out[1] static shared bytes, out[2] local (spill) bytes per
+ * thread, out[3] threads per CTA, out[4] dynamic shared bytes, out[5] resident
+ * CTAs per SM (occupancy API), out[6] grid size, out[7] 1 if specialised.
+ * `n` >= 8.  Counterpart of AmpereWarpRuntime.resource_report, which reads the
+ * compiled function's num_regs / shared_size_bytes / local_size_bytes
+ * (kernels/warp_tiled_ampere.py:814-833).
+ */
+PT_API int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n);
+
+/*
+ * Device-side error word: kernels never spin without bound; a wait that runs
+ * past its limit sets a bit here and the kernel returns early.  Reads (and
+ * with clear != 0, resets) the word of the current device; synchronises the
+ * device.  The reference has no device-side error channel (its kernels return
+ * silently on L > 48, kernels/warp_tiled_ampere.py:390).
+ */
+PT_API int pt_device_error(unsigned int* out, int clear);
+
+/* Human-readable text for a status code. */
+PT_API const char* pt_status_string(int status);
+
+/* CUDA error code of the last PT_ERR_CUDA on this host thread (0 if none). */
+PT_API int pt_last_cuda_error(void);
+
+/* Library version: major*10000 + minor*100 + patch. */
+PT_API int pt_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PATHTILE_B200_H_ */

@@ -1,0 +1,101 @@
+"""ctypes binding of ``libpathtile_b200.so`` (the C ABI in include/pathtile_b200.h).
+
+The shared library is built in-tree by :mod:`pathtile_b200.build`.  There is
+no fallback: if the library is missing or cannot be loaded, every entry point
+raises.  The binding exposes the raw functions; tensor-level wrappers live in
+:mod:`pathtile_b200.ops`.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libpathtile_b200.so"
+
+PT_OK = 0
+PT_ERR_ARGS = -2
+PT_ERR_UNSUPPORTED = -3
+PT_ERR_ALIGN = -4
+PT_ERR_WORKSPACE = -5
+PT_ERR_CUDA = -6
+PT_ERR_DEVICE = -7
+
+PT_DK_ATOMIC = 0
+PT_DK_DETERMINISTIC = 1
+PT_DK_DETERMINISTIC_ACCUMULATE = 2
+
+PT_PATH_FWD = 0
+PT_PATH_DX = 1
+PT_PATH_DK = 2
+
+PT_MAX_L = 48
+PT_MAX_K = 48
+
+# Every symbol include/pathtile_b200.h declares, with (restype, argtypes).
+_c_int, _c_size, _vp, _fp = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "pt_fwd": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "pt_dx": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "pt_dk": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
+    "pt_dk_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
+    "pt_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int]),
+    "pt_set_config": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
+    "pt_kernel_info": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int]),
+    "pt_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint), _c_int]),
+    "pt_status_string": (ctypes.c_char_p, [_c_int]),
+    "pt_last_cuda_error": (_c_int, []),
+    "pt_version": (_c_int, []),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class PathTileError(RuntimeError):
+    """A non-zero status from the native library."""
+
+    def __init__(self, status: int, what: str, detail: str = "") -> None:
+        self.status = status
+        msg = f"{what} failed with status {status}: {status_string(status)}"
+        if detail:
+            msg += f" ({detail})"
+        super().__init__(msg)
+
+
+def load() -> ctypes.CDLL:
+    """Load the native library once; raise if it is absent (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"native library {LIB_PATH} is missing; build it with "
+                "`python -m pathtile_b200.build` (nvcc, sm_100a). There is no CPU fallback."
+            )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def status_string(status: int) -> str:
+    return load().pt_status_string(int(status)).decode()
+
+
+def last_cuda_error() -> int:
+    return int(load().pt_last_cuda_error())
+
+
+def check(status: int, what: str) -> None:
+    if status != PT_OK:
+        detail = ""
+        if status == PT_ERR_CUDA:
+            detail = f"cuda error {last_cuda_error()}"
+        raise PathTileError(status, what, detail)

@@ -1,0 +1,480 @@
+// pt_api.cu -- C ABI of the library (declared in include/pathtile_b200.h):
+// argument checks, tile planning, TMA descriptor encoding and launches.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "pathtile_b200.h"
+#define PT_KERNELS_IMPL 1
+#include "pt_frozen_config.h"
+#include "pt_kernels.cuh"
+#include "pt_registry.h"
+
+// Device error word (one per device context); kernels receive its address.
+__device__ unsigned int g_pt_device_error;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kGenericRows = 128;
+
+thread_local int t_last_cuda_error = 0;
+
+struct DeviceInfo {
+  bool ready = false;
+  int sm_count = 0;
+  int major = 0;
+  int minor = 0;
+  int max_smem = 0;  // opt-in dynamic shared memory per block
+  unsigned* err = nullptr;
+  std::unordered_map<const void*, size_t> smem_attr;  // max dynamic smem already granted
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+std::once_flag g_once;
+std::vector<pt::Entry>* g_entries = nullptr;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+pt::LaunchCfg g_override[3];
+bool g_has_override[3] = {false, false, false};
+
+int cuda_fail(cudaError_t e) {
+  t_last_cuda_error = static_cast<int>(e);
+  return PT_ERR_CUDA;
+}
+
+void init_once() {
+  g_entries = new std::vector<pt::Entry>();
+  pt::register_shard_0(*g_entries);
+  pt::register_shard_1(*g_entries);
+  pt::register_shard_2(*g_entries);
+  pt::register_shard_3(*g_entries);
+  pt::register_shard_4(*g_entries);
+  pt::register_shard_5(*g_entries);
+  pt::register_shard_6(*g_entries);
+  pt::register_shard_7(*g_entries);
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+  if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+          cudaSuccess &&
+      q == cudaDriverEntryPointSuccess) {
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  (void)cudaGetLastError();
+}
+
+// Current device's info; PT_ERR_DEVICE unless it is compute capability 10.0.
+int current_device(DeviceInfo*& di) {
+  std::call_once(g_once, init_once);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return PT_ERR_DEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    if ((e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return cuda_fail(e);
+    if ((e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+      return cuda_fail(e);
+    if ((e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+      return cuda_fail(e);
+    if ((e = cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) !=
+        cudaSuccess)
+      return cuda_fail(e);
+    if (d.major == 10 && d.minor == 0) {
+      void* p = nullptr;
+      if ((e = cudaGetSymbolAddress(&p, g_pt_device_error)) != cudaSuccess) return cuda_fail(e);
+      d.err = static_cast<unsigned*>(p);
+    }
+    d.ready = true;
+  }
+  if (d.major != 10 || d.minor != 0) return PT_ERR_DEVICE;
+  di = &d;
+  return PT_OK;
+}
+
+int ensure_smem_attr(DeviceInfo& di, const void* func, size_t bytes) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = di.smem_attr.find(func);
+  if (it != di.smem_attr.end() && it->second >= bytes) return PT_OK;
+  cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e != cudaSuccess) return cuda_fail(e);
+  di.smem_attr[func] = bytes;
+  return PT_OK;
+}
+
+pt::LaunchCfg cfg_for(int path) {
+  return g_has_override[path] ? g_override[path] : pt::kFrozenCfg[path];
+}
+
+const pt::Entry* find_entry(int L, int K) {
+  for (const pt::Entry& e : *g_entries)
+    if (e.L == L && e.K == K) return &e;
+  return nullptr;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int round_up(int v, int q) { return (v + q - 1) / q * q; }
+
+struct Plan {
+  bool exact = false;
+  int loader = 0;
+  const void* func = nullptr;
+  pt::TileGeom g{};
+  int threads = 0;
+  size_t smem = 0;
+};
+
+// Row pitch (floats) for TMA3D tiles: 128-bit LDS by 8 consecutive rows hits
+// 8 distinct 16-byte bank groups iff pitch/4 is odd.
+int tma_pitch(int L) { return ((L / 4) % 2 == 1) ? L : L + 4; }
+
+int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::Entry& e, Plan& p) {
+  const pt::LaunchCfg cfg = cfg_for(path);
+  pt::TileGeom& g = p.g;
+  g.B = B;
+  g.H = H;
+  g.L = L;
+  g.K = K;
+  const int R = cfg.rows;
+  if (H <= R) {
+    g.Th = H;
+    g.Tb = R / H;
+    if (g.Tb > 256) g.Tb = 256;
+    g.nhb = 1;
+  } else {
+    g.Th = R;
+    g.Tb = 1;
+    g.nhb = (H + R - 1) / R;
+  }
+  g.Q = (B + g.Tb - 1) / g.Tb;
+  g.stages = cfg.stages;
+  p.loader = e.loader;
+  g.pitch = (e.loader == pt::LOAD_TMA3D) ? tma_pitch(L) : L;
+  const int T = g.Th * g.Tb;
+  const long long tile_bytes = static_cast<long long>(g.pitch) * T * 4;
+  long long stage = (tile_bytes + 1023) / 1024 * 1024;
+  const int n_in = (path == PT_PATH_DK) ? 2 : 1;
+  // Fewer stages when the ring would not fit the per-block shared memory.
+  while (g.stages > 2 &&
+         static_cast<long long>(n_in) * g.stages * stage + g.stages * 8 > di.max_smem)
+    --g.stages;
+  if (path == PT_PATH_DK) {
+    // The idle ring doubles as the [K][T] in-CTA reduction buffer at the end.
+    const long long red = static_cast<long long>(K) * T * 4;
+    if (n_in * g.stages * stage < red)
+      stage = ((red + n_in * g.stages - 1) / (n_in * g.stages) + 1023) / 1024 * 1024;
+  }
+  if (static_cast<long long>(n_in) * g.stages * stage + g.stages * 8 > di.max_smem) return PT_ERR_UNSUPPORTED;
+  g.stage_bytes = static_cast<unsigned>(stage);
+  g.tx_bytes = static_cast<unsigned>(tile_bytes);
+  p.smem = static_cast<size_t>(n_in) * g.stages * stage + static_cast<size_t>(g.stages) * 8;
+  p.threads = round_up(T, 32);
+  p.func = (path == PT_PATH_FWD) ? e.fwd : (path == PT_PATH_DX) ? e.dx : e.dk;
+  p.exact = true;
+  int rc = ensure_smem_attr(di, p.func, p.smem);
+  if (rc != PT_OK) return rc;
+  int occ = 0;
+  cudaError_t ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, p.func, p.threads, p.smem);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  if (occ < 1) return PT_ERR_UNSUPPORTED;
+  const int cps = cfg.ctas_per_sm < occ ? cfg.ctas_per_sm : occ;
+  long long G = static_cast<long long>(di.sm_count) * cps;
+  const long long tiles = static_cast<long long>(g.Q) * g.nhb;
+  if (G > tiles) G = tiles;
+  G = G / g.nhb * g.nhb;
+  if (G < g.nhb) G = g.nhb;
+  g.G = static_cast<int>(G);
+  return PT_OK;
+}
+
+void plan_generic_dk(int B, int H, int L, int K, const DeviceInfo& di, Plan& p) {
+  pt::TileGeom& g = p.g;
+  g.B = B;
+  g.H = H;
+  g.L = L;
+  g.K = K;
+  g.Th = H;
+  g.Tb = 1;
+  g.nhb = 1;
+  int G = di.sm_count * 4;
+  if (G > B) G = B;
+  if (G < 1) G = 1;
+  g.G = G;
+  p.exact = false;
+}
+
+int plan(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
+  const pt::Entry* e = find_entry(L, K);
+  const bool tma_ok = g_encode != nullptr;
+  if (e && ((e->loader == pt::LOAD_TMA3D && tma_ok) ||
+            (e->loader == pt::LOAD_BULK1D && (static_cast<long long>(H) * L) % 4 == 0)))
+    return plan_exact(path, B, H, L, K, di, *e, p);
+  if (path == PT_PATH_DK) plan_generic_dk(B, H, L, K, di, p);
+  p.exact = false;
+  return PT_OK;
+}
+
+// 3-D tensor map over a [B,H,L] float tensor with box (pitch, Th, Tb).
+int encode_rows_tmap(CUtensorMap* tm, const float* base, const pt::TileGeom& g) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(g.L), static_cast<cuuint64_t>(g.H),
+                        static_cast<cuuint64_t>(g.B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(g.L) * 4,
+                           static_cast<cuuint64_t>(g.L) * g.H * 4};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(g.pitch), static_cast<cuuint32_t>(g.Th),
+                       static_cast<cuuint32_t>(g.Tb)};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                        strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = static_cast<int>(r);
+    return PT_ERR_CUDA;
+  }
+  return PT_OK;
+}
+
+int check_common(const void* a, const void* b, const void* c, int B, int H, int L, int K) {
+  if (!a || !b || !c) return PT_ERR_ARGS;
+  if (B < 0 || H < 1 || L < 1 || K < 1) return PT_ERR_ARGS;
+  if (L > PT_MAX_L || K > PT_MAX_K) return PT_ERR_UNSUPPORTED;
+  if (static_cast<long long>(B) * H > (1ll << 31)) return PT_ERR_ARGS;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c)) return PT_ERR_ALIGN;
+  return PT_OK;
+}
+
+int launch_rows(int path, const float* in, const float* taps, float* out, int B, int H, int L, int K,
+                cudaStream_t stream) {
+  int rc = check_common(in, taps, out, B, H, L, K);
+  if (rc != PT_OK) return rc;
+  if (B == 0) return PT_OK;
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device(di)) != PT_OK) return rc;
+  Plan p;
+  if ((rc = plan(path, B, H, L, K, *di, p)) != PT_OK) return rc;
+  cudaError_t ce;
+  if (p.exact) {
+    CUtensorMap tm_in, tm_out;
+    std::memset(&tm_in, 0, sizeof(tm_in));
+    std::memset(&tm_out, 0, sizeof(tm_out));
+    if (p.loader == pt::LOAD_TMA3D) {
+      if ((rc = encode_rows_tmap(&tm_in, in, p.g)) != PT_OK) return rc;
+      if ((rc = encode_rows_tmap(&tm_out, out, p.g)) != PT_OK) return rc;
+    }
+    unsigned* err = di->err;
+    pt::TileGeom g = p.g;
+    void* args[] = {&tm_in, &tm_out, const_cast<float**>(&in), const_cast<float**>(&taps), &out, &g, &err};
+    ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
+  } else {
+    const long long S = static_cast<long long>(B) * H;
+    const long long n_tiles = (S + kGenericRows - 1) / kGenericRows;
+    long long grid = static_cast<long long>(di->sm_count) * 8;
+    if (grid > n_tiles) grid = n_tiles;
+    if (path == PT_PATH_FWD)
+      pt::conv_generic_kernel<pt::OP_FWD><<<static_cast<unsigned>(grid), kGenericRows, 0, stream>>>(
+          in, taps, out, B, H, L, K, n_tiles);
+    else
+      pt::conv_generic_kernel<pt::OP_DX><<<static_cast<unsigned>(grid), kGenericRows, 0, stream>>>(
+          in, taps, out, B, H, L, K, n_tiles);
+    ce = cudaGetLastError();
+  }
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  return PT_OK;
+}
+
+size_t dk_ws_bytes(const Plan& p) {
+  return static_cast<size_t>(p.g.G) * p.g.K * p.g.Th * sizeof(float);
+}
+
+}  // namespace
+
+extern "C" {
+
+int pt_fwd(const float* x, const float* k, float* y, int B, int H, int L, int K, void* stream) {
+  return launch_rows(PT_PATH_FWD, x, k, y, B, H, L, K, static_cast<cudaStream_t>(stream));
+}
+
+int pt_dx(const float* dy, const float* k, float* dx, int B, int H, int L, int K, void* stream) {
+  return launch_rows(PT_PATH_DX, dy, k, dx, B, H, L, K, static_cast<cudaStream_t>(stream));
+}
+
+size_t pt_dk_workspace_bytes(int B, int H, int L, int K) {
+  if (B < 1 || H < 1 || L < 1 || K < 1 || L > PT_MAX_L || K > PT_MAX_K) return 0;
+  DeviceInfo* di = nullptr;
+  if (current_device(di) != PT_OK) return 0;
+  Plan p;
+  if (plan(PT_PATH_DK, B, H, L, K, *di, p) != PT_OK) return 0;
+  return dk_ws_bytes(p);
+}
+
+int pt_dk(const float* dy, const float* x, float* dk, int B, int H, int L, int K, int mode, void* ws,
+          size_t ws_bytes, void* stream_v) {
+  int rc = check_common(dy, x, dk, B, H, L, K);
+  if (rc != PT_OK) return rc;
+  if (mode != PT_DK_ATOMIC && mode != PT_DK_DETERMINISTIC && mode != PT_DK_DETERMINISTIC_ACCUMULATE)
+    return PT_ERR_ARGS;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  cudaError_t ce;
+  if (B == 0) {
+    if (mode == PT_DK_DETERMINISTIC) {
+      ce = cudaMemsetAsync(dk, 0, static_cast<size_t>(H) * K * sizeof(float), stream);
+      if (ce != cudaSuccess) return cuda_fail(ce);
+    }
+    return PT_OK;
+  }
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device(di)) != PT_OK) return rc;
+  Plan p;
+  if ((rc = plan(PT_PATH_DK, B, H, L, K, *di, p)) != PT_OK) return rc;
+  const int atomic_mode = (mode == PT_DK_ATOMIC) ? 1 : 0;
+  float* dst = dk;
+  if (!atomic_mode) {
+    if (!ws || ws_bytes < dk_ws_bytes(p)) return PT_ERR_WORKSPACE;
+    if (!aligned16(ws)) return PT_ERR_ALIGN;
+    dst = static_cast<float*>(ws);
+  }
+  pt::TileGeom g = p.g;
+  if (p.exact) {
+    CUtensorMap tm_dy, tm_x;
+    std::memset(&tm_dy, 0, sizeof(tm_dy));
+    std::memset(&tm_x, 0, sizeof(tm_x));
+    if (p.loader == pt::LOAD_TMA3D) {
+      if ((rc = encode_rows_tmap(&tm_dy, dy, g)) != PT_OK) return rc;
+      if ((rc = encode_rows_tmap(&tm_x, x, g)) != PT_OK) return rc;
+    }
+    unsigned* err = di->err;
+    void* args[] = {&tm_dy, &tm_x, const_cast<float**>(&dy), const_cast<float**>(&x), &dst, &g,
+                    const_cast<int*>(&atomic_mode), &err};
+    ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
+  } else {
+    pt::dk_generic_kernel<<<g.G, 128, 0, stream>>>(dy, x, dst, B, H, L, K, g.G, atomic_mode);
+    ce = cudaGetLastError();
+  }
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  if (!atomic_mode) {
+    const dim3 grid2((H + 31) / 32, K);
+    pt::dk_reduce_kernel<<<grid2, 256, 0, stream>>>(dst, dk, g,
+                                                    mode == PT_DK_DETERMINISTIC_ACCUMULATE ? 1 : 0);
+    ce = cudaGetLastError();
+    if (ce != cudaSuccess) return cuda_fail(ce);
+  }
+  return PT_OK;
+}
+
+int pt_config(int path, int B, int H, int L, int K, int* out, int n) {
+  if (path < 0 || path > 2 || !out || n < 4) return PT_ERR_ARGS;
+  if (B < 1 || H < 1 || L < 1 || K < 1) return PT_ERR_ARGS;
+  if (L > PT_MAX_L || K > PT_MAX_K) return PT_ERR_UNSUPPORTED;
+  std::call_once(g_once, init_once);
+  const pt::LaunchCfg c = cfg_for(path);
+  const pt::Entry* e = find_entry(L, K);
+  out[0] = c.rows;
+  out[1] = c.stages;
+  out[2] = c.ctas_per_sm;
+  out[3] = (e && (e->loader == pt::LOAD_TMA3D || (static_cast<long long>(H) * L) % 4 == 0)) ? 1 : 0;
+  return PT_OK;
+}
+
+int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n) {
+  if (path < 0 || path > 2 || !out || n < 8) return PT_ERR_ARGS;
+  if (B < 1 || H < 1 || L < 1 || K < 1) return PT_ERR_ARGS;
+  if (L > PT_MAX_L || K > PT_MAX_K) return PT_ERR_UNSUPPORTED;
+  DeviceInfo* di = nullptr;
+  int rc = current_device(di);
+  if (rc != PT_OK) return rc;
+  Plan p;
+  if ((rc = plan(path, B, H, L, K, *di, p)) != PT_OK) return rc;
+  const void* func = p.func;
+  int threads = p.threads;
+  size_t dyn = p.smem;
+  int grid = p.g.G;
+  if (!p.exact) {
+    threads = (path == PT_PATH_DK) ? 128 : kGenericRows;
+    dyn = 0;
+    if (path == PT_PATH_FWD)
+      func = reinterpret_cast<const void*>(&pt::conv_generic_kernel<pt::OP_FWD>);
+    else if (path == PT_PATH_DX)
+      func = reinterpret_cast<const void*>(&pt::conv_generic_kernel<pt::OP_DX>);
+    else
+      func = reinterpret_cast<const void*>(&pt::dk_generic_kernel);
+    if (path != PT_PATH_DK) {
+      const long long S = static_cast<long long>(B) * H;
+      const long long n_tiles = (S + kGenericRows - 1) / kGenericRows;
+      long long gsz = static_cast<long long>(di->sm_count) * 8;
+      grid = static_cast<int>(gsz < n_tiles ? gsz : n_tiles);
+    }
+  }
+  cudaFuncAttributes fa;
+  cudaError_t ce = cudaFuncGetAttributes(&fa, func);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  int occ = 0;
+  ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, func, threads, dyn);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  out[0] = fa.numRegs;
+  out[1] = static_cast<int>(fa.sharedSizeBytes);
+  out[2] = static_cast<int>(fa.localSizeBytes);
+  out[3] = threads;
+  out[4] = static_cast<int>(dyn);
+  out[5] = occ;
+  out[6] = grid;
+  out[7] = p.exact ? 1 : 0;
+  return PT_OK;
+}
+
+int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm) {
+  if (path < 0 || path > 2) return PT_ERR_ARGS;
+  if (rows_per_tile == 0) {
+    g_has_override[path] = false;
+    return PT_OK;
+  }
+  if (rows_per_tile < 32 || rows_per_tile > 256 || rows_per_tile % 32 != 0) return PT_ERR_ARGS;
+  if (stages < 2 || stages > 4 || ctas_per_sm < 1 || ctas_per_sm > 4) return PT_ERR_ARGS;
+  g_override[path] = pt::LaunchCfg{rows_per_tile, stages, ctas_per_sm};
+  g_has_override[path] = true;
+  return PT_OK;
+}
+
+int pt_device_error(unsigned int* out, int clear) {
+  if (!out) return PT_ERR_ARGS;
+  DeviceInfo* di = nullptr;
+  int rc = current_device(di);
+  if (rc != PT_OK) return rc;
+  cudaError_t ce = cudaDeviceSynchronize();
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  ce = cudaMemcpyFromSymbol(out, g_pt_device_error, sizeof(unsigned));
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  if (clear) {
+    const unsigned zero = 0;
+    ce = cudaMemcpyToSymbol(g_pt_device_error, &zero, sizeof(unsigned));
+    if (ce != cudaSuccess) return cuda_fail(ce);
+  }
+  return PT_OK;
+}
+
+const char* pt_status_string(int status) {
+  switch (status) {
+    case PT_OK: return "ok";
+    case PT_ERR_ARGS: return "invalid arguments (null pointer, non-positive or mismatched dimensions)";
+    case PT_ERR_UNSUPPORTED: return "unsupported shape: kernels require L <= 48 and K <= 48";
+    case PT_ERR_ALIGN: return "pointer not 16-byte aligned";
+    case PT_ERR_WORKSPACE: return "deterministic dK workspace missing or smaller than pt_dk_workspace_bytes()";
+    case PT_ERR_CUDA: return "CUDA call or kernel launch failed (see pt_last_cuda_error)";
+    case PT_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    default: return "unknown status";
+  }
+}
+
+int pt_last_cuda_error(void) { return t_last_cuda_error; }
+
+int pt_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,618 @@
+// pt_kernels.cuh -- sm_100a kernels of the short depthwise Conv1D training path.
+//
+// Math (same-length cross-correlation, left pad K/2, right pad K-1-K/2), the
+// contract of the reference path (benchmark/benchmark_shape_sweep_ampere.py:
+// 220-239 and kernels/warp_tiled_ampere.py:372-619):
+//   FWD  y [b,h,t] = sum_j x [b,h,t+j-K/2]   k[h,j]
+//   DX   dx[b,h,t] = sum_j dy[b,h,t-j+K/2]   k[h,j]   (= FWD with reversed taps
+//                                                     and left pad K-1-K/2)
+//   DK   dk[h,j]   = sum_{b,t} dy[b,h,t] x[b,h,t+j-K/2]
+//
+// Work decomposition (B200 design, not the reference's): a tile is Tb batches x
+// Th channels of whole rows (a row = one (b,h) sequence of L floats).  If H fits
+// in the tile (Th = H, "case A") a tile is Tb*H contiguous rows; otherwise the
+// channels are split into nhb blocks of Th (Tb = 1, "case B").  A persistent CTA
+// keeps one channel block for its whole life, so thread i always owns channel
+// hb*Th + i%Th: FWD/DX hold that channel's K taps in registers for the whole
+// kernel and DK keeps K per-thread accumulators across all its tiles.
+//
+// Tiles stream through a ring of `stages` shared-memory buffers filled by TMA:
+// a 3-D tensor map (dims L,H,B) when L%4 == 0, whose box is `pitch` floats wide
+// so that rows land at a bank-conflict-free pitch for 128-bit LDS, or one 1-D
+// bulk copy of the tile's contiguous bytes otherwise.  One thread per row loads
+// its row into registers, runs the fully unrolled (L,K) in-range FFMA nest, and
+// (FWD/DX) writes the output row back in place; the tile then leaves by a TMA
+// store.  Every mbarrier wait is bounded by a %globaltimer limit; on expiry the
+// kernel sets a bit in the caller's device error word and returns once its own
+// bulk copies have drained.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pt {
+
+enum Op { OP_FWD = 0, OP_DX = 1, OP_DK = 2 };
+enum Loader { LOAD_TMA3D = 0, LOAD_BULK1D = 1 };
+
+// Device error bits (written with atomicOr into the error word).
+constexpr unsigned DEVERR_TIMEOUT_FULL = 1u;   // a tile never arrived
+constexpr unsigned DEVERR_TIMEOUT_DRAIN = 2u;  // an in-flight copy did not drain
+// Wait limit: far above any legitimate tile latency (microseconds).
+constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
+
+struct TileGeom {
+  int B, H, L, K;
+  int Th, Tb;       // tile = Tb batches x Th channels
+  int nhb;          // channel blocks: ceil(H / Th)
+  int Q;            // tile positions along the batch: ceil(B / Tb)
+  int G;            // persistent CTAs (multiple of nhb)
+  int stages;       // ring depth
+  int pitch;        // shared-memory row pitch in floats
+  unsigned stage_bytes;  // bytes of one stage buffer (one input)
+  unsigned tx_bytes;     // TMA transaction bytes of one input per full tile
+};
+
+// ---------------------------------------------------------------------------
+// PTX helpers (mbarrier, TMA, bulk copies, proxy fences).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for phase `parity` of `bar`; false (and an error bit) on expiry.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned* err,
+                                                  unsigned errbit) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+      atomicOr(err, errbit);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tm, int c0, int c1,
+                                            int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, uint32_t src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tm)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_load_1d(uint32_t dst, const void* src, uint32_t bytes,
+                                             uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_store_1d(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Row <-> register movement.  TMA3D rows sit at a pitch that is a multiple of
+// 4 floats (128-bit accesses); BULK1D rows are dense at pitch L (64-bit
+// accesses when L is even, 32-bit otherwise).
+// ---------------------------------------------------------------------------
+template <int L, int LOADER>
+__device__ __forceinline__ void row_load(const float* __restrict__ p, float (&v)[L]) {
+  if constexpr (LOADER == LOAD_TMA3D) {
+    static_assert(L % 4 == 0, "TMA3D rows need L % 4 == 0");
+#pragma unroll
+    for (int c = 0; c < L / 4; ++c) {
+      const float4 q = reinterpret_cast<const float4*>(p)[c];
+      v[4 * c + 0] = q.x;
+      v[4 * c + 1] = q.y;
+      v[4 * c + 2] = q.z;
+      v[4 * c + 3] = q.w;
+    }
+  } else if constexpr (L % 2 == 0) {
+#pragma unroll
+    for (int c = 0; c < L / 2; ++c) {
+      const float2 q = reinterpret_cast<const float2*>(p)[c];
+      v[2 * c + 0] = q.x;
+      v[2 * c + 1] = q.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < L; ++i) v[i] = p[i];
+  }
+}
+
+template <int L, int LOADER>
+__device__ __forceinline__ void row_store(float* __restrict__ p, const float (&v)[L]) {
+  if constexpr (LOADER == LOAD_TMA3D) {
+#pragma unroll
+    for (int c = 0; c < L / 4; ++c)
+      reinterpret_cast<float4*>(p)[c] =
+          make_float4(v[4 * c + 0], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  } else if constexpr (L % 2 == 0) {
+#pragma unroll
+    for (int c = 0; c < L / 2; ++c)
+      reinterpret_cast<float2*>(p)[c] = make_float2(v[2 * c + 0], v[2 * c + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < L; ++i) p[i] = v[i];
+  }
+}
+
+// One output row: y[t] = sum_j in[t + j - PAD] * taps[j], in-range pairs only
+// (the out-of-range pairs are dropped at compile time: no predicates).
+template <int L, int K, int PAD>
+__device__ __forceinline__ void conv_row(const float (&in)[L], const float (&taps)[K],
+                                         float (&y)[L]) {
+#pragma unroll
+  for (int t = 0; t < L; ++t) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const int i = t + j - PAD;
+      if (i >= 0 && i < L) acc = fmaf(in[i], taps[j], acc);
+    }
+    y[t] = acc;
+  }
+}
+
+// One row's contribution to the filter gradient: acc[j] += sum_t dy[t] x[t+j-PAD].
+template <int L, int K, int PAD>
+__device__ __forceinline__ void xcorr_row(const float (&dy)[L], const float (&x)[L],
+                                          float (&acc)[K]) {
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      const int i = t + j - PAD;
+      if (i >= 0 && i < L) acc[j] = fmaf(dy[t], x[i], acc[j]);
+    }
+  }
+}
+
+// Tile bookkeeping shared by the FWD/DX and DK kernels.
+struct TileCursor {
+  int hb, q0, qs, n_it;
+  __device__ __forceinline__ TileCursor(const TileGeom& g) {
+    hb = static_cast<int>(blockIdx.x) % g.nhb;
+    q0 = static_cast<int>(blockIdx.x) / g.nhb;
+    qs = g.G / g.nhb;
+    n_it = (q0 < g.Q) ? (g.Q - q0 + qs - 1) / qs : 0;
+  }
+  __device__ __forceinline__ int q(int it) const { return q0 + it * qs; }
+};
+
+// First row (flattened b*H + h) and row count of tile q in channel block hb.
+__device__ __forceinline__ void tile_rows(const TileGeom& g, int hb, int q, long long& row0,
+                                          int& nrows) {
+  if (g.nhb == 1) {
+    const int b0 = q * g.Tb;
+    const int nb = min(g.Tb, g.B - b0);
+    row0 = static_cast<long long>(b0) * g.H;
+    nrows = nb * g.H;
+  } else {
+    row0 = static_cast<long long>(q) * g.H + static_cast<long long>(hb) * g.Th;
+    nrows = min(g.Th, g.H - hb * g.Th);
+  }
+}
+
+template <int LOADER>
+__device__ __forceinline__ void issue_tile_load(const TileGeom& g, const CUtensorMap* tm,
+                                                const float* base, int hb, int q, uint32_t dst,
+                                                uint32_t bar) {
+  if constexpr (LOADER == LOAD_TMA3D) {
+    tma_load_3d(dst, tm, 0, hb * g.Th, q * g.Tb, bar);
+  } else {
+    long long row0;
+    int nrows;
+    tile_rows(g, hb, q, row0, nrows);
+    bulk_load_1d(dst, base + row0 * g.L, static_cast<uint32_t>(nrows) * g.L * 4u, bar);
+  }
+}
+
+template <int LOADER>
+__device__ __forceinline__ uint32_t tile_tx_bytes(const TileGeom& g, int hb, int q) {
+  if constexpr (LOADER == LOAD_TMA3D) {
+    return g.tx_bytes;  // a TMA box always lands whole (out-of-bounds part zero-filled)
+  } else {
+    long long row0;
+    int nrows;
+    tile_rows(g, hb, q, row0, nrows);
+    return static_cast<uint32_t>(nrows) * g.L * 4u;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// FWD / DX: persistent, TMA-pipelined, one row per thread, in-place output.
+// ---------------------------------------------------------------------------
+template <int L, int K, int OP, int LOADER>
+__global__ void __launch_bounds__(256, 1)
+    conv_rows_kernel(const __grid_constant__ CUtensorMap tm_in,
+                     const __grid_constant__ CUtensorMap tm_out, const float* __restrict__ in,
+                     const float* __restrict__ taps_hk, float* __restrict__ out, const TileGeom g,
+                     unsigned* __restrict__ err) {
+  static_assert(OP == OP_FWD || OP == OP_DX, "conv_rows_kernel computes FWD or DX");
+  constexpr int PAD = (OP == OP_FWD) ? (K / 2) : (K - 1 - K / 2);
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const int tid = static_cast<int>(threadIdx.x);
+  const TileCursor cur(g);
+  const int T = g.Th * g.Tb;
+  const int h_local = tid % g.Th;
+  const int b_local = tid / g.Th;
+  const int h = cur.hb * g.Th + h_local;
+  const bool thread_has_row = (tid < T) && (h < g.H);
+
+  // This thread's taps, once per kernel (reversed for DX).
+  float taps[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const int src = (OP == OP_FWD) ? j : (K - 1 - j);
+    taps[j] = thread_has_row ? __ldg(taps_hk + static_cast<long long>(h) * K + src) : 0.0f;
+  }
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(g.stages) * g.stage_bytes);
+  if (tid == 0) {
+    if constexpr (LOADER == LOAD_TMA3D) {
+      prefetch_tmap(&tm_in);
+      prefetch_tmap(&tm_out);
+    }
+    for (int s = 0; s < g.stages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto stage_ptr = [&](int s) -> float* {
+    return reinterpret_cast<float*>(smem + static_cast<size_t>(s) * g.stage_bytes);
+  };
+  auto load = [&](int it) {
+    const int s = it % g.stages;
+    const int q = cur.q(it);
+    const uint32_t bar = smem_u32(&bars[s]);
+    mbar_arrive_expect_tx(bar, tile_tx_bytes<LOADER>(g, cur.hb, q));
+    issue_tile_load<LOADER>(g, &tm_in, in, cur.hb, q, smem_u32(stage_ptr(s)), bar);
+  };
+
+  if (tid == 0) {
+    const int pro = min(g.stages - 1, cur.n_it);
+    for (int it = 0; it < pro; ++it) load(it);
+  }
+
+  int it = 0;
+  for (; it < cur.n_it; ++it) {
+    const int s = it % g.stages;
+    const uint32_t parity = static_cast<uint32_t>(it / g.stages) & 1u;
+    const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_FULL);
+    const int q = cur.q(it);
+    const bool row_valid = thread_has_row && (q * g.Tb + b_local < g.B);
+    float* rowp = stage_ptr(s) + static_cast<size_t>(tid) * g.pitch;
+    if (ok && row_valid) {
+      float xin[L];
+      float yout[L];
+      row_load<L, LOADER>(rowp, xin);
+      conv_row<L, K, PAD>(xin, taps, yout);
+      row_store<L, LOADER>(rowp, yout);
+    }
+    fence_proxy_async_smem();
+    if (__syncthreads_or(!ok)) break;
+    if (tid == 0) {
+      if constexpr (LOADER == LOAD_TMA3D) {
+        tma_store_3d(&tm_out, smem_u32(stage_ptr(s)), 0, cur.hb * g.Th, q * g.Tb);
+      } else {
+        long long row0;
+        int nrows;
+        tile_rows(g, cur.hb, q, row0, nrows);
+        bulk_store_1d(out + row0 * g.L, smem_u32(stage_ptr(s)),
+                      static_cast<uint32_t>(nrows) * g.L * 4u);
+      }
+      bulk_commit();
+      // Refill the stage of tile it-1 with tile it-1+stages once its store has
+      // finished reading shared memory (tile it's store may still be reading).
+      bulk_wait_read<1>();
+      const int nxt = it + g.stages - 1;
+      if (nxt < cur.n_it) load(nxt);
+    }
+  }
+
+  if (tid == 0) {
+    bulk_wait_all();
+    if (it < cur.n_it) {
+      // Aborted: let every load this CTA issued land before shared memory goes away.
+      const int issued_end = min(cur.n_it, it + g.stages - 1);
+      for (int k2 = it + 1; k2 < issued_end; ++k2) {
+        const int s = k2 % g.stages;
+        const uint32_t parity = static_cast<uint32_t>(k2 / g.stages) & 1u;
+        if (!mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_DRAIN)) break;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// DK pass 1: persistent, TMA-pipelined; per-thread accumulators over all tiles,
+// then an in-CTA reduction over the Tb batch slots of each channel (fixed
+// order) and either one float atomic per (CTA,h,j) or one partial per (CTA,j,h).
+// ---------------------------------------------------------------------------
+template <int L, int K, int LOADER>
+__global__ void __launch_bounds__(256, 1)
+    dk_rows_kernel(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_x,
+                   const float* __restrict__ dy, const float* __restrict__ x,
+                   float* __restrict__ dst, const TileGeom g, const int atomic_mode,
+                   unsigned* __restrict__ err) {
+  constexpr int PAD = K / 2;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const int tid = static_cast<int>(threadIdx.x);
+  const TileCursor cur(g);
+  const int T = g.Th * g.Tb;
+  const int h_local = tid % g.Th;
+  const int b_local = tid / g.Th;
+  const int h = cur.hb * g.Th + h_local;
+  const bool thread_has_row = (tid < T) && (h < g.H);
+
+  // Stage s: dy buffer at 2*s, x buffer at 2*s+1.
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(2 * g.stages) * g.stage_bytes);
+  if (tid == 0) {
+    if constexpr (LOADER == LOAD_TMA3D) {
+      prefetch_tmap(&tm_dy);
+      prefetch_tmap(&tm_x);
+    }
+    for (int s = 0; s < g.stages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto buf = [&](int s, int which) -> float* {
+    return reinterpret_cast<float*>(smem + static_cast<size_t>(2 * s + which) * g.stage_bytes);
+  };
+  auto load = [&](int it) {
+    const int s = it % g.stages;
+    const int q = cur.q(it);
+    const uint32_t bar = smem_u32(&bars[s]);
+    mbar_arrive_expect_tx(bar, 2u * tile_tx_bytes<LOADER>(g, cur.hb, q));
+    issue_tile_load<LOADER>(g, &tm_dy, dy, cur.hb, q, smem_u32(buf(s, 0)), bar);
+    issue_tile_load<LOADER>(g, &tm_x, x, cur.hb, q, smem_u32(buf(s, 1)), bar);
+  };
+
+  if (tid == 0) {
+    const int pro = min(g.stages, cur.n_it);
+    for (int it = 0; it < pro; ++it) load(it);
+  }
+
+  float acc[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) acc[j] = 0.0f;
+
+  int it = 0;
+  for (; it < cur.n_it; ++it) {
+    const int s = it % g.stages;
+    const uint32_t parity = static_cast<uint32_t>(it / g.stages) & 1u;
+    const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_FULL);
+    const int q = cur.q(it);
+    const bool row_valid = thread_has_row && (q * g.Tb + b_local < g.B);
+    if (ok && row_valid) {
+      float gyr[L];
+      float xr[L];
+      row_load<L, LOADER>(buf(s, 0) + static_cast<size_t>(tid) * g.pitch, gyr);
+      row_load<L, LOADER>(buf(s, 1) + static_cast<size_t>(tid) * g.pitch, xr);
+      xcorr_row<L, K, PAD>(gyr, xr, acc);
+    }
+    if (__syncthreads_or(!ok)) break;
+    if (tid == 0) {
+      const int nxt = it + g.stages;
+      if (nxt < cur.n_it) load(nxt);
+    }
+  }
+
+  if (it < cur.n_it) {
+    if (tid == 0) {
+      const int issued_end = min(cur.n_it, it + g.stages);
+      for (int k2 = it + 1; k2 < issued_end; ++k2) {
+        const int s = k2 % g.stages;
+        const uint32_t parity = static_cast<uint32_t>(k2 / g.stages) & 1u;
+        if (!mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_DRAIN)) break;
+      }
+    }
+    return;
+  }
+
+  // In-CTA reduction over batch slots (the stage ring is idle now).
+  float* red = reinterpret_cast<float*>(smem);  // [K][T]
+  __syncthreads();
+  if (tid < T) {
+#pragma unroll
+    for (int j = 0; j < K; ++j) red[j * T + tid] = acc[j];
+  }
+  __syncthreads();
+  const int nh = min(g.Th, g.H - cur.hb * g.Th);
+  for (int idx = tid; idx < K * nh; idx += static_cast<int>(blockDim.x)) {
+    const int j = idx / nh;
+    const int hl = idx - j * nh;
+    float sum = 0.0f;
+    for (int bl = 0; bl < g.Tb; ++bl) sum += red[j * T + bl * g.Th + hl];
+    if (atomic_mode) {
+      atomicAdd(dst + static_cast<long long>(cur.hb * g.Th + hl) * g.K + j, sum);
+    } else {
+      dst[(static_cast<long long>(blockIdx.x) * g.K + j) * g.Th + hl] = sum;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Generic kernels: any L <= 48, K <= 48, any alignment of H*L.  Tiles of
+// `rows` contiguous rows are staged in shared memory by coalesced loads; the
+// tap loops run on runtime bounds.  They carry every shape the specialised
+// table does not, at lower FFMA density.
+// ---------------------------------------------------------------------------
+template <int OP>
+__global__ void __launch_bounds__(128)
+    conv_generic_kernel(const float* __restrict__ in, const float* __restrict__ taps_hk,
+                        float* __restrict__ out, int B, int H, int L, int K, long long n_tiles) {
+  static_assert(OP == OP_FWD || OP == OP_DX, "FWD or DX");
+  constexpr int ROWS = 128;
+  __shared__ float s_in[ROWS * 48];
+  __shared__ float s_out[ROWS * 48];
+  const int tid = static_cast<int>(threadIdx.x);
+  const long long S = static_cast<long long>(B) * H;
+  const int pad = (OP == OP_FWD) ? (K / 2) : (K - 1 - K / 2);
+  for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const long long r0 = tile * ROWS;
+    const int nrows = static_cast<int>(min(static_cast<long long>(ROWS), S - r0));
+    const int nelem = nrows * L;
+    const float* src = in + r0 * L;
+    for (int e = tid; e < nelem; e += ROWS) s_in[e] = src[e];
+    __syncthreads();
+    if (tid < nrows) {
+      const int hh = static_cast<int>((r0 + tid) % H);
+      const float* kp = taps_hk + static_cast<long long>(hh) * K;
+      const float* xr = s_in + tid * L;
+      for (int t = 0; t < L; ++t) {
+        float acc = 0.0f;
+        for (int j = 0; j < K; ++j) {
+          const int i = t + j - pad;
+          const float kv = (OP == OP_FWD) ? __ldg(kp + j) : __ldg(kp + (K - 1 - j));
+          if (i >= 0 && i < L) acc = fmaf(xr[i], kv, acc);
+        }
+        s_out[tid * L + t] = acc;
+      }
+    }
+    __syncthreads();
+    float* dstp = out + r0 * L;
+    for (int e = tid; e < nelem; e += ROWS) dstp[e] = s_out[e];
+    __syncthreads();
+  }
+}
+
+#ifdef PT_KERNELS_IMPL
+// Non-template kernels are emitted by exactly one unit (pt_api.cu).
+
+// ---------------------------------------------------------------------------
+// DK pass 2 (deterministic): dk[h,j] (+)= sum over the CTAs of h's channel
+// block, in ascending CTA order split over 8 warps, then warp-ordered combine.
+// partial layout [G][K][Th].  Grid (ceil(H/32), K), block 256.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) dk_reduce_kernel(const float* __restrict__ partial,
+                                                        float* __restrict__ dk, const TileGeom g,
+                                                        const int accumulate) {
+  __shared__ float sums[8][33];
+  const int lane = static_cast<int>(threadIdx.x) & 31;
+  const int w = static_cast<int>(threadIdx.x) >> 5;
+  const int h = static_cast<int>(blockIdx.x) * 32 + lane;
+  const int j = static_cast<int>(blockIdx.y);
+  float s = 0.0f;
+  if (h < g.H) {
+    const int hb = h / g.Th;
+    const int hl = h - hb * g.Th;
+    const int step = g.nhb * 8;
+    for (int c = hb + g.nhb * w; c < g.G; c += step)
+      s += __ldg(partial + (static_cast<long long>(c) * g.K + j) * g.Th + hl);
+  }
+  sums[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && h < g.H) {
+    float total = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) total += sums[k][lane];
+    float* o = dk + static_cast<long long>(h) * g.K + j;
+    *o = accumulate ? (*o + total) : total;
+  }
+}
+
+// Generic DK pass 1: CTA c owns the batches b = c, c+G, ... of every channel.
+// Block 128 threads; thread (hh, jj) pairs over a [H x K] grid in strides.
+// Writes partial[c][j][h] (layout [G][K][H], i.e. Th = H, nhb = 1).
+__global__ void __launch_bounds__(128)
+    dk_generic_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                      float* __restrict__ dst, int B, int H, int L, int K, int G, int atomic_mode) {
+  const int tid = static_cast<int>(threadIdx.x);
+  const int c = static_cast<int>(blockIdx.x);
+  const int pad = K / 2;
+  for (int p = tid; p < H * K; p += 128) {
+    const int hh = p / K;
+    const int j = p - hh * K;
+    float acc = 0.0f;
+    for (int b = c; b < B; b += G) {
+      const float* g1 = dy + (static_cast<long long>(b) * H + hh) * L;
+      const float* x1 = x + (static_cast<long long>(b) * H + hh) * L;
+      for (int t = 0; t < L; ++t) {
+        const int i = t + j - pad;
+        if (i >= 0 && i < L) acc = fmaf(__ldg(g1 + t), __ldg(x1 + i), acc);
+      }
+    }
+    if (atomic_mode)
+      atomicAdd(dst + static_cast<long long>(hh) * K + j, acc);
+    else
+      dst[(static_cast<long long>(c) * K + j) * H + hh] = acc;
+  }
+}
+
+#endif  // PT_KERNELS_IMPL
+
+}  // namespace pt

@@ -1,0 +1,246 @@
+"""Tensor-level launches of the native FWD / dX / dK kernels.
+
+Each function validates its tensors the way the reference runtime does
+(``AmpereWarpRuntime._check_shapes``, kernels/warp_tiled_ampere.py:704-717:
+ValueError for device, dtype, rank, channel mismatch and L/K > 48), then calls
+the C ABI on the tensors' device and on ``torch.cuda.current_stream()`` of
+that device (the reference launched on PyCUDA's default stream,
+kernels/warp_tiled_ampere.py:734-744; here the caller's stream is honoured).
+No computation happens on the host and there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import (
+    PT_DK_ATOMIC,
+    PT_DK_DETERMINISTIC,
+    PT_DK_DETERMINISTIC_ACCUMULATE,
+    PT_MAX_K,
+    PT_MAX_L,
+    PT_PATH_DK,
+    PT_PATH_DX,
+    PT_PATH_FWD,
+)
+
+DK_MODES = {
+    "atomic": PT_DK_ATOMIC,
+    "deterministic": PT_DK_DETERMINISTIC,
+}
+
+
+def _ensure_cuda_f32(t: torch.Tensor, name: str) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != torch.float32:
+        raise ValueError(f"{name}: only FP32 is supported, got {t.dtype}")
+
+
+def _ensure_raw(t: torch.Tensor, name: str) -> None:
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if t.numel() and t.data_ptr() % 16:
+        raise ValueError(f"{name} must be 16-byte aligned")
+
+
+def check_shapes(x: torch.Tensor, k: torch.Tensor) -> tuple[int, int, int, int]:
+    """Validate x[B,H,L] and k[H,K]; return (B, H, L, K)."""
+    _ensure_cuda_f32(x, "x")
+    _ensure_cuda_f32(k, "k")
+    if x.ndim != 3 or k.ndim != 2:
+        raise ValueError("Expected x[B,H,L] and k[H,K]")
+    B, H, L = map(int, x.shape)
+    Hk, K = map(int, k.shape)
+    if H != Hk:
+        raise ValueError("x and k channel dimensions do not match")
+    if L > PT_MAX_L or K > PT_MAX_K:
+        raise ValueError(f"Specialized kernels require L<={PT_MAX_L}, K<={PT_MAX_K}")
+    if H < 1 or L < 1 or K < 1:
+        raise ValueError("H, L and K must be positive")
+    if x.device != k.device:
+        raise ValueError("x and k must be on the same device")
+    return B, H, L, K
+
+
+def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _launch_rows(path: int, inp: torch.Tensor, k: torch.Tensor, out: torch.Tensor, what: str) -> None:
+    B, H, L, K = check_shapes(inp, k)
+    _ensure_cuda_f32(out, "out")
+    if tuple(out.shape) != (B, H, L):
+        raise ValueError(f"out must have shape {(B, H, L)}")
+    if out.device != inp.device:
+        raise ValueError("out must be on the input's device")
+    for t, n in ((inp, "input"), (k, "k"), (out, "out")):
+        _ensure_raw(t, n)
+    if B == 0:
+        return
+    lib = _lib.load()
+    fn = lib.pt_fwd if path == PT_PATH_FWD else lib.pt_dx
+    with torch.cuda.device(inp.device):
+        st = fn(_ptr(inp), _ptr(k), _ptr(out), B, H, L, K, _stream(inp.device))
+    _lib.check(st, what)
+
+
+def fwd(x: torch.Tensor, k: torch.Tensor, y: torch.Tensor | None = None) -> torch.Tensor:
+    """y[b,h,t] = sum_j x[b,h,t+j-K//2] k[h,j] (same length L)."""
+    if y is None:
+        check_shapes(x, k)
+        y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    _launch_rows(PT_PATH_FWD, x, k, y, "pt_fwd")
+    return y
+
+
+def dx(dy: torch.Tensor, k: torch.Tensor, gx: torch.Tensor | None = None) -> torch.Tensor:
+    """gx[b,h,t] = sum_j dy[b,h,t-j+K//2] k[h,j]."""
+    if gx is None:
+        check_shapes(dy, k)
+        gx = torch.empty_like(dy, memory_format=torch.contiguous_format)
+    _launch_rows(PT_PATH_DX, dy, k, gx, "pt_dx")
+    return gx
+
+
+class _WorkspaceCache:
+    """One reusable deterministic-dK workspace per device (the reference caches
+    its [H,K,num_btiles] partials the same way,
+    kernels/warp_tiled_noatomic_optimized.py:1448-1471).  The buffer is
+    recorded on the launch stream so the caching allocator never hands it out
+    while a launch still reads it."""
+
+    def __init__(self) -> None:
+        self._lock = threading.Lock()
+        self._bufs: dict[int, torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        with self._lock:
+            buf = self._bufs.get(idx)
+            if buf is None or buf.numel() < nbytes:
+                n = max(nbytes, 1 << 20)
+                buf = torch.empty(n, dtype=torch.uint8, device=torch.device("cuda", idx))
+                self._bufs[idx] = buf
+            return buf
+
+
+WORKSPACES = _WorkspaceCache()
+
+
+def dk_workspace_bytes(B: int, H: int, L: int, K: int, device: torch.device | None = None) -> int:
+    lib = _lib.load()
+    if device is None:
+        return int(lib.pt_dk_workspace_bytes(B, H, L, K))
+    with torch.cuda.device(device):
+        return int(lib.pt_dk_workspace_bytes(B, H, L, K))
+
+
+def dk(
+    dy: torch.Tensor,
+    x: torch.Tensor,
+    gk: torch.Tensor,
+    mode: str = "deterministic",
+    accumulate: bool = False,
+    workspace: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Filter gradient dk[h,j] = sum_{b,t} dy[b,h,t] x[b,h,t+j-K//2] into gk[H,K].
+
+    mode "atomic": gk += dK through float atomics (gk must be zeroed first for a
+    plain gradient; the reference's contract, kernels/warp_tiled_ampere.py:890-893).
+    mode "deterministic": two passes through a workspace; gk = dK, or gk += dK
+    with accumulate=True; bit-reproducible for a fixed launch configuration.
+    """
+    _ensure_cuda_f32(dy, "gy")
+    _ensure_cuda_f32(x, "x")
+    _ensure_cuda_f32(gk, "gk")
+    if tuple(dy.shape) != tuple(x.shape):
+        raise ValueError("gy and x must have the same [B,H,L] shape")
+    if x.ndim != 3 or gk.ndim != 2:
+        raise ValueError("Expected gy/x [B,H,L] and gk [H,K]")
+    B, H, L = map(int, x.shape)
+    K = int(gk.shape[1])
+    if tuple(gk.shape) != (H, K):
+        raise ValueError(f"gk must have shape {(H, K)}")
+    if L > PT_MAX_L or K > PT_MAX_K:
+        raise ValueError(f"Specialized kernels require L<={PT_MAX_L}, K<={PT_MAX_K}")
+    if H < 1 or L < 1 or K < 1:
+        raise ValueError("H, L and K must be positive")
+    if not (dy.device == x.device == gk.device):
+        raise ValueError("gy, x and gk must be on one device")
+    if mode not in DK_MODES:
+        raise ValueError(f"mode must be one of {sorted(DK_MODES)}")
+    for t, n in ((dy, "gy"), (x, "x"), (gk, "gk")):
+        _ensure_raw(t, n)
+    code = DK_MODES[mode]
+    if code == PT_DK_DETERMINISTIC and accumulate:
+        code = PT_DK_DETERMINISTIC_ACCUMULATE
+    lib = _lib.load()
+    dev = x.device
+    with torch.cuda.device(dev):
+        ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
+        if code != PT_DK_ATOMIC and B > 0:
+            ws_bytes = int(lib.pt_dk_workspace_bytes(B, H, L, K))
+            if ws_bytes == 0:
+                raise _lib.PathTileError(_lib.PT_ERR_WORKSPACE, "pt_dk_workspace_bytes")
+            ws = workspace if workspace is not None else WORKSPACES.get(dev, ws_bytes)
+            if ws.device != dev or ws.numel() * ws.element_size() < ws_bytes:
+                raise ValueError(f"workspace must be on {dev} and hold {ws_bytes} bytes")
+            ws.record_stream(torch.cuda.current_stream(dev))
+            ws_ptr = _ptr(ws)
+            ws_bytes = ws.numel() * ws.element_size()
+        st = lib.pt_dk(_ptr(dy), _ptr(x), _ptr(gk), B, H, L, K, code, ws_ptr, ws_bytes, _stream(dev))
+    _lib.check(st, "pt_dk")
+    return gk
+
+
+def config(path: str, B: int, H: int, L: int, K: int) -> dict[str, int]:
+    """Frozen launch choice of one path at one shape (C ABI pt_config)."""
+    code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
+    out = (ctypes.c_int * 4)()
+    _lib.check(_lib.load().pt_config(code, B, H, L, K, out, 4), "pt_config")
+    return {"rows_per_tile": out[0], "stages": out[1], "ctas_per_sm": out[2], "specialised": out[3]}
+
+
+def kernel_info(path: str, B: int, H: int, L: int, K: int, device: torch.device | int | None = None) -> dict[str, int]:
+    """Registers, shared memory, occupancy and grid of the kernel a path launches (C ABI pt_kernel_info)."""
+    code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
+    out = (ctypes.c_int * 8)()
+    lib = _lib.load()
+    if device is None:
+        st = lib.pt_kernel_info(code, B, H, L, K, out, 8)
+    else:
+        with torch.cuda.device(device):
+            st = lib.pt_kernel_info(code, B, H, L, K, out, 8)
+    _lib.check(st, "pt_kernel_info")
+    keys = ("regs_per_thread", "static_smem_bytes", "local_memory_bytes", "threads_per_block",
+            "dynamic_smem_bytes", "resident_blocks_per_sm", "grid", "specialised")
+    return dict(zip(keys, (int(v) for v in out)))
+
+
+def set_config(path: str, rows_per_tile: int = 0, stages: int = 3, ctas_per_sm: int = 2) -> None:
+    """Override one path's launch configuration (rows_per_tile=0 restores the frozen table)."""
+    code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
+    _lib.check(_lib.load().pt_set_config(code, rows_per_tile, stages, ctas_per_sm), "pt_set_config")
+
+
+def device_error(clear: bool = False, device: torch.device | int | None = None) -> int:
+    """Read (and optionally clear) the device error word; synchronises the device."""
+    out = ctypes.c_uint(0)
+    lib = _lib.load()
+    if device is None:
+        st = lib.pt_device_error(ctypes.byref(out), int(clear))
+    else:
+        with torch.cuda.device(device):
+            st = lib.pt_device_error(ctypes.byref(out), int(clear))
+    _lib.check(st, "pt_device_error")
+    return int(out.value)
