@@ -197,7 +197,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     dist = None
     if world > 1:
         import torch.distributed as dist
-    B = B_PER_GPU
+    B = args.batch
     g = torch.Generator(device=dev).manual_seed(42 + rank)
     x = torch.randn(B, H, L, device=dev, generator=g)
     k = torch.randn(H, K, device=dev, generator=torch.Generator(device=dev).manual_seed(42)) / (K ** 0.5)
@@ -241,6 +241,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         phase_ms = dict(zip(phase_ms, map(float, t.tolist())))
 
+    if args.no_e2e:
+        err = ops.device_error()
+        if rank == 0:
+            print(json.dumps({"profile_run": True, "B": B, "ms_per_step": step_ms, "phase_ms": phase_ms,
+                              "device_error_word": err}), flush=True)
+        return None
     # End to end through the host-buffer API: pinned host inputs in, host outputs back.
     pin = dict(device="cpu", pin_memory=True)
     x_h = torch.empty(B, H, L, **pin)
@@ -394,6 +400,9 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=3.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-sample-b", type=int, default=256)
+    ap.add_argument("--batch", type=int, default=B_PER_GPU,
+                    help="batch per GPU (default: the primary workload; smaller only for profiling)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -41,6 +41,9 @@ DeviceInfo g_dev[kMaxDevices];
 std::once_flag g_once;
 std::vector<pt::Entry>* g_entries = nullptr;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+// Rows are padded to a bank-conflict-free pitch by a TMA box wider than the
+// row; if the driver ever rejects such a box, rows fall back to pitch L.
+bool g_padded_box_ok = true;
 pt::LaunchCfg g_override[3];
 bool g_has_override[3] = {false, false, false};
 
@@ -136,7 +139,7 @@ struct Plan {
 
 // Row pitch (floats) for TMA3D tiles: 128-bit LDS by 8 consecutive rows hits
 // 8 distinct 16-byte bank groups iff pitch/4 is odd.
-int tma_pitch(int L) { return ((L / 4) % 2 == 1) ? L : L + 4; }
+int tma_pitch(int L) { return (!g_padded_box_ok || (L / 4) % 2 == 1) ? L : L + 4; }
 
 int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::Entry& e, Plan& p) {
   const pt::LaunchCfg cfg = cfg_for(path);
@@ -166,7 +169,7 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
   const int n_in = (path == PT_PATH_DK) ? 2 : 1;
   // Fewer stages when the ring would not fit the per-block shared memory.
   while (g.stages > 2 &&
-         static_cast<long long>(n_in) * g.stages * stage + g.stages * 8 > di.max_smem)
+         static_cast<long long>(n_in) * g.stages * stage + g.stages * 8 + 1024 > di.max_smem)
     --g.stages;
   if (path == PT_PATH_DK) {
     // The idle ring doubles as the [K][T] in-CTA reduction buffer at the end.
@@ -174,10 +177,11 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
     if (n_in * g.stages * stage < red)
       stage = ((red + n_in * g.stages - 1) / (n_in * g.stages) + 1023) / 1024 * 1024;
   }
-  if (static_cast<long long>(n_in) * g.stages * stage + g.stages * 8 > di.max_smem) return PT_ERR_UNSUPPORTED;
+  if (static_cast<long long>(n_in) * g.stages * stage + g.stages * 8 + 1024 > di.max_smem)
+    return PT_ERR_UNSUPPORTED;
   g.stage_bytes = static_cast<unsigned>(stage);
   g.tx_bytes = static_cast<unsigned>(tile_bytes);
-  p.smem = static_cast<size_t>(n_in) * g.stages * stage + static_cast<size_t>(g.stages) * 8;
+  p.smem = static_cast<size_t>(n_in) * g.stages * stage + static_cast<size_t>(g.stages) * 8 + 1024;
   p.threads = round_up(T, 32);
   p.func = (path == PT_PATH_FWD) ? e.fwd : (path == PT_PATH_DX) ? e.dx : e.dk;
   p.exact = true;
@@ -243,18 +247,34 @@ int encode_rows_tmap(CUtensorMap* tm, const float* base, const pt::TileGeom& g) 
   return PT_OK;
 }
 
-int check_common(const void* a, const void* b, const void* c, int B, int H, int L, int K) {
-  if (!a || !b || !c) return PT_ERR_ARGS;
+// Encode the two tensor maps of a TMA3D plan.  If the driver refuses the
+// padded-pitch box, switch every later plan to pitch L, re-plan and retry.
+int encode_pair(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p, CUtensorMap* a,
+                const float* pa, CUtensorMap* b, const float* pb) {
+  int rc = encode_rows_tmap(a, pa, p.g);
+  if (rc == PT_OK) rc = encode_rows_tmap(b, pb, p.g);
+  if (rc == PT_OK || p.g.pitch == L) return rc;
+  g_padded_box_ok = false;
+  if ((rc = plan(path, B, H, L, K, di, p)) != PT_OK) return rc;
+  rc = encode_rows_tmap(a, pa, p.g);
+  if (rc == PT_OK) rc = encode_rows_tmap(b, pb, p.g);
+  return rc;
+}
+
+// act1/act2 are [B,H,L] activations (may be null when B == 0, as an empty
+// tensor has no storage); hk is the [H,K] filter or filter gradient.
+int check_common(const void* act1, const void* act2, const void* hk, int B, int H, int L, int K) {
   if (B < 0 || H < 1 || L < 1 || K < 1) return PT_ERR_ARGS;
+  if (!hk || (B > 0 && (!act1 || !act2))) return PT_ERR_ARGS;
   if (L > PT_MAX_L || K > PT_MAX_K) return PT_ERR_UNSUPPORTED;
   if (static_cast<long long>(B) * H > (1ll << 31)) return PT_ERR_ARGS;
-  if (!aligned16(a) || !aligned16(b) || !aligned16(c)) return PT_ERR_ALIGN;
+  if (!aligned16(act1) || !aligned16(act2) || !aligned16(hk)) return PT_ERR_ALIGN;
   return PT_OK;
 }
 
 int launch_rows(int path, const float* in, const float* taps, float* out, int B, int H, int L, int K,
                 cudaStream_t stream) {
-  int rc = check_common(in, taps, out, B, H, L, K);
+  int rc = check_common(in, out, taps, B, H, L, K);
   if (rc != PT_OK) return rc;
   if (B == 0) return PT_OK;
   DeviceInfo* di = nullptr;
@@ -267,8 +287,7 @@ int launch_rows(int path, const float* in, const float* taps, float* out, int B,
     std::memset(&tm_in, 0, sizeof(tm_in));
     std::memset(&tm_out, 0, sizeof(tm_out));
     if (p.loader == pt::LOAD_TMA3D) {
-      if ((rc = encode_rows_tmap(&tm_in, in, p.g)) != PT_OK) return rc;
-      if ((rc = encode_rows_tmap(&tm_out, out, p.g)) != PT_OK) return rc;
+      if ((rc = encode_pair(path, B, H, L, K, *di, p, &tm_in, in, &tm_out, out)) != PT_OK) return rc;
     }
     unsigned* err = di->err;
     pt::TileGeom g = p.g;
@@ -348,8 +367,9 @@ int pt_dk(const float* dy, const float* x, float* dk, int B, int H, int L, int K
     std::memset(&tm_dy, 0, sizeof(tm_dy));
     std::memset(&tm_x, 0, sizeof(tm_x));
     if (p.loader == pt::LOAD_TMA3D) {
-      if ((rc = encode_rows_tmap(&tm_dy, dy, g)) != PT_OK) return rc;
-      if ((rc = encode_rows_tmap(&tm_x, x, g)) != PT_OK) return rc;
+      if ((rc = encode_pair(PT_PATH_DK, B, H, L, K, *di, p, &tm_dy, dy, &tm_x, x)) != PT_OK) return rc;
+      if (!atomic_mode && ws_bytes < dk_ws_bytes(p)) return PT_ERR_WORKSPACE;
+      g = p.g;
     }
     unsigned* err = di->err;
     void* args[] = {&tm_dy, &tm_x, const_cast<float**>(&dy), const_cast<float**>(&x), &dst, &g,

@@ -160,6 +160,13 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }
 
+// Dynamic shared memory rounded up to a 1024-byte boundary (the host adds
+// 1024 bytes of slack), so every stage buffer is a valid TMA destination.
+__device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
+  const uint32_t a = smem_u32(raw);
+  return raw + ((1024u - (a & 1023u)) & 1023u);
+}
+
 // ---------------------------------------------------------------------------
 // Row <-> register movement.  TMA3D rows sit at a pitch that is a multiple of
 // 4 floats (128-bit accesses); BULK1D rows are dense at pitch L (64-bit
@@ -225,13 +232,15 @@ __device__ __forceinline__ void conv_row(const float (&in)[L], const float (&tap
 }
 
 // One row's contribution to the filter gradient: acc[j] += sum_t dy[t] x[t+j-PAD].
+// t outer / j inner: consecutive FFMAs update different accumulators, so the
+// K per-tap chains interleave instead of stalling on FFMA latency.
 template <int L, int K, int PAD>
 __device__ __forceinline__ void xcorr_row(const float (&dy)[L], const float (&x)[L],
                                           float (&acc)[K]) {
 #pragma unroll
-  for (int j = 0; j < K; ++j) {
+  for (int t = 0; t < L; ++t) {
 #pragma unroll
-    for (int t = 0; t < L; ++t) {
+    for (int j = 0; j < K; ++j) {
       const int i = t + j - PAD;
       if (i >= 0 && i < L) acc[j] = fmaf(dy[t], x[i], acc[j]);
     }
@@ -301,7 +310,8 @@ __global__ void __launch_bounds__(256, 1)
                      unsigned* __restrict__ err) {
   static_assert(OP == OP_FWD || OP == OP_DX, "conv_rows_kernel computes FWD or DX");
   constexpr int PAD = (OP == OP_FWD) ? (K / 2) : (K - 1 - K / 2);
-  extern __shared__ __align__(1024) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
   const int tid = static_cast<int>(threadIdx.x);
   const TileCursor cur(g);
   const int T = g.Th * g.Tb;
@@ -407,7 +417,8 @@ __global__ void __launch_bounds__(256, 1)
                    float* __restrict__ dst, const TileGeom g, const int atomic_mode,
                    unsigned* __restrict__ err) {
   constexpr int PAD = K / 2;
-  extern __shared__ __align__(1024) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
   const int tid = static_cast<int>(threadIdx.x);
   const TileCursor cur(g);
   const int T = g.Th * g.Tb;
@@ -571,8 +582,20 @@ __global__ void __launch_bounds__(256) dk_reduce_kernel(const float* __restrict_
     const int hb = h / g.Th;
     const int hl = h - hb * g.Th;
     const int step = g.nhb * 8;
-    for (int c = hb + g.nhb * w; c < g.G; c += step)
-      s += __ldg(partial + (static_cast<long long>(c) * g.K + j) * g.Th + hl);
+    const long long cstride = static_cast<long long>(g.K) * g.Th;
+    const float* base = partial + static_cast<long long>(j) * g.Th + hl;
+    // Batches of 8 independent loads, then the adds in ascending CTA order:
+    // the same summation order as a plain loop, with 8 L2 requests in flight.
+    for (int c0 = hb + g.nhb * w; c0 < g.G; c0 += 8 * step) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * step;
+        v[u] = (c < g.G) ? __ldg(base + c * cstride) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s += v[u];
+    }
   }
   sums[w][lane] = s;
   __syncthreads();

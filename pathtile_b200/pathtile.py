@@ -1,0 +1,406 @@
+"""PathTile offline launch-configuration selection, re-run for B200.
+
+The reference sweeps launch candidates per path on 20 tuning shapes, picks
+per path the candidate with the minimum SUM of mean latency over those shapes
+(ties to the smaller value), freezes it, and scores it on held-out shapes by
+regret = frozen_total / oracle_total - 1, where total = FWD + dX + dK and the
+oracle picks the best candidate per shape and path
+(benchmark/benchmark_pathtile_candidate_sweep.py:485-560,
+scripts/aggregate_pathtile_results.py:222-240 and :376-420).
+
+B200 candidate axes are runtime values of the native library (no
+recompilation): rows per tile (one thread per row), TMA ring depth and
+persistent CTAs per SM, per path.  Every candidate is validated before it is
+timed, at a batch of at most 128, against PyTorch's own conv1d on the GPU with
+TF32 off (the reference's validation recipe, :153-243).
+
+Modes:
+  run        sweep one preset, one trial -> <out>/trialN/raw.csv, summary.csv
+  aggregate  average trials, select the frozen policy -> frozen_config.json and
+             the C header pathtile_b200/csrc/pt_frozen_config.h
+  regret     score the frozen policy on a held-out sweep against its per-shape oracle
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import json
+import statistics
+import time
+import zlib
+from dataclasses import asdict, dataclass
+from pathlib import Path
+
+PATHS = ("fwd", "bwd_input", "bwd_weight")
+ROWS = (64, 128, 256)
+STAGES = (2, 3, 4)
+CTAS = (1, 2, 3, 4)
+HEADER = Path(__file__).resolve().parent / "csrc" / "pt_frozen_config.h"
+
+
+@dataclass(frozen=True)
+class ShapeCase:
+    config_id: str
+    B: int
+    H: int
+    L: int
+    K: int
+    sweep_group: str
+
+    def validate(self) -> None:
+        if min(self.B, self.H, self.L, self.K) <= 0:
+            raise ValueError(f"All dimensions must be positive: {self}")
+        if self.L > 48 or self.K > 48:
+            raise ValueError(f"{self.config_id}: kernels require L<=48 and K<=48")
+
+
+def _c(cid: str, B: int, H: int, L: int, K: int, group: str) -> ShapeCase:
+    return ShapeCase(cid, B, H, L, K, group)
+
+
+# The reference's 20 tuning shapes and 10 held-out shapes
+# (benchmark/benchmark_shape_sweep_ampere.py:79-178), same ids and sizes.
+PATHTILE_TRAIN_CASES = [
+    _c("main_b16384_h128_l48_k48", 16384, 128, 48, 48, "main"),
+    _c("batch_b2048_h128_l48_k48", 2048, 128, 48, 48, "batch"),
+    _c("batch_b8192_h128_l48_k48", 8192, 128, 48, 48, "batch"),
+    _c("channel_b8192_h64_l48_k48", 8192, 64, 48, 48, "channel"),
+    _c("channel_b8192_h256_l48_k48", 8192, 256, 48, 48, "channel"),
+    _c("sequence_b8192_h128_l16_k16", 8192, 128, 16, 16, "sequence"),
+    _c("sequence_b8192_h128_l24_k24", 8192, 128, 24, 24, "sequence"),
+    _c("sequence_b8192_h128_l32_k32", 8192, 128, 32, 32, "sequence"),
+    _c("kernel_b8192_h128_l48_k8", 8192, 128, 48, 8, "kernel"),
+    _c("kernel_b8192_h128_l48_k24", 8192, 128, 48, 24, "kernel"),
+    _c("mix_b4096_h64_l32_k16", 4096, 64, 32, 16, "mixed"),
+    _c("mix_b4096_h256_l48_k24", 4096, 256, 48, 24, "mixed"),
+    _c("mix_b2048_h64_l24_k8", 2048, 64, 24, 8, "mixed"),
+    _c("mix_b2048_h256_l32_k32", 2048, 256, 32, 32, "mixed"),
+    _c("mix_b8192_h64_l32_k24", 8192, 64, 32, 24, "mixed"),
+    _c("mix_b8192_h256_l24_k16", 8192, 256, 24, 16, "mixed"),
+    _c("mix_b16384_h64_l48_k8", 16384, 64, 48, 8, "mixed"),
+    _c("mix_b16384_h256_l16_k16", 16384, 256, 16, 16, "mixed"),
+    _c("mix_b16384_h128_l32_k24", 16384, 128, 32, 24, "mixed"),
+    _c("mix_b4096_h128_l48_k32", 4096, 128, 48, 32, "mixed"),
+]
+
+PATHTILE_HOLDOUT_CASES = [
+    _c("holdout_b4096_h96_l40_k20", 4096, 96, 40, 20, "holdout"),
+    _c("holdout_b12288_h192_l40_k32", 12288, 192, 40, 32, "holdout"),
+    _c("holdout_b12288_h96_l20_k12", 12288, 96, 20, 12, "holdout"),
+    _c("holdout_b4096_h192_l28_k24", 4096, 192, 28, 24, "holdout"),
+    _c("holdout_b12288_h64_l40_k40", 12288, 64, 40, 40, "holdout"),
+    _c("holdout_b4096_h256_l20_k16", 4096, 256, 20, 16, "holdout"),
+    _c("holdout_b2048_h192_l40_k32", 2048, 192, 40, 32, "holdout"),
+    _c("holdout_b12288_h128_l28_k20", 12288, 128, 28, 20, "holdout"),
+    _c("holdout_b4096_h64_l40_k12", 4096, 64, 40, 12, "holdout"),
+    _c("holdout_b12288_h256_l32_k24", 12288, 256, 32, 24, "holdout"),
+]
+
+# Held-out sweep of this build's specification: B x H x (L, K), K <= L.
+SWEEP_LK = [(24, 8), (24, 16), (32, 8), (32, 16), (32, 32), (48, 8), (48, 16), (48, 32), (48, 48)]
+HELDOUT_SWEEP_CASES = [
+    _c(f"sweep_b{B}_h{H}_l{L}_k{K}", B, H, L, K, "sweep")
+    for B in (4096, 16384, 32768) for H in (64, 128, 256) for (L, K) in SWEEP_LK
+]
+
+EDGE_CASES = [
+    _c("edge_b4096_h64_l37_k13", 4096, 64, 37, 13, "edge"),
+    _c("edge_b8192_h256_l16_k4", 8192, 256, 16, 4, "edge"),
+    _c("edge_b16384_h128_l48_k3", 16384, 128, 48, 3, "edge"),
+    _c("edge_b2048_h512_l33_k33", 2048, 512, 33, 33, "edge"),
+]
+
+SMOKE_CASES = [
+    _c("smoke_b64_h8_l16_k8", 64, 8, 16, 8, "smoke"),
+    _c("smoke_b128_h16_l48_k48", 128, 16, 48, 48, "smoke"),
+]
+
+PRESETS = {
+    "pathtile-train": PATHTILE_TRAIN_CASES,
+    "pathtile-holdout": PATHTILE_HOLDOUT_CASES,
+    "heldout-sweep": HELDOUT_SWEEP_CASES,
+    "edge": EDGE_CASES,
+    "smoke": SMOKE_CASES,
+}
+
+
+def cases_for_preset(preset: str) -> list[ShapeCase]:
+    if preset not in PRESETS:
+        raise ValueError(f"Unknown preset: {preset}")
+    cases = list(PRESETS[preset])
+    for c in cases:
+        c.validate()
+    return cases
+
+
+def case_seed(base_seed: int, case: ShapeCase) -> int:
+    """base + crc32(config id), as benchmark_pathtile_candidate_sweep.py:109-110."""
+    return int(base_seed + zlib.crc32(case.config_id.encode("utf-8")))
+
+
+def candidates() -> list[tuple[int, int, int]]:
+    return [(r, s, c) for r in ROWS for s in STAGES for c in CTAS]
+
+
+def candidate_id(c: tuple[int, int, int]) -> str:
+    return f"r{c[0]}s{c[1]}c{c[2]}"
+
+
+# ---------------------------------------------------------------------------
+# Selection logic (pure; unit-tested on CPU)
+# ---------------------------------------------------------------------------
+def select_policy(summary: list[dict]) -> dict[str, tuple[int, int, int]]:
+    """Per path, the candidate with the minimum sum over shapes of mean_ms;
+    ties go to the smaller candidate tuple.  Candidates missing any shape
+    (invalid or failed) are not eligible."""
+    shapes = {r["config_id"] for r in summary}
+    chosen = {}
+    for path in PATHS:
+        totals: dict[tuple[int, int, int], float] = {}
+        seen: dict[tuple[int, int, int], set] = {}
+        for r in summary:
+            if r["phase"] != path:
+                continue
+            c = (int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))
+            totals[c] = totals.get(c, 0.0) + float(r["mean_ms"])
+            seen.setdefault(c, set()).add(r["config_id"])
+        eligible = [(t, c) for c, t in totals.items() if seen[c] == shapes]
+        if not eligible:
+            raise ValueError(f"No candidate covers every shape for {path}")
+        chosen[path] = min(eligible)[1]
+    return chosen
+
+
+def oracle_totals(summary: list[dict]) -> dict[str, dict[str, float]]:
+    """Per shape: best mean_ms per path over all candidates."""
+    best: dict[str, dict[str, float]] = {}
+    for r in summary:
+        d = best.setdefault(r["config_id"], {})
+        v = float(r["mean_ms"])
+        if r["phase"] not in d or v < d[r["phase"]]:
+            d[r["phase"]] = v
+    return best
+
+
+def regret_table(summary: list[dict], policy: dict[str, tuple[int, int, int]]) -> list[dict]:
+    """Per shape: frozen total, oracle total and regret (frozen/oracle - 1)."""
+    lookup = {}
+    for r in summary:
+        lookup[(r["config_id"], r["phase"], int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))] = float(
+            r["mean_ms"])
+    best = oracle_totals(summary)
+    rows = []
+    for cid in sorted(best):
+        frozen = sum(lookup[(cid, p, *policy[p])] for p in PATHS)
+        oracle = sum(best[cid][p] for p in PATHS)
+        rows.append({"config_id": cid, "frozen_total_ms": frozen, "oracle_total_ms": oracle,
+                     "regret_pct": 100.0 * (frozen / oracle - 1.0)})
+    return rows
+
+
+def render_header(policy: dict[str, tuple[int, int, int]], source: str) -> str:
+    lines = [
+        "// pt_frozen_config.h -- launch configuration per path, frozen offline.",
+        "//",
+        "// Written by `python -m pathtile_b200.pathtile --mode aggregate`: per path the",
+        "// candidate (rows per tile, ring stages, CTAs per SM) with the minimum sum of",
+        "// mean latency over the tuning shapes, ties to the smaller candidate -- the",
+        "// reference's selection rule (scripts/aggregate_pathtile_results.py:222-240).",
+        "// Deployment does no per-shape search.",
+        "#pragma once",
+        "",
+        "namespace pt {",
+        "",
+        "struct LaunchCfg {",
+        "  int rows;         // rows per tile = threads doing math per CTA (32..256)",
+        "  int stages;       // shared-memory ring depth (2..4)",
+        "  int ctas_per_sm;  // persistent CTAs per SM (1..4), clamped by occupancy",
+        "};",
+        "",
+        "// Index: PT_PATH_FWD, PT_PATH_DX, PT_PATH_DK.",
+        "constexpr LaunchCfg kFrozenCfg[3] = {",
+    ]
+    for p, name in zip(PATHS, ("FWD", "DX", "DK")):
+        r, s, c = policy[p]
+        lines.append(f"    {{{r}, {s}, {c}}},  // {name}")
+    lines += ["};", "", f'constexpr const char* kFrozenCfgSource = "{source}";', "", "}  // namespace pt", ""]
+    return "\n".join(lines)
+
+
+# ---------------------------------------------------------------------------
+# GPU sweep
+# ---------------------------------------------------------------------------
+def _make_inputs(case: ShapeCase, seed: int, B: int, device):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(B, case.H, case.L, device=device, generator=g)
+    k = torch.randn(case.H, case.K, device=device, generator=g) / (case.K ** 0.5)
+    dy = torch.randn(B, case.H, case.L, device=device, generator=g)
+    return x, k, dy
+
+
+def _validate(case: ShapeCase, seed: int, device) -> dict[str, float]:
+    """Max normalised error of each path at B<=128 against torch conv1d (TF32 off)."""
+    import torch
+    import torch.nn.functional as F
+
+    from . import ops
+
+    Bv = min(case.B, 128)
+    x, k, dy = _make_inputs(case, seed, Bv, device)
+    y = ops.fwd(x, k)
+    gx = ops.dx(dy, k)
+    gk = torch.empty_like(k)
+    ops.dk(dy, x, gk)
+    xr = x.clone().requires_grad_(True)
+    kr = k.clone().requires_grad_(True)
+    left = case.K // 2
+    yr = F.conv1d(F.pad(xr, (left, case.K - 1 - left)), kr.unsqueeze(1), groups=case.H)
+    gxr, gkr = torch.autograd.grad(yr, (xr, kr), dy)
+    err = {}
+    for name, a, b in (("fwd", y, yr), ("bwd_input", gx, gxr), ("bwd_weight", gk, gkr)):
+        err[name] = float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+    return err
+
+
+def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: int, out: Path) -> None:
+    import torch
+
+    from . import ops
+
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", torch.cuda.current_device())
+    out.mkdir(parents=True, exist_ok=True)
+    order = cases if trial % 2 else list(reversed(cases))
+    cands = candidates() if trial % 2 else list(reversed(candidates()))
+    raw_rows, summ = [], []
+    stream = torch.cuda.current_stream()
+    for case in order:
+        sd = case_seed(seed, case)
+        x, k, dy = _make_inputs(case, sd, case.B, dev)
+        y, gx, gk = torch.empty_like(x), torch.empty_like(x), torch.empty_like(k)
+        launch = {
+            "fwd": lambda: ops.fwd(x, k, y),
+            "bwd_input": lambda: ops.dx(dy, k, gx),
+            "bwd_weight": lambda: ops.dk(dy, x, gk, mode="deterministic"),
+        }
+        for cand in cands:
+            for p in PATHS:
+                ops.set_config(p, *cand)
+            err = _validate(case, sd, dev)
+            for p in PATHS:
+                ok = err[p] <= (1e-5 if p != "bwd_weight" else 1e-4)
+                if not ok:
+                    summ.append({**asdict(case), "trial": trial, "phase": p, "rows": cand[0], "stages": cand[1],
+                                 "ctas_per_sm": cand[2], "valid": False, "max_norm_err": err[p]})
+                    continue
+                for _ in range(warmup):
+                    launch[p]()
+                times = []
+                for _ in range(runs):
+                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s.record(stream)
+                    launch[p]()
+                    e.record(stream)
+                    times.append((s, e))
+                torch.cuda.synchronize()
+                ms = [s.elapsed_time(e) for s, e in times]
+                info = ops.kernel_info(p, case.B, case.H, case.L, case.K)
+                for i, v in enumerate(ms):
+                    raw_rows.append({"config_id": case.config_id, "trial": trial, "phase": p,
+                                     "candidate": candidate_id(cand), "run": i, "runtime_ms": v})
+                summ.append({**asdict(case), "trial": trial, "phase": p, "rows": cand[0], "stages": cand[1],
+                             "ctas_per_sm": cand[2], "valid": True, "max_norm_err": err[p],
+                             "mean_ms": statistics.mean(ms), "median_ms": statistics.median(ms),
+                             "std_ms": statistics.stdev(ms) if len(ms) > 1 else 0.0,
+                             "grid": info["grid"], "resident_blocks_per_sm": info["resident_blocks_per_sm"]})
+        del x, k, dy, y, gx, gk
+        torch.cuda.empty_cache()
+    for p in PATHS:
+        ops.set_config(p, 0)
+    _write_csv(out / "raw.csv", raw_rows)
+    _write_csv(out / "summary.csv", summ)
+    (out / "metadata.json").write_text(json.dumps({
+        "trial": trial, "warmup": warmup, "runs": runs, "seed": seed, "device": torch.cuda.get_device_name(),
+        "cases": [asdict(c) for c in cases], "candidates": [candidate_id(c) for c in candidates()],
+        "created_unix": time.time(),
+        "measurement_contract": {"strict_fp32": True, "cuda_event_kernel_timing": True,
+                                 "validation_timed": False, "dk_mode": "deterministic",
+                                 "candidate_order": "listed on odd trials; reversed on even trials",
+                                 "shape_order": "listed on odd trials; reversed on even trials"}},
+        indent=1))
+
+
+def _write_csv(path: Path, rows: list[dict]) -> None:
+    if not rows:
+        path.write_text("")
+        return
+    keys = list(dict.fromkeys(k for r in rows for k in r))
+    with path.open("w", newline="") as f:
+        w = csv.DictWriter(f, fieldnames=keys)
+        w.writeheader()
+        w.writerows(rows)
+
+
+def _read_csv(path: Path) -> list[dict]:
+    with path.open() as f:
+        return list(csv.DictReader(f))
+
+
+def aggregate_trials(root: Path) -> list[dict]:
+    """Mean over trials of each (shape, phase, candidate) mean_ms; invalid rows dropped."""
+    acc: dict[tuple, list[float]] = {}
+    for t in sorted(root.glob("trial*/summary.csv")):
+        for r in _read_csv(t):
+            if r.get("valid") != "True":
+                continue
+            key = (r["config_id"], r["phase"], int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))
+            acc.setdefault(key, []).append(float(r["mean_ms"]))
+    return [{"config_id": k[0], "phase": k[1], "rows": k[2], "stages": k[3], "ctas_per_sm": k[4],
+             "mean_ms": statistics.mean(v), "trials": len(v)} for k, v in sorted(acc.items())]
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--mode", choices=("run", "aggregate", "regret"), required=True)
+    ap.add_argument("--preset", default="pathtile-train", choices=sorted(PRESETS))
+    ap.add_argument("--out", type=Path, required=True, help="results directory of this preset")
+    ap.add_argument("--trial", type=int, default=1)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--runs", type=int, default=30)
+    ap.add_argument("--seed", type=int, default=42)
+    ap.add_argument("--write-header", action="store_true", help="aggregate: rewrite pt_frozen_config.h")
+    ap.add_argument("--policy", type=Path, help="regret: frozen_config.json to score")
+    args = ap.parse_args()
+    if args.mode == "run":
+        run_sweep(cases_for_preset(args.preset), args.warmup, args.runs, args.trial, args.seed,
+                  args.out / f"trial{args.trial}")
+    elif args.mode == "aggregate":
+        summary = aggregate_trials(args.out)
+        policy = select_policy(summary)
+        _write_csv(args.out / "aggregate_summary.csv", summary)
+        reg = regret_table(summary, policy)
+        doc = {"policy": {p: dict(zip(("rows", "stages", "ctas_per_sm"), policy[p])) for p in PATHS},
+               "tuning_preset": args.preset, "tuning_shapes": sorted({r["config_id"] for r in summary}),
+               "training_regret_pct_mean": statistics.mean(r["regret_pct"] for r in reg)}
+        (args.out / "frozen_config.json").write_text(json.dumps(doc, indent=1))
+        print(json.dumps(doc, indent=1))
+        if args.write_header:
+            HEADER.write_text(render_header(policy, f"B200 sweep of preset {args.preset}"))
+    else:
+        summary = aggregate_trials(args.out)
+        pol = json.loads(args.policy.read_text())["policy"]
+        policy = {p: (pol[p]["rows"], pol[p]["stages"], pol[p]["ctas_per_sm"]) for p in PATHS}
+        reg = regret_table(summary, policy)
+        _write_csv(args.out / "regret.csv", reg)
+        vals = [r["regret_pct"] for r in reg]
+        print(json.dumps({"shapes": len(vals), "mean_regret_pct": statistics.mean(vals),
+                          "max_regret_pct": max(vals),
+                          "within_1pct": sum(v <= 1.0 for v in vals),
+                          "within_2pct": sum(v <= 2.0 for v in vals)}, indent=1))
+
+
+if __name__ == "__main__":
+    main()
