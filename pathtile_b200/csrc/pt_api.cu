@@ -166,22 +166,23 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
   const int T = g.Th * g.Tb;
   const long long tile_bytes = static_cast<long long>(g.pitch) * T * 4;
   long long stage = (tile_bytes + 1023) / 1024 * 1024;
-  const int n_in = (path == PT_PATH_DK) ? 2 : 1;
-  // Fewer stages when the ring would not fit the per-block shared memory.
+  // Buffers: DK = (dy, x) per stage; FWD/DX = input ring + 2 output buffers.
+  auto n_buf = [&](int stages) { return (path == PT_PATH_DK) ? 2 * stages : stages + 2; };
+  // Fewer stages when the buffers would not fit the per-block shared memory.
   while (g.stages > 2 &&
-         static_cast<long long>(n_in) * g.stages * stage + g.stages * 8 + 1024 > di.max_smem)
+         static_cast<long long>(n_buf(g.stages)) * stage + g.stages * 8 + 1024 > di.max_smem)
     --g.stages;
   if (path == PT_PATH_DK) {
     // The idle ring doubles as the [K][T] in-CTA reduction buffer at the end.
     const long long red = static_cast<long long>(K) * T * 4;
-    if (n_in * g.stages * stage < red)
-      stage = ((red + n_in * g.stages - 1) / (n_in * g.stages) + 1023) / 1024 * 1024;
+    if (n_buf(g.stages) * stage < red)
+      stage = ((red + n_buf(g.stages) - 1) / n_buf(g.stages) + 1023) / 1024 * 1024;
   }
-  if (static_cast<long long>(n_in) * g.stages * stage + g.stages * 8 + 1024 > di.max_smem)
+  if (static_cast<long long>(n_buf(g.stages)) * stage + g.stages * 8 + 1024 > di.max_smem)
     return PT_ERR_UNSUPPORTED;
   g.stage_bytes = static_cast<unsigned>(stage);
   g.tx_bytes = static_cast<unsigned>(tile_bytes);
-  p.smem = static_cast<size_t>(n_in) * g.stages * stage + static_cast<size_t>(g.stages) * 8 + 1024;
+  p.smem = static_cast<size_t>(n_buf(g.stages)) * stage + static_cast<size_t>(g.stages) * 8 + 1024;
   p.threads = round_up(T, 32);
   p.func = (path == PT_PATH_FWD) ? e.fwd : (path == PT_PATH_DX) ? e.dx : e.dk;
   p.exact = true;

@@ -215,19 +215,30 @@ __device__ __forceinline__ void row_store(float* __restrict__ p, const float (&v
 }
 
 // One output row: y[t] = sum_j in[t + j - PAD] * taps[j], in-range pairs only
-// (the out-of-range pairs are dropped at compile time: no predicates).
+// (the out-of-range pairs are dropped at compile time: no predicates).  Four
+// outputs advance together so consecutive FFMAs are independent; each output
+// still sums its taps in ascending j.
 template <int L, int K, int PAD>
 __device__ __forceinline__ void conv_row(const float (&in)[L], const float (&taps)[K],
                                          float (&y)[L]) {
+  constexpr int G = 4;
 #pragma unroll
-  for (int t = 0; t < L; ++t) {
-    float acc = 0.0f;
+  for (int t0 = 0; t0 < L; t0 += G) {
+    float acc[G];
+#pragma unroll
+    for (int u = 0; u < G; ++u) acc[u] = 0.0f;
 #pragma unroll
     for (int j = 0; j < K; ++j) {
-      const int i = t + j - PAD;
-      if (i >= 0 && i < L) acc = fmaf(in[i], taps[j], acc);
+#pragma unroll
+      for (int u = 0; u < G; ++u) {
+        const int t = t0 + u;
+        const int i = t + j - PAD;
+        if (t < L && i >= 0 && i < L) acc[u] = fmaf(in[i], taps[j], acc[u]);
+      }
     }
-    y[t] = acc;
+#pragma unroll
+    for (int u = 0; u < G; ++u)
+      if (t0 + u < L) y[t0 + u] = acc[u];
   }
 }
 
@@ -300,7 +311,11 @@ __device__ __forceinline__ uint32_t tile_tx_bytes(const TileGeom& g, int hb, int
 }
 
 // ---------------------------------------------------------------------------
-// FWD / DX: persistent, TMA-pipelined, one row per thread, in-place output.
+// FWD / DX: persistent and TMA-pipelined, one row per thread.
+// Shared memory: input ring [stages] | output double buffer [2] | mbarriers.
+// An input stage is released as soon as every thread holds its row in
+// registers, so during the FFMA nest the whole ring is in flight; outputs go
+// to the double buffer and leave by TMA store.
 // ---------------------------------------------------------------------------
 template <int L, int K, int OP, int LOADER>
 __global__ void __launch_bounds__(256, 1)
@@ -328,7 +343,8 @@ __global__ void __launch_bounds__(256, 1)
     taps[j] = thread_has_row ? __ldg(taps_hk + static_cast<long long>(h) * K + src) : 0.0f;
   }
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(g.stages) * g.stage_bytes);
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(g.stages + 2) * g.stage_bytes);
   if (tid == 0) {
     if constexpr (LOADER == LOAD_TMA3D) {
       prefetch_tmap(&tm_in);
@@ -342,6 +358,9 @@ __global__ void __launch_bounds__(256, 1)
   auto stage_ptr = [&](int s) -> float* {
     return reinterpret_cast<float*>(smem + static_cast<size_t>(s) * g.stage_bytes);
   };
+  auto ybuf_ptr = [&](int i) -> float* {
+    return reinterpret_cast<float*>(smem + static_cast<size_t>(g.stages + i) * g.stage_bytes);
+  };
   auto load = [&](int it) {
     const int s = it % g.stages;
     const int q = cur.q(it);
@@ -351,7 +370,7 @@ __global__ void __launch_bounds__(256, 1)
   };
 
   if (tid == 0) {
-    const int pro = min(g.stages - 1, cur.n_it);
+    const int pro = min(g.stages, cur.n_it);
     for (int it = 0; it < pro; ++it) load(it);
   }
 
@@ -362,32 +381,32 @@ __global__ void __launch_bounds__(256, 1)
     const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_FULL);
     const int q = cur.q(it);
     const bool row_valid = thread_has_row && (q * g.Tb + b_local < g.B);
-    float* rowp = stage_ptr(s) + static_cast<size_t>(tid) * g.pitch;
-    if (ok && row_valid) {
-      float xin[L];
+    float xin[L];
+    if (ok && row_valid) row_load<L, LOADER>(stage_ptr(s) + static_cast<size_t>(tid) * g.pitch, xin);
+    // Every row of stage s is in registers: refill it with tile it+stages.
+    if (__syncthreads_or(!ok)) break;
+    if (tid == 0 && it + g.stages < cur.n_it) load(it + g.stages);
+    float* ybuf = ybuf_ptr(it & 1);
+    if (row_valid) {
       float yout[L];
-      row_load<L, LOADER>(rowp, xin);
       conv_row<L, K, PAD>(xin, taps, yout);
-      row_store<L, LOADER>(rowp, yout);
+      row_store<L, LOADER>(ybuf + static_cast<size_t>(tid) * g.pitch, yout);
     }
     fence_proxy_async_smem();
-    if (__syncthreads_or(!ok)) break;
+    __syncthreads();
     if (tid == 0) {
       if constexpr (LOADER == LOAD_TMA3D) {
-        tma_store_3d(&tm_out, smem_u32(stage_ptr(s)), 0, cur.hb * g.Th, q * g.Tb);
+        tma_store_3d(&tm_out, smem_u32(ybuf), 0, cur.hb * g.Th, q * g.Tb);
       } else {
         long long row0;
         int nrows;
         tile_rows(g, cur.hb, q, row0, nrows);
-        bulk_store_1d(out + row0 * g.L, smem_u32(stage_ptr(s)),
-                      static_cast<uint32_t>(nrows) * g.L * 4u);
+        bulk_store_1d(out + row0 * g.L, smem_u32(ybuf), static_cast<uint32_t>(nrows) * g.L * 4u);
       }
       bulk_commit();
-      // Refill the stage of tile it-1 with tile it-1+stages once its store has
-      // finished reading shared memory (tile it's store may still be reading).
+      // The store of tile it-1 has read its buffer before anyone writes it again
+      // (next iteration, after the first barrier, which thread 0 reaches after this).
       bulk_wait_read<1>();
-      const int nxt = it + g.stages - 1;
-      if (nxt < cur.n_it) load(nxt);
     }
   }
 
@@ -395,7 +414,7 @@ __global__ void __launch_bounds__(256, 1)
     bulk_wait_all();
     if (it < cur.n_it) {
       // Aborted: let every load this CTA issued land before shared memory goes away.
-      const int issued_end = min(cur.n_it, it + g.stages - 1);
+      const int issued_end = min(cur.n_it, it + g.stages);
       for (int k2 = it + 1; k2 < issued_end; ++k2) {
         const int s = k2 % g.stages;
         const uint32_t parity = static_cast<uint32_t>(k2 / g.stages) & 1u;
@@ -406,7 +425,8 @@ __global__ void __launch_bounds__(256, 1)
 }
 
 // ---------------------------------------------------------------------------
-// DK pass 1: persistent, TMA-pipelined; per-thread accumulators over all tiles,
+// DK pass 1: persistent, TMA-pipelined (stages released once read into
+// registers); per-thread accumulators over all tiles,
 // then an in-CTA reduction over the Tb batch slots of each channel (fixed
 // order) and either one float atomic per (CTA,h,j) or one partial per (CTA,j,h).
 // ---------------------------------------------------------------------------
@@ -468,18 +488,16 @@ __global__ void __launch_bounds__(256, 1)
     const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_FULL);
     const int q = cur.q(it);
     const bool row_valid = thread_has_row && (q * g.Tb + b_local < g.B);
+    float gyr[L];
+    float xr[L];
     if (ok && row_valid) {
-      float gyr[L];
-      float xr[L];
       row_load<L, LOADER>(buf(s, 0) + static_cast<size_t>(tid) * g.pitch, gyr);
       row_load<L, LOADER>(buf(s, 1) + static_cast<size_t>(tid) * g.pitch, xr);
-      xcorr_row<L, K, PAD>(gyr, xr, acc);
     }
+    // Every row of stage s is in registers: refill it before the FFMA nest.
     if (__syncthreads_or(!ok)) break;
-    if (tid == 0) {
-      const int nxt = it + g.stages;
-      if (nxt < cur.n_it) load(nxt);
-    }
+    if (tid == 0 && it + g.stages < cur.n_it) load(it + g.stages);
+    if (row_valid) xcorr_row<L, K, PAD>(gyr, xr, acc);
   }
 
   if (it < cur.n_it) {
