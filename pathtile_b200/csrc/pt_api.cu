@@ -166,11 +166,11 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
   const int T = g.Th * g.Tb;
   const long long tile_bytes = static_cast<long long>(g.pitch) * T * 4;
   long long stage = (tile_bytes + 1023) / 1024 * 1024;
-  // Buffers: DK = (dy, x) per stage; FWD/DX = input ring + 2 output buffers.
-  auto n_buf = [&](int stages) { return (path == PT_PATH_DK) ? 2 * stages : stages + 2; };
+  // Buffers: DK = (dy, x) per stage; FWD/DX = input ring + 1 output buffer.
+  auto n_buf = [&](int stages) { return (path == PT_PATH_DK) ? 2 * stages : stages + 1; };
   // Fewer stages when the buffers would not fit the per-block shared memory.
   while (g.stages > 2 &&
-         static_cast<long long>(n_buf(g.stages)) * stage + g.stages * 8 + 1024 > di.max_smem)
+         static_cast<long long>(n_buf(g.stages)) * stage + (2LL * g.stages + 2) * 8 + 1024 > di.max_smem)
     --g.stages;
   if (path == PT_PATH_DK) {
     // The idle ring doubles as the [K][T] in-CTA reduction buffer at the end.
@@ -178,12 +178,13 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
     if (n_buf(g.stages) * stage < red)
       stage = ((red + n_buf(g.stages) - 1) / n_buf(g.stages) + 1023) / 1024 * 1024;
   }
-  if (static_cast<long long>(n_buf(g.stages)) * stage + g.stages * 8 + 1024 > di.max_smem)
+  const long long bar_bytes = (2LL * g.stages + 2) * 8;  // full/empty per stage + yfull/yempty
+  if (static_cast<long long>(n_buf(g.stages)) * stage + bar_bytes + 1024 > di.max_smem)
     return PT_ERR_UNSUPPORTED;
   g.stage_bytes = static_cast<unsigned>(stage);
   g.tx_bytes = static_cast<unsigned>(tile_bytes);
-  p.smem = static_cast<size_t>(n_buf(g.stages)) * stage + static_cast<size_t>(g.stages) * 8 + 1024;
-  p.threads = round_up(T, 32);
+  p.smem = static_cast<size_t>(n_buf(g.stages)) * stage + static_cast<size_t>(bar_bytes) + 1024;
+  p.threads = round_up(T, 32) + 32;  // consumer warps + one producer warp
   p.func = (path == PT_PATH_FWD) ? e.fwd : (path == PT_PATH_DX) ? e.dx : e.dk;
   p.exact = true;
   int rc = ensure_smem_attr(di, p.func, p.smem);

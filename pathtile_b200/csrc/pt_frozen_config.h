@@ -18,8 +18,8 @@ struct LaunchCfg {
 
 // Index: PT_PATH_FWD, PT_PATH_DX, PT_PATH_DK.
 constexpr LaunchCfg kFrozenCfg[3] = {
-    {128, 2, 2},  // FWD
-    {128, 2, 2},  // DX
+    {128, 3, 2},  // FWD
+    {128, 3, 2},  // DX
     {128, 2, 2},  // DK
 };
 

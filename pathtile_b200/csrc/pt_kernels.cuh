@@ -106,6 +106,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Barrier `id` over the first `n` threads (a multiple of 32) of the CTA,
+// returning the OR of `pred` over them.
+__device__ __forceinline__ bool named_barrier_or(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void named_barrier(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -311,14 +334,48 @@ __device__ __forceinline__ uint32_t tile_tx_bytes(const TileGeom& g, int hb, int
 }
 
 // ---------------------------------------------------------------------------
-// FWD / DX: persistent and TMA-pipelined, one row per thread.
-// Shared memory: input ring [stages] | output double buffer [2] | mbarriers.
-// An input stage is released as soon as every thread holds its row in
-// registers, so during the FFMA nest the whole ring is in flight; outputs go
-// to the double buffer and leave by TMA store.
+// Warp-specialised persistent kernels.  The CTA is `nc` consumer threads (one
+// per tile row, rounded up to whole warps) plus one producer warp whose lane 0
+// drives TMA.  Stages are handed over with mbarriers only:
+//   full[s]  : producer arrive.expect_tx + TMA bytes  -> consumers may read
+//   empty[s] : every consumer thread, once its row is in registers
+//              -> the producer refills stage s (so the whole ring is in flight
+//                 while the FFMA nests run)
+//   FWD/DX also stage the output tile in one buffer:
+//   yfull    : every consumer thread after writing its output row -> TMA store
+//   yempty   : producer, once the previous store has read the buffer
+// Consumer warps never wait on each other.  Every wait is bounded; a thread
+// whose wait expires stops, the producer drains the loads it issued, and the
+// error word records it.
+// ---------------------------------------------------------------------------
+struct PipeBars {
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* yfull;
+  uint64_t* yempty;
+};
+
+__device__ __forceinline__ PipeBars carve_bars(unsigned char* base, int stages) {
+  uint64_t* b = reinterpret_cast<uint64_t*>(base);
+  return PipeBars{b, b + stages, b + 2 * stages, b + 2 * stages + 1};
+}
+
+// Producer tail: every stage's most recently issued load has landed (bounded),
+// then all bulk stores are complete.
+__device__ __forceinline__ void producer_drain(const PipeBars& bars, int stages, int issued,
+                                               unsigned* err) {
+  for (int t = max(0, issued - stages); t < issued; ++t) {
+    const uint32_t parity = static_cast<uint32_t>(t / stages) & 1u;
+    if (!mbar_wait_bounded(smem_u32(&bars.full[t % stages]), parity, err, DEVERR_TIMEOUT_DRAIN)) break;
+  }
+  bulk_wait_all();
+}
+
+// ---------------------------------------------------------------------------
+// FWD / DX.  Shared memory: input ring [stages] | output buffer | mbarriers.
 // ---------------------------------------------------------------------------
 template <int L, int K, int OP, int LOADER>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(288, 1)
     conv_rows_kernel(const __grid_constant__ CUtensorMap tm_in,
                      const __grid_constant__ CUtensorMap tm_out, const float* __restrict__ in,
                      const float* __restrict__ taps_hk, float* __restrict__ out, const TileGeom g,
@@ -328,73 +385,54 @@ __global__ void __launch_bounds__(256, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   const int tid = static_cast<int>(threadIdx.x);
+  const int nc = static_cast<int>(blockDim.x) - 32;  // consumer threads
   const TileCursor cur(g);
-  const int T = g.Th * g.Tb;
-  const int h_local = tid % g.Th;
-  const int b_local = tid / g.Th;
-  const int h = cur.hb * g.Th + h_local;
-  const bool thread_has_row = (tid < T) && (h < g.H);
+  const int S = g.stages;
+  auto stage_ptr = [&](int s) -> float* {
+    return reinterpret_cast<float*>(smem + static_cast<size_t>(s) * g.stage_bytes);
+  };
+  float* ybuf = stage_ptr(S);
+  const PipeBars bars = carve_bars(smem + static_cast<size_t>(S + 1) * g.stage_bytes, S);
 
-  // This thread's taps, once per kernel (reversed for DX).
-  float taps[K];
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
-    const int src = (OP == OP_FWD) ? j : (K - 1 - j);
-    taps[j] = thread_has_row ? __ldg(taps_hk + static_cast<long long>(h) * K + src) : 0.0f;
-  }
-
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(g.stages + 2) * g.stage_bytes);
   if (tid == 0) {
-    if constexpr (LOADER == LOAD_TMA3D) {
-      prefetch_tmap(&tm_in);
-      prefetch_tmap(&tm_out);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&bars.full[s]), 1);
+      mbar_init(smem_u32(&bars.empty[s]), static_cast<uint32_t>(nc));
     }
-    for (int s = 0; s < g.stages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    mbar_init(smem_u32(bars.yfull), static_cast<uint32_t>(nc));
+    mbar_init(smem_u32(bars.yempty), 1);
     fence_mbar_init();
   }
   __syncthreads();
 
-  auto stage_ptr = [&](int s) -> float* {
-    return reinterpret_cast<float*>(smem + static_cast<size_t>(s) * g.stage_bytes);
-  };
-  auto ybuf_ptr = [&](int i) -> float* {
-    return reinterpret_cast<float*>(smem + static_cast<size_t>(g.stages + i) * g.stage_bytes);
-  };
-  auto load = [&](int it) {
-    const int s = it % g.stages;
-    const int q = cur.q(it);
-    const uint32_t bar = smem_u32(&bars[s]);
-    mbar_arrive_expect_tx(bar, tile_tx_bytes<LOADER>(g, cur.hb, q));
-    issue_tile_load<LOADER>(g, &tm_in, in, cur.hb, q, smem_u32(stage_ptr(s)), bar);
-  };
-
-  if (tid == 0) {
-    const int pro = min(g.stages, cur.n_it);
-    for (int it = 0; it < pro; ++it) load(it);
-  }
-
-  int it = 0;
-  for (; it < cur.n_it; ++it) {
-    const int s = it % g.stages;
-    const uint32_t parity = static_cast<uint32_t>(it / g.stages) & 1u;
-    const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_FULL);
-    const int q = cur.q(it);
-    const bool row_valid = thread_has_row && (q * g.Tb + b_local < g.B);
-    float xin[L];
-    if (ok && row_valid) row_load<L, LOADER>(stage_ptr(s) + static_cast<size_t>(tid) * g.pitch, xin);
-    // Every row of stage s is in registers: refill it with tile it+stages.
-    if (__syncthreads_or(!ok)) break;
-    if (tid == 0 && it + g.stages < cur.n_it) load(it + g.stages);
-    float* ybuf = ybuf_ptr(it & 1);
-    if (row_valid) {
-      float yout[L];
-      conv_row<L, K, PAD>(xin, taps, yout);
-      row_store<L, LOADER>(ybuf + static_cast<size_t>(tid) * g.pitch, yout);
+  if (tid >= nc) {  // ---------------- producer warp ----------------
+    if (tid != nc) return;
+    if constexpr (LOADER == LOAD_TMA3D) {
+      prefetch_tmap(&tm_in);
+      prefetch_tmap(&tm_out);
     }
-    fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {
+    auto load = [&](int t) {
+      const int s = t % S;
+      const int q = cur.q(t);
+      const uint32_t bar = smem_u32(&bars.full[s]);
+      mbar_arrive_expect_tx(bar, tile_tx_bytes<LOADER>(g, cur.hb, q));
+      issue_tile_load<LOADER>(g, &tm_in, in, cur.hb, q, smem_u32(stage_ptr(s)), bar);
+    };
+    int issued = 0;
+    for (; issued < min(S, cur.n_it); ++issued) load(issued);
+    for (int it = 0; it < cur.n_it; ++it) {
+      // Refill stage it%S with tile it+S as soon as the consumers hold tile it in registers.
+      if (it + S < cur.n_it) {
+        if (!mbar_wait_bounded(smem_u32(&bars.empty[it % S]), static_cast<uint32_t>(it / S) & 1u, err,
+                               DEVERR_TIMEOUT_FULL))
+          break;
+        load(it + S);
+        ++issued;
+      }
+      // Store tile it once every consumer row is written.
+      if (!mbar_wait_bounded(smem_u32(bars.yfull), static_cast<uint32_t>(it) & 1u, err, DEVERR_TIMEOUT_FULL))
+        break;
+      const int q = cur.q(it);
       if constexpr (LOADER == LOAD_TMA3D) {
         tma_store_3d(&tm_out, smem_u32(ybuf), 0, cur.hb * g.Th, q * g.Tb);
       } else {
@@ -404,34 +442,54 @@ __global__ void __launch_bounds__(256, 1)
         bulk_store_1d(out + row0 * g.L, smem_u32(ybuf), static_cast<uint32_t>(nrows) * g.L * 4u);
       }
       bulk_commit();
-      // The store of tile it-1 has read its buffer before anyone writes it again
-      // (next iteration, after the first barrier, which thread 0 reaches after this).
-      bulk_wait_read<1>();
+      bulk_wait_read<0>();
+      mbar_arrive(smem_u32(bars.yempty));
     }
+    producer_drain(bars, S, issued, err);
+    return;
   }
 
-  if (tid == 0) {
-    bulk_wait_all();
-    if (it < cur.n_it) {
-      // Aborted: let every load this CTA issued land before shared memory goes away.
-      const int issued_end = min(cur.n_it, it + g.stages);
-      for (int k2 = it + 1; k2 < issued_end; ++k2) {
-        const int s = k2 % g.stages;
-        const uint32_t parity = static_cast<uint32_t>(k2 / g.stages) & 1u;
-        if (!mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_DRAIN)) break;
-      }
-    }
+  // ---------------- consumer threads: one row each ----------------
+  const int T = g.Th * g.Tb;
+  const int h_local = tid % g.Th;
+  const int b_local = tid / g.Th;
+  const int h = cur.hb * g.Th + h_local;
+  const bool thread_has_row = (tid < T) && (h < g.H);
+  float taps[K];  // this thread's taps for the whole kernel (reversed for DX)
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const int src = (OP == OP_FWD) ? j : (K - 1 - j);
+    taps[j] = thread_has_row ? __ldg(taps_hk + static_cast<long long>(h) * K + src) : 0.0f;
+  }
+  float* yrow = ybuf + static_cast<size_t>(tid) * g.pitch;
+  for (int it = 0; it < cur.n_it; ++it) {
+    const int s = it % S;
+    if (!mbar_wait_bounded(smem_u32(&bars.full[s]), static_cast<uint32_t>(it / S) & 1u, err,
+                           DEVERR_TIMEOUT_FULL))
+      return;
+    const bool row_valid = thread_has_row && (cur.q(it) * g.Tb + b_local < g.B);
+    float xin[L];
+    if (row_valid) row_load<L, LOADER>(stage_ptr(s) + static_cast<size_t>(tid) * g.pitch, xin);
+    mbar_arrive(smem_u32(&bars.empty[s]));
+    float yout[L];
+    if (row_valid) conv_row<L, K, PAD>(xin, taps, yout);
+    if (it > 0 && !mbar_wait_bounded(smem_u32(bars.yempty), static_cast<uint32_t>(it - 1) & 1u, err,
+                                     DEVERR_TIMEOUT_FULL))
+      return;
+    if (row_valid) row_store<L, LOADER>(yrow, yout);
+    fence_proxy_async_smem();
+    mbar_arrive(smem_u32(bars.yfull));
   }
 }
 
 // ---------------------------------------------------------------------------
-// DK pass 1: persistent, TMA-pipelined (stages released once read into
-// registers); per-thread accumulators over all tiles,
-// then an in-CTA reduction over the Tb batch slots of each channel (fixed
-// order) and either one float atomic per (CTA,h,j) or one partial per (CTA,j,h).
+// DK pass 1.  Shared memory: (dy, x) ring [stages] | mbarriers.  Per-thread
+// accumulators run over all tiles; then an in-CTA reduction over the Tb batch
+// slots of each channel (fixed order) and either one float atomic per
+// (CTA, h, j) or one partial per (CTA, j, h).
 // ---------------------------------------------------------------------------
 template <int L, int K, int LOADER>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(288, 1)
     dk_rows_kernel(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_x,
                    const float* __restrict__ dy, const float* __restrict__ x,
                    float* __restrict__ dst, const TileGeom g, const int atomic_mode,
@@ -440,88 +498,88 @@ __global__ void __launch_bounds__(256, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   const int tid = static_cast<int>(threadIdx.x);
+  const int nc = static_cast<int>(blockDim.x) - 32;
   const TileCursor cur(g);
+  const int S = g.stages;
+  auto buf = [&](int s, int which) -> float* {
+    return reinterpret_cast<float*>(smem + static_cast<size_t>(2 * s + which) * g.stage_bytes);
+  };
+  const PipeBars bars = carve_bars(smem + static_cast<size_t>(2 * S) * g.stage_bytes, S);
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&bars.full[s]), 1);
+      mbar_init(smem_u32(&bars.empty[s]), static_cast<uint32_t>(nc));
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (tid >= nc) {  // ---------------- producer warp ----------------
+    if (tid != nc) return;
+    if constexpr (LOADER == LOAD_TMA3D) {
+      prefetch_tmap(&tm_dy);
+      prefetch_tmap(&tm_x);
+    }
+    auto load = [&](int t) {
+      const int s = t % S;
+      const int q = cur.q(t);
+      const uint32_t bar = smem_u32(&bars.full[s]);
+      mbar_arrive_expect_tx(bar, 2u * tile_tx_bytes<LOADER>(g, cur.hb, q));
+      issue_tile_load<LOADER>(g, &tm_dy, dy, cur.hb, q, smem_u32(buf(s, 0)), bar);
+      issue_tile_load<LOADER>(g, &tm_x, x, cur.hb, q, smem_u32(buf(s, 1)), bar);
+    };
+    int issued = 0;
+    for (; issued < min(S, cur.n_it); ++issued) load(issued);
+    for (int it = 0; it + S < cur.n_it; ++it) {
+      if (!mbar_wait_bounded(smem_u32(&bars.empty[it % S]), static_cast<uint32_t>(it / S) & 1u, err,
+                             DEVERR_TIMEOUT_FULL))
+        break;
+      load(it + S);
+      ++issued;
+    }
+    producer_drain(bars, S, issued, err);
+    return;
+  }
+
+  // ---------------- consumer threads: one row each ----------------
   const int T = g.Th * g.Tb;
   const int h_local = tid % g.Th;
   const int b_local = tid / g.Th;
   const int h = cur.hb * g.Th + h_local;
   const bool thread_has_row = (tid < T) && (h < g.H);
-
-  // Stage s: dy buffer at 2*s, x buffer at 2*s+1.
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(2 * g.stages) * g.stage_bytes);
-  if (tid == 0) {
-    if constexpr (LOADER == LOAD_TMA3D) {
-      prefetch_tmap(&tm_dy);
-      prefetch_tmap(&tm_x);
-    }
-    for (int s = 0; s < g.stages; ++s) mbar_init(smem_u32(&bars[s]), 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-
-  auto buf = [&](int s, int which) -> float* {
-    return reinterpret_cast<float*>(smem + static_cast<size_t>(2 * s + which) * g.stage_bytes);
-  };
-  auto load = [&](int it) {
-    const int s = it % g.stages;
-    const int q = cur.q(it);
-    const uint32_t bar = smem_u32(&bars[s]);
-    mbar_arrive_expect_tx(bar, 2u * tile_tx_bytes<LOADER>(g, cur.hb, q));
-    issue_tile_load<LOADER>(g, &tm_dy, dy, cur.hb, q, smem_u32(buf(s, 0)), bar);
-    issue_tile_load<LOADER>(g, &tm_x, x, cur.hb, q, smem_u32(buf(s, 1)), bar);
-  };
-
-  if (tid == 0) {
-    const int pro = min(g.stages, cur.n_it);
-    for (int it = 0; it < pro; ++it) load(it);
-  }
-
   float acc[K];
 #pragma unroll
   for (int j = 0; j < K; ++j) acc[j] = 0.0f;
-
-  int it = 0;
-  for (; it < cur.n_it; ++it) {
-    const int s = it % g.stages;
-    const uint32_t parity = static_cast<uint32_t>(it / g.stages) & 1u;
-    const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_FULL);
-    const int q = cur.q(it);
-    const bool row_valid = thread_has_row && (q * g.Tb + b_local < g.B);
+  bool failed = false;
+  for (int it = 0; it < cur.n_it; ++it) {
+    const int s = it % S;
+    if (!mbar_wait_bounded(smem_u32(&bars.full[s]), static_cast<uint32_t>(it / S) & 1u, err,
+                           DEVERR_TIMEOUT_FULL)) {
+      failed = true;
+      break;
+    }
+    const bool row_valid = thread_has_row && (cur.q(it) * g.Tb + b_local < g.B);
     float gyr[L];
     float xr[L];
-    if (ok && row_valid) {
+    if (row_valid) {
       row_load<L, LOADER>(buf(s, 0) + static_cast<size_t>(tid) * g.pitch, gyr);
       row_load<L, LOADER>(buf(s, 1) + static_cast<size_t>(tid) * g.pitch, xr);
     }
-    // Every row of stage s is in registers: refill it before the FFMA nest.
-    if (__syncthreads_or(!ok)) break;
-    if (tid == 0 && it + g.stages < cur.n_it) load(it + g.stages);
+    mbar_arrive(smem_u32(&bars.empty[s]));
     if (row_valid) xcorr_row<L, K, PAD>(gyr, xr, acc);
   }
+  // All consumers agree before the epilogue reuses the ring (barrier 1 excludes the producer).
+  if (named_barrier_or(1, nc, failed)) return;
 
-  if (it < cur.n_it) {
-    if (tid == 0) {
-      const int issued_end = min(cur.n_it, it + g.stages);
-      for (int k2 = it + 1; k2 < issued_end; ++k2) {
-        const int s = k2 % g.stages;
-        const uint32_t parity = static_cast<uint32_t>(k2 / g.stages) & 1u;
-        if (!mbar_wait_bounded(smem_u32(&bars[s]), parity, err, DEVERR_TIMEOUT_DRAIN)) break;
-      }
-    }
-    return;
-  }
-
-  // In-CTA reduction over batch slots (the stage ring is idle now).
-  float* red = reinterpret_cast<float*>(smem);  // [K][T]
-  __syncthreads();
+  float* red = reinterpret_cast<float*>(smem);  // [K][T]; every load was consumed
   if (tid < T) {
 #pragma unroll
     for (int j = 0; j < K; ++j) red[j * T + tid] = acc[j];
   }
-  __syncthreads();
+  named_barrier(1, nc);
   const int nh = min(g.Th, g.H - cur.hb * g.Th);
-  for (int idx = tid; idx < K * nh; idx += static_cast<int>(blockDim.x)) {
+  for (int idx = tid; idx < K * nh; idx += nc) {
     const int j = idx / nh;
     const int hl = idx - j * nh;
     float sum = 0.0f;
