@@ -36,9 +36,12 @@ namespace pt {
 enum Op { OP_FWD = 0, OP_DX = 1, OP_DK = 2 };
 enum Loader { LOAD_TMA3D = 0, LOAD_BULK1D = 1 };
 
-// Device error bits (written with atomicOr into the error word).
-constexpr unsigned DEVERR_TIMEOUT_FULL = 1u;   // a tile never arrived
-constexpr unsigned DEVERR_TIMEOUT_DRAIN = 2u;  // an in-flight copy did not drain
+// Device error bits (written with atomicOr into the error word), one per wait site.
+constexpr unsigned DEVERR_TIMEOUT_FULL = 1u;    // consumer: a tile never arrived
+constexpr unsigned DEVERR_TIMEOUT_DRAIN = 2u;   // producer: an in-flight copy did not drain
+constexpr unsigned DEVERR_TIMEOUT_EMPTY = 4u;   // producer: a stage was never released
+constexpr unsigned DEVERR_TIMEOUT_YFULL = 8u;   // producer: an output tile was never completed
+constexpr unsigned DEVERR_TIMEOUT_YEMPTY = 16u; // consumer: the output buffer was never freed
 // Wait limit: far above any legitimate tile latency (microseconds).
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
 
@@ -99,7 +102,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+    if (static_cast<long long>(globaltimer_ns() - t0) > static_cast<long long>(WAIT_LIMIT_NS)) {
       atomicOr(err, errbit);
       return false;
     }
@@ -338,7 +341,8 @@ __device__ __forceinline__ uint32_t tile_tx_bytes(const TileGeom& g, int hb, int
 // per tile row, rounded up to whole warps) plus one producer warp whose lane 0
 // drives TMA.  Stages are handed over with mbarriers only:
 //   full[s]  : producer arrive.expect_tx + TMA bytes  -> consumers may read
-//   empty[s] : every consumer thread, once its row is in registers
+//   empty[s] : every consumer thread, once its row is in registers and a
+//              fence.proxy.async has ordered those reads before the refill
 //              -> the producer refills stage s (so the whole ring is in flight
 //                 while the FFMA nests run)
 //   FWD/DX also stage the output tile in one buffer:
@@ -424,13 +428,13 @@ __global__ void __launch_bounds__(288, 1)
       // Refill stage it%S with tile it+S as soon as the consumers hold tile it in registers.
       if (it + S < cur.n_it) {
         if (!mbar_wait_bounded(smem_u32(&bars.empty[it % S]), static_cast<uint32_t>(it / S) & 1u, err,
-                               DEVERR_TIMEOUT_FULL))
+                               DEVERR_TIMEOUT_EMPTY))
           break;
         load(it + S);
         ++issued;
       }
       // Store tile it once every consumer row is written.
-      if (!mbar_wait_bounded(smem_u32(bars.yfull), static_cast<uint32_t>(it) & 1u, err, DEVERR_TIMEOUT_FULL))
+      if (!mbar_wait_bounded(smem_u32(bars.yfull), static_cast<uint32_t>(it) & 1u, err, DEVERR_TIMEOUT_YFULL))
         break;
       const int q = cur.q(it);
       if constexpr (LOADER == LOAD_TMA3D) {
@@ -470,11 +474,15 @@ __global__ void __launch_bounds__(288, 1)
     const bool row_valid = thread_has_row && (cur.q(it) * g.Tb + b_local < g.B);
     float xin[L];
     if (row_valid) row_load<L, LOADER>(stage_ptr(s) + static_cast<size_t>(tid) * g.pitch, xin);
+    // The refill is an async-proxy write: order this thread's generic-proxy
+    // reads of the stage before it (without the fence the TMA load can land
+    // before the reads are performed; measured on B200).
+    fence_proxy_async_smem();
     mbar_arrive(smem_u32(&bars.empty[s]));
     float yout[L];
     if (row_valid) conv_row<L, K, PAD>(xin, taps, yout);
     if (it > 0 && !mbar_wait_bounded(smem_u32(bars.yempty), static_cast<uint32_t>(it - 1) & 1u, err,
-                                     DEVERR_TIMEOUT_FULL))
+                                     DEVERR_TIMEOUT_YEMPTY))
       return;
     if (row_valid) row_store<L, LOADER>(yrow, yout);
     fence_proxy_async_smem();
@@ -533,7 +541,7 @@ __global__ void __launch_bounds__(288, 1)
     for (; issued < min(S, cur.n_it); ++issued) load(issued);
     for (int it = 0; it + S < cur.n_it; ++it) {
       if (!mbar_wait_bounded(smem_u32(&bars.empty[it % S]), static_cast<uint32_t>(it / S) & 1u, err,
-                             DEVERR_TIMEOUT_FULL))
+                             DEVERR_TIMEOUT_EMPTY))
         break;
       load(it + S);
       ++issued;
@@ -566,6 +574,7 @@ __global__ void __launch_bounds__(288, 1)
       row_load<L, LOADER>(buf(s, 0) + static_cast<size_t>(tid) * g.pitch, gyr);
       row_load<L, LOADER>(buf(s, 1) + static_cast<size_t>(tid) * g.pitch, xr);
     }
+    fence_proxy_async_smem();  // reads of the stage precede its async-proxy refill
     mbar_arrive(smem_u32(&bars.empty[s]));
     if (row_valid) xcorr_row<L, K, PAD>(gyr, xr, acc);
   }

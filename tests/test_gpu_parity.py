@@ -34,6 +34,7 @@ def run_path(x, k, dy, mode="deterministic"):
     gk = torch.zeros_like(k) if mode == "atomic" else torch.full_like(k, float("nan"))
     ops.dk(dy, x, gk, mode=mode)
     torch.cuda.synchronize()
+    assert ops.device_error(clear=True) == 0, "a kernel wait expired"
     return y, gx, gk
 
 
