@@ -44,6 +44,7 @@ extern "C" {
 #define PT_ERR_WORKSPACE (-5)   /* deterministic dK workspace missing or too small */
 #define PT_ERR_CUDA (-6)        /* a CUDA runtime/driver call or launch failed */
 #define PT_ERR_DEVICE (-7)      /* current device is not compute capability 10.x */
+#define PT_ERR_SCRATCH_LIMIT (-8) /* pt_dk_noalloc: shape needs more than its fixed scratch */
 
 #define PT_MAX_L 48
 #define PT_MAX_K 48
@@ -86,6 +87,26 @@ PT_API int pt_dx(const float* dy, const float* k, float* dx, int B, int H, int L
  */
 PT_API int pt_dk(const float* dy, const float* x, float* dk, int B, int H, int L, int K,
           int mode, void* ws, size_t ws_bytes, void* stream);
+
+/*
+ * Deterministic weight gradient that allocates nothing; it has no counterpart
+ * in the reference.  For callers that may not allocate device memory (a
+ * runtime that owns a fixed memory budget and every allocation in it, or a
+ * steady-state loop where cudaMalloc/cudaFree would block on the device): the
+ * per-CTA partial sums go to a fixed scratch array inside the library
+ * (PT_DK_NOALLOC_SCRATCH_BYTES = 8 MiB of device memory, held by every GPU
+ * that loads the library until the process exits) instead of a caller
+ * workspace.  dk = dK, or dk += dK when `accumulate` is non-zero; results are
+ * identical to pt_dk in PT_DK_DETERMINISTIC mode.  Returns
+ * PT_ERR_SCRATCH_LIMIT when pt_dk_workspace_bytes(B,H,L,K) exceeds the
+ * scratch size (the primary B=16384,H=128,L=K=48 shape needs 7.3 MB).  The
+ * first call on each device resolves the array's device address and must be
+ * made before any stream capture; calls that overlap on the GPU share the one
+ * array and race, so the caller serialises them.
+ */
+#define PT_DK_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+PT_API int pt_dk_noalloc(const float* dy, const float* x, float* dk, int B, int H, int L, int K,
+                         int accumulate, void* stream);
 
 /*
  * Bytes of deterministic-dK workspace for this shape under the active launch

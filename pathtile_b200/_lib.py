@@ -20,6 +20,8 @@ PT_ERR_ALIGN = -4
 PT_ERR_WORKSPACE = -5
 PT_ERR_CUDA = -6
 PT_ERR_DEVICE = -7
+PT_ERR_SCRATCH_LIMIT = -8
+PT_DK_NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
 
 PT_DK_ATOMIC = 0
 PT_DK_DETERMINISTIC = 1
@@ -39,6 +41,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_dx": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _vp]),
     "pt_dk": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
     "pt_dk_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
+    "pt_dk_noalloc": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "pt_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int]),
     "pt_set_config": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
     "pt_kernel_info": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int]),

@@ -491,6 +491,8 @@ const char* pt_status_string(int status) {
     case PT_ERR_WORKSPACE: return "deterministic dK workspace missing or smaller than pt_dk_workspace_bytes()";
     case PT_ERR_CUDA: return "CUDA call or kernel launch failed (see pt_last_cuda_error)";
     case PT_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    case PT_ERR_SCRATCH_LIMIT:
+      return "shape needs more dK scratch than pt_dk_noalloc's fixed 8 MiB array; use pt_dk with a workspace";
     default: return "unknown status";
   }
 }
