@@ -166,11 +166,11 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
   const int T = g.Th * g.Tb;
   const long long tile_bytes = static_cast<long long>(g.pitch) * T * 4;
   long long stage = (tile_bytes + 1023) / 1024 * 1024;
-  // Buffers: DK = (dy, x) per stage; FWD/DX = input ring + 1 output buffer.
-  auto n_buf = [&](int stages) { return (path == PT_PATH_DK) ? 2 * stages : stages + 1; };
+  // Buffers: DK = (dy, x) per stage; FWD/DX = one in-place buffer per stage.
+  auto n_buf = [&](int stages) { return (path == PT_PATH_DK) ? 2 * stages : stages; };
   // Fewer stages when the buffers would not fit the per-block shared memory.
   while (g.stages > 2 &&
-         static_cast<long long>(n_buf(g.stages)) * stage + (2LL * g.stages + 2) * 8 + 1024 > di.max_smem)
+         static_cast<long long>(n_buf(g.stages)) * stage + (2LL * g.stages) * 8 + 1024 > di.max_smem)
     --g.stages;
   if (path == PT_PATH_DK) {
     // The idle ring doubles as the [K][T] in-CTA reduction buffer at the end.
@@ -178,7 +178,7 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
     if (n_buf(g.stages) * stage < red)
       stage = ((red + n_buf(g.stages) - 1) / n_buf(g.stages) + 1023) / 1024 * 1024;
   }
-  const long long bar_bytes = (2LL * g.stages + 2) * 8;  // full/empty per stage + yfull/yempty
+  const long long bar_bytes = 2LL * g.stages * 8;  // full + done per stage
   if (static_cast<long long>(n_buf(g.stages)) * stage + bar_bytes + 1024 > di.max_smem)
     return PT_ERR_UNSUPPORTED;
   g.stage_bytes = static_cast<unsigned>(stage);

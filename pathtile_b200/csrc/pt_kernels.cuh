@@ -340,28 +340,24 @@ __device__ __forceinline__ uint32_t tile_tx_bytes(const TileGeom& g, int hb, int
 // Warp-specialised persistent kernels.  The CTA is `nc` consumer threads (one
 // per tile row, rounded up to whole warps) plus one producer warp whose lane 0
 // drives TMA.  Stages are handed over with mbarriers only:
-//   full[s]  : producer arrive.expect_tx + TMA bytes  -> consumers may read
-//   empty[s] : every consumer thread, once its row is in registers and a
-//              fence.proxy.async has ordered those reads before the refill
-//              -> the producer refills stage s (so the whole ring is in flight
-//                 while the FFMA nests run)
-//   FWD/DX also stage the output tile in one buffer:
-//   yfull    : every consumer thread after writing its output row -> TMA store
-//   yempty   : producer, once the previous store has read the buffer
-// Consumer warps never wait on each other.  Every wait is bounded; a thread
-// whose wait expires stops, the producer drains the loads it issued, and the
-// error word records it.
+//   full[s]  : producer arrive.expect_tx + TMA bytes -> consumers may read
+//   done[s]  : every consumer thread, after its FFMA nest has consumed the row
+//              (and, for FWD/DX, written its output row back in place), behind
+//              a fence.proxy.async that orders those generic-proxy accesses
+//              before the async-proxy store / refill of the stage
+// Consumer warps never wait on each other; releasing a stage only after the
+// nest means the fence finds nothing outstanding, and shared-memory loads
+// overlap the FFMAs.  Every wait is bounded; a thread whose wait expires
+// stops, the producer drains the loads it issued, and the error word records it.
 // ---------------------------------------------------------------------------
 struct PipeBars {
   uint64_t* full;
-  uint64_t* empty;
-  uint64_t* yfull;
-  uint64_t* yempty;
+  uint64_t* done;
 };
 
 __device__ __forceinline__ PipeBars carve_bars(unsigned char* base, int stages) {
   uint64_t* b = reinterpret_cast<uint64_t*>(base);
-  return PipeBars{b, b + stages, b + 2 * stages, b + 2 * stages + 1};
+  return PipeBars{b, b + stages};
 }
 
 // Producer tail: every stage's most recently issued load has landed (bounded),
@@ -376,7 +372,9 @@ __device__ __forceinline__ void producer_drain(const PipeBars& bars, int stages,
 }
 
 // ---------------------------------------------------------------------------
-// FWD / DX.  Shared memory: input ring [stages] | output buffer | mbarriers.
+// FWD / DX.  Shared memory: tile ring [stages] | mbarriers.  Each consumer
+// thread overwrites its input row with its output row; the producer stores the
+// tile from the same stage, waits until the store has read it, then refills it.
 // ---------------------------------------------------------------------------
 template <int L, int K, int OP, int LOADER>
 __global__ void __launch_bounds__(288, 1)
@@ -395,16 +393,13 @@ __global__ void __launch_bounds__(288, 1)
   auto stage_ptr = [&](int s) -> float* {
     return reinterpret_cast<float*>(smem + static_cast<size_t>(s) * g.stage_bytes);
   };
-  float* ybuf = stage_ptr(S);
-  const PipeBars bars = carve_bars(smem + static_cast<size_t>(S + 1) * g.stage_bytes, S);
+  const PipeBars bars = carve_bars(smem + static_cast<size_t>(S) * g.stage_bytes, S);
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&bars.full[s]), 1);
-      mbar_init(smem_u32(&bars.empty[s]), static_cast<uint32_t>(nc));
+      mbar_init(smem_u32(&bars.done[s]), static_cast<uint32_t>(nc));
     }
-    mbar_init(smem_u32(bars.yfull), static_cast<uint32_t>(nc));
-    mbar_init(smem_u32(bars.yempty), 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -425,29 +420,26 @@ __global__ void __launch_bounds__(288, 1)
     int issued = 0;
     for (; issued < min(S, cur.n_it); ++issued) load(issued);
     for (int it = 0; it < cur.n_it; ++it) {
-      // Refill stage it%S with tile it+S as soon as the consumers hold tile it in registers.
-      if (it + S < cur.n_it) {
-        if (!mbar_wait_bounded(smem_u32(&bars.empty[it % S]), static_cast<uint32_t>(it / S) & 1u, err,
-                               DEVERR_TIMEOUT_EMPTY))
-          break;
-        load(it + S);
-        ++issued;
-      }
-      // Store tile it once every consumer row is written.
-      if (!mbar_wait_bounded(smem_u32(bars.yfull), static_cast<uint32_t>(it) & 1u, err, DEVERR_TIMEOUT_YFULL))
+      const int s = it % S;
+      // Every row of tile it has been written back: store it.
+      if (!mbar_wait_bounded(smem_u32(&bars.done[s]), static_cast<uint32_t>(it / S) & 1u, err,
+                             DEVERR_TIMEOUT_YFULL))
         break;
       const int q = cur.q(it);
       if constexpr (LOADER == LOAD_TMA3D) {
-        tma_store_3d(&tm_out, smem_u32(ybuf), 0, cur.hb * g.Th, q * g.Tb);
+        tma_store_3d(&tm_out, smem_u32(stage_ptr(s)), 0, cur.hb * g.Th, q * g.Tb);
       } else {
         long long row0;
         int nrows;
         tile_rows(g, cur.hb, q, row0, nrows);
-        bulk_store_1d(out + row0 * g.L, smem_u32(ybuf), static_cast<uint32_t>(nrows) * g.L * 4u);
+        bulk_store_1d(out + row0 * g.L, smem_u32(stage_ptr(s)), static_cast<uint32_t>(nrows) * g.L * 4u);
       }
       bulk_commit();
-      bulk_wait_read<0>();
-      mbar_arrive(smem_u32(bars.yempty));
+      if (it + S < cur.n_it) {
+        bulk_wait_read<0>();  // the store has read stage s: refill it
+        load(it + S);
+        ++issued;
+      }
     }
     producer_drain(bars, S, issued, err);
     return;
@@ -465,33 +457,27 @@ __global__ void __launch_bounds__(288, 1)
     const int src = (OP == OP_FWD) ? j : (K - 1 - j);
     taps[j] = thread_has_row ? __ldg(taps_hk + static_cast<long long>(h) * K + src) : 0.0f;
   }
-  float* yrow = ybuf + static_cast<size_t>(tid) * g.pitch;
   for (int it = 0; it < cur.n_it; ++it) {
     const int s = it % S;
     if (!mbar_wait_bounded(smem_u32(&bars.full[s]), static_cast<uint32_t>(it / S) & 1u, err,
                            DEVERR_TIMEOUT_FULL))
       return;
-    const bool row_valid = thread_has_row && (cur.q(it) * g.Tb + b_local < g.B);
-    float xin[L];
-    if (row_valid) row_load<L, LOADER>(stage_ptr(s) + static_cast<size_t>(tid) * g.pitch, xin);
-    // The refill is an async-proxy write: order this thread's generic-proxy
-    // reads of the stage before it (without the fence the TMA load can land
-    // before the reads are performed; measured on B200).
+    if (thread_has_row && cur.q(it) * g.Tb + b_local < g.B) {
+      float* rowp = stage_ptr(s) + static_cast<size_t>(tid) * g.pitch;
+      float xin[L];
+      float yout[L];
+      row_load<L, LOADER>(rowp, xin);
+      conv_row<L, K, PAD>(xin, taps, yout);
+      row_store<L, LOADER>(rowp, yout);
+    }
     fence_proxy_async_smem();
-    mbar_arrive(smem_u32(&bars.empty[s]));
-    float yout[L];
-    if (row_valid) conv_row<L, K, PAD>(xin, taps, yout);
-    if (it > 0 && !mbar_wait_bounded(smem_u32(bars.yempty), static_cast<uint32_t>(it - 1) & 1u, err,
-                                     DEVERR_TIMEOUT_YEMPTY))
-      return;
-    if (row_valid) row_store<L, LOADER>(yrow, yout);
-    fence_proxy_async_smem();
-    mbar_arrive(smem_u32(bars.yfull));
+    mbar_arrive(smem_u32(&bars.done[s]));
   }
 }
 
 // ---------------------------------------------------------------------------
-// DK pass 1.  Shared memory: (dy, x) ring [stages] | mbarriers.  Per-thread
+// DK pass 1.  Shared memory: (dy, x) ring [stages] | mbarriers; a stage is
+// released (done[s]) once its rows went through the FFMA nest.  Per-thread
 // accumulators run over all tiles; then an in-CTA reduction over the Tb batch
 // slots of each channel (fixed order) and either one float atomic per
 // (CTA, h, j) or one partial per (CTA, j, h).
@@ -517,7 +503,7 @@ __global__ void __launch_bounds__(288, 1)
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&bars.full[s]), 1);
-      mbar_init(smem_u32(&bars.empty[s]), static_cast<uint32_t>(nc));
+      mbar_init(smem_u32(&bars.done[s]), static_cast<uint32_t>(nc));
     }
     fence_mbar_init();
   }
@@ -540,7 +526,7 @@ __global__ void __launch_bounds__(288, 1)
     int issued = 0;
     for (; issued < min(S, cur.n_it); ++issued) load(issued);
     for (int it = 0; it + S < cur.n_it; ++it) {
-      if (!mbar_wait_bounded(smem_u32(&bars.empty[it % S]), static_cast<uint32_t>(it / S) & 1u, err,
+      if (!mbar_wait_bounded(smem_u32(&bars.done[it % S]), static_cast<uint32_t>(it / S) & 1u, err,
                              DEVERR_TIMEOUT_EMPTY))
         break;
       load(it + S);
@@ -567,16 +553,15 @@ __global__ void __launch_bounds__(288, 1)
       failed = true;
       break;
     }
-    const bool row_valid = thread_has_row && (cur.q(it) * g.Tb + b_local < g.B);
-    float gyr[L];
-    float xr[L];
-    if (row_valid) {
+    if (thread_has_row && cur.q(it) * g.Tb + b_local < g.B) {
+      float gyr[L];
+      float xr[L];
       row_load<L, LOADER>(buf(s, 0) + static_cast<size_t>(tid) * g.pitch, gyr);
       row_load<L, LOADER>(buf(s, 1) + static_cast<size_t>(tid) * g.pitch, xr);
+      xcorr_row<L, K, PAD>(gyr, xr, acc);
     }
     fence_proxy_async_smem();  // reads of the stage precede its async-proxy refill
-    mbar_arrive(smem_u32(&bars.empty[s]));
-    if (row_valid) xcorr_row<L, K, PAD>(gyr, xr, acc);
+    mbar_arrive(smem_u32(&bars.done[s]));
   }
   // All consumers agree before the epilogue reuses the ring (barrier 1 excludes the producer).
   if (named_barrier_or(1, nc, failed)) return;
