@@ -150,7 +150,9 @@ PT_API int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n)
 
 /*
  * Device-side error word: kernels never spin without bound; a wait that runs
- * past its limit sets a bit here and the kernel returns early.  Reads (and
+ * past its limit (2 s) sets a bit here and the kernel returns early: bit 0 a
+ * consumer waited for a tile, bit 1 the producer waited for an in-flight copy
+ * to drain, bit 2 the producer waited for consumers to finish a stage.  Reads (and
  * with clear != 0, resets) the word of the current device; synchronises the
  * device.  The reference has no device-side error channel (its kernels return
  * silently on L > 48, kernels/warp_tiled_ampere.py:390).

@@ -18,12 +18,12 @@ struct LaunchCfg {
 
 // Index: PT_PATH_FWD, PT_PATH_DX, PT_PATH_DK.
 constexpr LaunchCfg kFrozenCfg[3] = {
-    {128, 3, 2},  // FWD
-    {128, 3, 2},  // DX
-    {128, 2, 2},  // DK
+    {128, 4, 2},  // FWD
+    {128, 4, 2},  // DX
+    {256, 3, 1},  // DK
 };
 
 // Provenance of the table above, reported by pt_config callers.
-constexpr const char* kFrozenCfgSource = "initial design point (before the B200 sweep)";
+constexpr const char* kFrozenCfgSource = "B200 sweep of preset pathtile-train (3 trials)";
 
 }  // namespace pt

@@ -37,11 +37,9 @@ enum Op { OP_FWD = 0, OP_DX = 1, OP_DK = 2 };
 enum Loader { LOAD_TMA3D = 0, LOAD_BULK1D = 1 };
 
 // Device error bits (written with atomicOr into the error word), one per wait site.
-constexpr unsigned DEVERR_TIMEOUT_FULL = 1u;    // consumer: a tile never arrived
-constexpr unsigned DEVERR_TIMEOUT_DRAIN = 2u;   // producer: an in-flight copy did not drain
-constexpr unsigned DEVERR_TIMEOUT_EMPTY = 4u;   // producer: a stage was never released
-constexpr unsigned DEVERR_TIMEOUT_YFULL = 8u;   // producer: an output tile was never completed
-constexpr unsigned DEVERR_TIMEOUT_YEMPTY = 16u; // consumer: the output buffer was never freed
+constexpr unsigned DEVERR_TIMEOUT_FULL = 1u;   // consumer: a tile never arrived
+constexpr unsigned DEVERR_TIMEOUT_DRAIN = 2u;  // producer: an in-flight copy did not drain
+constexpr unsigned DEVERR_TIMEOUT_DONE = 4u;   // producer: a stage's rows were never finished
 // Wait limit: far above any legitimate tile latency (microseconds).
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
 
@@ -423,7 +421,7 @@ __global__ void __launch_bounds__(288, 1)
       const int s = it % S;
       // Every row of tile it has been written back: store it.
       if (!mbar_wait_bounded(smem_u32(&bars.done[s]), static_cast<uint32_t>(it / S) & 1u, err,
-                             DEVERR_TIMEOUT_YFULL))
+                             DEVERR_TIMEOUT_DONE))
         break;
       const int q = cur.q(it);
       if constexpr (LOADER == LOAD_TMA3D) {
@@ -527,7 +525,7 @@ __global__ void __launch_bounds__(288, 1)
     for (; issued < min(S, cur.n_it); ++issued) load(issued);
     for (int it = 0; it + S < cur.n_it; ++it) {
       if (!mbar_wait_bounded(smem_u32(&bars.done[it % S]), static_cast<uint32_t>(it / S) & 1u, err,
-                             DEVERR_TIMEOUT_EMPTY))
+                             DEVERR_TIMEOUT_DONE))
         break;
       load(it + S);
       ++issued;

@@ -264,7 +264,13 @@ def _validate(case: ShapeCase, seed: int, device) -> dict[str, float]:
     return err
 
 
-def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: int, out: Path) -> None:
+def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: int, out: Path,
+              reps: int = 3) -> None:
+    """Time every candidate on every shape.  Within a shape the candidates are
+    visited round-robin `reps` times (each visit: warm-up, then `runs` timed
+    launches), and a candidate's figure is the median of its per-visit means, so
+    slow drifts of the SM clock (power capping) average out instead of
+    favouring whichever candidate ran first."""
     import torch
 
     from . import ops
@@ -279,6 +285,11 @@ def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: 
     stream = torch.cuda.current_stream()
     for case in order:
         sd = case_seed(seed, case)
+        valid: dict[tuple, dict[str, float]] = {}
+        for cand in cands:
+            for p in PATHS:
+                ops.set_config(p, *cand)
+            valid[cand] = _validate(case, sd, dev)
         x, k, dy = _make_inputs(case, sd, case.B, dev)
         y, gx, gk = torch.empty_like(x), torch.empty_like(x), torch.empty_like(k)
         launch = {
@@ -286,35 +297,58 @@ def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: 
             "bwd_input": lambda: ops.dx(dy, k, gx),
             "bwd_weight": lambda: ops.dk(dy, x, gk, mode="deterministic"),
         }
+        # Candidates whose clamped launch is identical (CTAs per SM limited by
+        # occupancy, stages by shared memory) are measured once: the first one
+        # of each effective launch is timed and the others alias it.
+        effective: dict[tuple, tuple] = {}
+        alias: dict[tuple, tuple] = {}
         for cand in cands:
             for p in PATHS:
                 ops.set_config(p, *cand)
-            err = _validate(case, sd, dev)
             for p in PATHS:
-                ok = err[p] <= (1e-5 if p != "bwd_weight" else 1e-4)
-                if not ok:
-                    summ.append({**asdict(case), "trial": trial, "phase": p, "rows": cand[0], "stages": cand[1],
-                                 "ctas_per_sm": cand[2], "valid": False, "max_norm_err": err[p]})
-                    continue
-                for _ in range(warmup):
-                    launch[p]()
-                times = []
-                for _ in range(runs):
-                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    s.record(stream)
-                    launch[p]()
-                    e.record(stream)
-                    times.append((s, e))
-                torch.cuda.synchronize()
-                ms = [s.elapsed_time(e) for s, e in times]
                 info = ops.kernel_info(p, case.B, case.H, case.L, case.K)
-                for i, v in enumerate(ms):
-                    raw_rows.append({"config_id": case.config_id, "trial": trial, "phase": p,
-                                     "candidate": candidate_id(cand), "run": i, "runtime_ms": v})
-                summ.append({**asdict(case), "trial": trial, "phase": p, "rows": cand[0], "stages": cand[1],
-                             "ctas_per_sm": cand[2], "valid": True, "max_norm_err": err[p],
-                             "mean_ms": statistics.mean(ms), "median_ms": statistics.median(ms),
-                             "std_ms": statistics.stdev(ms) if len(ms) > 1 else 0.0,
+                key = (p, cand[0], info["grid"], info["dynamic_smem_bytes"], info["threads_per_block"])
+                alias[(cand, p)] = effective.setdefault(key, cand)
+        visits: dict[tuple, list[float]] = {}
+        for rep in range(reps):
+            for cand in (cands if rep % 2 == 0 else list(reversed(cands))):
+                for p in PATHS:
+                    ops.set_config(p, *cand)
+                for p in PATHS:
+                    if alias[(cand, p)] != cand:
+                        continue
+                    if valid[cand][p] > (1e-5 if p != "bwd_weight" else 1e-4):
+                        continue
+                    for _ in range(warmup):
+                        launch[p]()
+                    ev = []
+                    for _ in range(runs):
+                        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        s.record(stream)
+                        launch[p]()
+                        e.record(stream)
+                        ev.append((s, e))
+                    torch.cuda.synchronize()
+                    ms = [s.elapsed_time(e) for s, e in ev]
+                    visits.setdefault((cand, p), []).append(statistics.mean(ms))
+                    for i, v in enumerate(ms):
+                        raw_rows.append({"config_id": case.config_id, "trial": trial, "rep": rep, "phase": p,
+                                         "candidate": candidate_id(cand), "run": i, "runtime_ms": v})
+        for cand in cands:
+            for p in PATHS:
+                for q in PATHS:
+                    ops.set_config(q, *cand)
+                base = {**asdict(case), "trial": trial, "phase": p, "rows": cand[0], "stages": cand[1],
+                        "ctas_per_sm": cand[2], "max_norm_err": valid[cand][p]}
+                src = alias[(cand, p)]
+                if (src, p) not in visits:
+                    summ.append({**base, "valid": False})
+                    continue
+                v = visits[(src, p)]
+                base["alias_of"] = candidate_id(src) if src != cand else ""
+                info = ops.kernel_info(p, case.B, case.H, case.L, case.K)
+                summ.append({**base, "valid": True, "mean_ms": statistics.median(v), "visits": len(v),
+                             "visit_spread_pct": 100.0 * (max(v) / min(v) - 1.0),
                              "grid": info["grid"], "resident_blocks_per_sm": info["resident_blocks_per_sm"]})
         del x, k, dy, y, gx, gk
         torch.cuda.empty_cache()
@@ -323,13 +357,16 @@ def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: 
     _write_csv(out / "raw.csv", raw_rows)
     _write_csv(out / "summary.csv", summ)
     (out / "metadata.json").write_text(json.dumps({
-        "trial": trial, "warmup": warmup, "runs": runs, "seed": seed, "device": torch.cuda.get_device_name(),
+        "trial": trial, "warmup": warmup, "runs": runs, "reps": reps, "seed": seed,
+        "device": torch.cuda.get_device_name(),
         "cases": [asdict(c) for c in cases], "candidates": [candidate_id(c) for c in candidates()],
         "created_unix": time.time(),
         "measurement_contract": {"strict_fp32": True, "cuda_event_kernel_timing": True,
                                  "validation_timed": False, "dk_mode": "deterministic",
-                                 "candidate_order": "listed on odd trials; reversed on even trials",
-                                 "shape_order": "listed on odd trials; reversed on even trials"}},
+                                 "candidate_order": "round-robin, direction alternating per visit; "
+                                                    "reversed on even trials",
+                                 "shape_order": "listed on odd trials; reversed on even trials",
+                                 "figure": "median over visits of the per-visit mean"}},
         indent=1))
 
 
@@ -368,15 +405,16 @@ def main() -> None:
     ap.add_argument("--preset", default="pathtile-train", choices=sorted(PRESETS))
     ap.add_argument("--out", type=Path, required=True, help="results directory of this preset")
     ap.add_argument("--trial", type=int, default=1)
-    ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--runs", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--runs", type=int, default=20)
+    ap.add_argument("--reps", type=int, default=3, help="round-robin visits per candidate and shape")
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--write-header", action="store_true", help="aggregate: rewrite pt_frozen_config.h")
     ap.add_argument("--policy", type=Path, help="regret: frozen_config.json to score")
     args = ap.parse_args()
     if args.mode == "run":
         run_sweep(cases_for_preset(args.preset), args.warmup, args.runs, args.trial, args.seed,
-                  args.out / f"trial{args.trial}")
+                  args.out / f"trial{args.trial}", reps=args.reps)
     elif args.mode == "aggregate":
         summary = aggregate_trials(args.out)
         policy = select_policy(summary)
