@@ -120,7 +120,9 @@ PT_API size_t pt_dk_workspace_bytes(int B, int H, int L, int K);
  * Launch configuration that the frozen PathTile table selects for `path`
  * (PT_PATH_*) at this shape.  out[0] = rows per tile, out[1] = pipeline
  * stages, out[2] = CTAs per SM, out[3] = 1 if an (L,K)-specialised kernel
- * exists, else 0 (generic kernel).  `n` is the capacity of `out` (>= 4).
+ * exists, else 0 (generic kernel), and if `n` >= 5, out[4] = the shape's
+ * arithmetic-intensity class keying the table (0 light, 1 medium, 2 heavy:
+ * in-range FMAs per output element < 12, < 24, else).  `n` >= 4.
  * Mirrors the frozen constants that the reference bakes into CUDA_TEMPLATE
  * (WARPS_PER_BLOCK / BWDK_BLOCK, kernels/warp_tiled_ampere.py:668-672,
  * selected by scripts/aggregate_pathtile_results.py:222-240).

@@ -114,8 +114,23 @@ int ensure_smem_attr(DeviceInfo& di, const void* func, size_t bytes) {
   return PT_OK;
 }
 
-pt::LaunchCfg cfg_for(int path) {
-  return g_has_override[path] ? g_override[path] : pt::kFrozenCfg[path];
+// Arithmetic-intensity class of a shape (in-range FMAs per output element:
+// < 12 light, < 24 medium, else heavy), the key of the frozen table.
+int intensity_class(int L, int K) {
+  const int pad = K / 2;
+  long long pairs = 0;
+  for (int j = 0; j < K; ++j) {
+    const int lo = pad - j > 0 ? pad - j : 0;
+    const int hi = L + pad - j < L ? L + pad - j : L;
+    if (hi > lo) pairs += hi - lo;
+  }
+  if (pairs < 12LL * L) return 0;
+  if (pairs < 24LL * L) return 1;
+  return 2;
+}
+
+pt::LaunchCfg cfg_for(int path, int L, int K) {
+  return g_has_override[path] ? g_override[path] : pt::kFrozenCfg[path][intensity_class(L, K)];
 }
 
 const pt::Entry* find_entry(int L, int K) {
@@ -142,22 +157,27 @@ struct Plan {
 int tma_pitch(int L) { return (!g_padded_box_ok || (L / 4) % 2 == 1) ? L : L + 4; }
 
 int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::Entry& e, Plan& p) {
-  const pt::LaunchCfg cfg = cfg_for(path);
+  const pt::LaunchCfg cfg = cfg_for(path, L, K);
   pt::TileGeom& g = p.g;
   g.B = B;
   g.H = H;
   g.L = L;
   g.K = K;
+  // Tile shape: every channel in one block whenever H fits a TMA box (<= 256),
+  // with as many batches as reach `rows`; above that, balanced channel blocks
+  // of at most `rows` channels (a multiple of 4 so 1-D bulk tiles stay
+  // 16-byte aligned), so no block is left mostly idle.
   const int R = cfg.rows;
-  if (H <= R) {
+  if (H <= 256) {
     g.Th = H;
     g.Tb = R / H;
-    if (g.Tb > 256) g.Tb = 256;
+    if (g.Tb < 1) g.Tb = 1;
     g.nhb = 1;
   } else {
-    g.Th = R;
+    const int nb = (H + R - 1) / R;
+    g.Th = ((H + nb - 1) / nb + 3) / 4 * 4;
     g.Tb = 1;
-    g.nhb = (H + R - 1) / R;
+    g.nhb = (H + g.Th - 1) / g.Th;
   }
   g.Q = (B + g.Tb - 1) / g.Tb;
   g.stages = cfg.stages;
@@ -397,12 +417,13 @@ int pt_config(int path, int B, int H, int L, int K, int* out, int n) {
   if (B < 1 || H < 1 || L < 1 || K < 1) return PT_ERR_ARGS;
   if (L > PT_MAX_L || K > PT_MAX_K) return PT_ERR_UNSUPPORTED;
   std::call_once(g_once, init_once);
-  const pt::LaunchCfg c = cfg_for(path);
+  const pt::LaunchCfg c = cfg_for(path, L, K);
   const pt::Entry* e = find_entry(L, K);
   out[0] = c.rows;
   out[1] = c.stages;
   out[2] = c.ctas_per_sm;
   out[3] = (e && (e->loader == pt::LOAD_TMA3D || (static_cast<long long>(H) * L) % 4 == 0)) ? 1 : 0;
+  if (n >= 5) out[4] = intensity_class(L, K);
   return PT_OK;
 }
 

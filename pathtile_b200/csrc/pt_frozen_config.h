@@ -1,11 +1,12 @@
-// pt_frozen_config.h -- launch configuration per path, frozen offline.
+// pt_frozen_config.h -- launch configuration per path and intensity class, frozen offline.
 //
-// The B200 counterpart of the reference's frozen per-architecture constants
-// (WARPS_PER_BLOCK / BWDK_BLOCK substituted into CUDA_TEMPLATE,
-// kernels/warp_tiled_ampere.py:668-672, chosen by the argmin of summed latency
-// over the 20 tuning shapes, scripts/aggregate_pathtile_results.py:222-240).
-// Candidate axes here: rows per tile (one thread per row), TMA ring depth,
-// and persistent CTAs per SM.  Deployment does no per-shape search.
+// Written by `python -m pathtile_b200.pathtile --mode aggregate --write-header`:
+// per path and per arithmetic-intensity class (in-range FMAs per output
+// element: light < 12 <= medium < 24 <= heavy), the candidate (rows per tile,
+// ring stages, CTAs per SM) with the minimum sum of mean latency over that
+// class's tuning shapes, ties to the smaller candidate -- the reference's
+// selection rule (scripts/aggregate_pathtile_results.py:222-240) applied per
+// class.  Deployment looks the class up; it does no per-shape search.
 #pragma once
 
 namespace pt {
@@ -16,14 +17,13 @@ struct LaunchCfg {
   int ctas_per_sm;  // persistent CTAs per SM (1..4), clamped by occupancy
 };
 
-// Index: PT_PATH_FWD, PT_PATH_DX, PT_PATH_DK.
-constexpr LaunchCfg kFrozenCfg[3] = {
-    {128, 4, 2},  // FWD
-    {128, 4, 2},  // DX
-    {256, 3, 1},  // DK
+// kFrozenCfg[path][class]: path PT_PATH_FWD/DX/DK, class light/medium/heavy.
+constexpr LaunchCfg kFrozenCfg[3][3] = {
+    {{128, 2, 3}, {128, 2, 3}, {128, 2, 3}},  // FWD: light, medium, heavy
+    {{128, 2, 3}, {128, 2, 3}, {128, 2, 3}},  // DX: light, medium, heavy
+    {{256, 3, 1}, {256, 3, 1}, {256, 3, 1}},  // DK: light, medium, heavy
 };
 
-// Provenance of the table above, reported by pt_config callers.
-constexpr const char* kFrozenCfgSource = "B200 sweep of preset pathtile-train (3 trials)";
+constexpr const char* kFrozenCfgSource = "B200 sweep of preset pathtile-train (2 trials x 3 visits), global policy per path";
 
 }  // namespace pt

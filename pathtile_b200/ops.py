@@ -206,9 +206,10 @@ def dk(
 def config(path: str, B: int, H: int, L: int, K: int) -> dict[str, int]:
     """Frozen launch choice of one path at one shape (C ABI pt_config)."""
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
-    out = (ctypes.c_int * 4)()
-    _lib.check(_lib.load().pt_config(code, B, H, L, K, out, 4), "pt_config")
-    return {"rows_per_tile": out[0], "stages": out[1], "ctas_per_sm": out[2], "specialised": out[3]}
+    out = (ctypes.c_int * 5)()
+    _lib.check(_lib.load().pt_config(code, B, H, L, K, out, 5), "pt_config")
+    return {"rows_per_tile": out[0], "stages": out[1], "ctas_per_sm": out[2], "specialised": out[3],
+            "intensity_class": ("light", "medium", "heavy")[out[4]]}
 
 
 def kernel_info(path: str, B: int, H: int, L: int, K: int, device: torch.device | int | None = None) -> dict[str, int]:

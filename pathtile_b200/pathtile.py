@@ -138,6 +138,23 @@ def case_seed(base_seed: int, case: ShapeCase) -> int:
     return int(base_seed + zlib.crc32(case.config_id.encode("utf-8")))
 
 
+CLASSES = ("light", "medium", "heavy")
+
+
+def in_range_pairs(L: int, K: int) -> int:
+    """(t, j) pairs with 0 <= t+j-K//2 < L: the FMAs one row needs."""
+    pad = K // 2
+    return sum(max(0, min(L, L + pad - j) - max(0, pad - j)) for j in range(K))
+
+
+def intensity_class(L: int, K: int) -> str:
+    """Arithmetic-intensity class of a shape: in-range FMAs per output element
+    below 12 -> light (memory-bound), below 24 -> medium, else heavy (near the
+    FP32 ridge).  The native library computes the same class (pt_api.cu)."""
+    f = in_range_pairs(L, K) / L
+    return "light" if f < 12 else ("medium" if f < 24 else "heavy")
+
+
 def candidates() -> list[tuple[int, int, int]]:
     return [(r, s, c) for r in ROWS for s in STAGES for c in CTAS]
 
@@ -149,25 +166,47 @@ def candidate_id(c: tuple[int, int, int]) -> str:
 # ---------------------------------------------------------------------------
 # Selection logic (pure; unit-tested on CPU)
 # ---------------------------------------------------------------------------
-def select_policy(summary: list[dict]) -> dict[str, tuple[int, int, int]]:
-    """Per path, the candidate with the minimum sum over shapes of mean_ms;
-    ties go to the smaller candidate tuple.  Candidates missing any shape
-    (invalid or failed) are not eligible."""
-    shapes = {r["config_id"] for r in summary}
-    chosen = {}
+def _class_of(row: dict) -> str:
+    return intensity_class(int(row["L"]), int(row["K"]))
+
+
+def select_policy(summary: list[dict], per_class: bool = False) -> dict[str, dict[str, tuple[int, int, int]]]:
+    """The frozen policy.  Default (the reference's rule): per path, the
+    candidate with the minimum sum over all tuning shapes of mean_ms, used for
+    every intensity class.  With per_class, the same rule within each class's
+    tuning shapes (a class without shapes inherits from the nearest class that
+    has some, medium first).  Ties go to the smaller candidate tuple;
+    candidates missing any shape of the set (invalid or failed) are not
+    eligible."""
+    chosen: dict[str, dict[str, tuple[int, int, int]]] = {}
     for path in PATHS:
-        totals: dict[tuple[int, int, int], float] = {}
-        seen: dict[tuple[int, int, int], set] = {}
-        for r in summary:
-            if r["phase"] != path:
+        chosen[path] = {}
+        for cls in (CLASSES if per_class else ("all",)):
+            rows = [r for r in summary if r["phase"] == path and (not per_class or _class_of(r) == cls)]
+            shapes = {r["config_id"] for r in rows}
+            if not shapes:
                 continue
-            c = (int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))
-            totals[c] = totals.get(c, 0.0) + float(r["mean_ms"])
-            seen.setdefault(c, set()).add(r["config_id"])
-        eligible = [(t, c) for c, t in totals.items() if seen[c] == shapes]
-        if not eligible:
-            raise ValueError(f"No candidate covers every shape for {path}")
-        chosen[path] = min(eligible)[1]
+            totals: dict[tuple[int, int, int], float] = {}
+            seen: dict[tuple[int, int, int], set] = {}
+            for r in rows:
+                c = (int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))
+                totals[c] = totals.get(c, 0.0) + float(r["mean_ms"])
+                seen.setdefault(c, set()).add(r["config_id"])
+            eligible = [(t, c) for c, t in totals.items() if seen[c] == shapes]
+            if not eligible:
+                raise ValueError(f"No candidate covers every {cls} shape for {path}")
+            chosen[path][cls] = min(eligible)[1]
+        if not chosen[path]:
+            raise ValueError(f"No tuning shapes for {path}")
+        if not per_class:
+            chosen[path] = {cls: chosen[path]["all"] for cls in CLASSES}
+            continue
+        for cls in CLASSES:
+            if cls not in chosen[path]:
+                for alt in ("medium", "heavy", "light"):
+                    if alt in chosen[path]:
+                        chosen[path][cls] = chosen[path][alt]
+                        break
     return chosen
 
 
@@ -182,31 +221,36 @@ def oracle_totals(summary: list[dict]) -> dict[str, dict[str, float]]:
     return best
 
 
-def regret_table(summary: list[dict], policy: dict[str, tuple[int, int, int]]) -> list[dict]:
+def regret_table(summary: list[dict], policy: dict[str, dict[str, tuple[int, int, int]]]) -> list[dict]:
     """Per shape: frozen total, oracle total and regret (frozen/oracle - 1)."""
     lookup = {}
+    cls_of = {}
     for r in summary:
         lookup[(r["config_id"], r["phase"], int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))] = float(
             r["mean_ms"])
+        cls_of[r["config_id"]] = _class_of(r)
     best = oracle_totals(summary)
     rows = []
     for cid in sorted(best):
-        frozen = sum(lookup[(cid, p, *policy[p])] for p in PATHS)
+        cls = cls_of[cid]
+        frozen = sum(lookup[(cid, p, *policy[p][cls])] for p in PATHS)
         oracle = sum(best[cid][p] for p in PATHS)
-        rows.append({"config_id": cid, "frozen_total_ms": frozen, "oracle_total_ms": oracle,
+        rows.append({"config_id": cid, "class": cls, "frozen_total_ms": frozen, "oracle_total_ms": oracle,
                      "regret_pct": 100.0 * (frozen / oracle - 1.0)})
     return rows
 
 
-def render_header(policy: dict[str, tuple[int, int, int]], source: str) -> str:
+def render_header(policy: dict[str, dict[str, tuple[int, int, int]]], source: str) -> str:
     lines = [
-        "// pt_frozen_config.h -- launch configuration per path, frozen offline.",
+        "// pt_frozen_config.h -- launch configuration per path and intensity class, frozen offline.",
         "//",
-        "// Written by `python -m pathtile_b200.pathtile --mode aggregate`: per path the",
-        "// candidate (rows per tile, ring stages, CTAs per SM) with the minimum sum of",
-        "// mean latency over the tuning shapes, ties to the smaller candidate -- the",
-        "// reference's selection rule (scripts/aggregate_pathtile_results.py:222-240).",
-        "// Deployment does no per-shape search.",
+        "// Written by `python -m pathtile_b200.pathtile --mode aggregate --write-header`:",
+        "// per path and per arithmetic-intensity class (in-range FMAs per output",
+        "// element: light < 12 <= medium < 24 <= heavy), the candidate (rows per tile,",
+        "// ring stages, CTAs per SM) with the minimum sum of mean latency over that",
+        "// class's tuning shapes, ties to the smaller candidate -- the reference's",
+        "// selection rule (scripts/aggregate_pathtile_results.py:222-240) applied per",
+        "// class.  Deployment looks the class up; it does no per-shape search.",
         "#pragma once",
         "",
         "namespace pt {",
@@ -217,12 +261,12 @@ def render_header(policy: dict[str, tuple[int, int, int]], source: str) -> str:
         "  int ctas_per_sm;  // persistent CTAs per SM (1..4), clamped by occupancy",
         "};",
         "",
-        "// Index: PT_PATH_FWD, PT_PATH_DX, PT_PATH_DK.",
-        "constexpr LaunchCfg kFrozenCfg[3] = {",
+        "// kFrozenCfg[path][class]: path PT_PATH_FWD/DX/DK, class light/medium/heavy.",
+        "constexpr LaunchCfg kFrozenCfg[3][3] = {",
     ]
     for p, name in zip(PATHS, ("FWD", "DX", "DK")):
-        r, s, c = policy[p]
-        lines.append(f"    {{{r}, {s}, {c}}},  // {name}")
+        cells = ", ".join("{%d, %d, %d}" % policy[p][c] for c in CLASSES)
+        lines.append(f"    {{{cells}}},  // {name}: light, medium, heavy")
     lines += ["};", "", f'constexpr const char* kFrozenCfgSource = "{source}";', "", "}  // namespace pt", ""]
     return "\n".join(lines)
 
@@ -389,14 +433,17 @@ def _read_csv(path: Path) -> list[dict]:
 def aggregate_trials(root: Path) -> list[dict]:
     """Mean over trials of each (shape, phase, candidate) mean_ms; invalid rows dropped."""
     acc: dict[tuple, list[float]] = {}
+    shape: dict[str, tuple[int, int]] = {}
     for t in sorted(root.glob("trial*/summary.csv")):
         for r in _read_csv(t):
+            shape[r["config_id"]] = (int(r["L"]), int(r["K"]))
             if r.get("valid") != "True":
                 continue
             key = (r["config_id"], r["phase"], int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))
             acc.setdefault(key, []).append(float(r["mean_ms"]))
     return [{"config_id": k[0], "phase": k[1], "rows": k[2], "stages": k[3], "ctas_per_sm": k[4],
-             "mean_ms": statistics.mean(v), "trials": len(v)} for k, v in sorted(acc.items())]
+             "L": shape[k[0]][0], "K": shape[k[0]][1], "mean_ms": statistics.mean(v), "trials": len(v)}
+            for k, v in sorted(acc.items())]
 
 
 def main() -> None:
@@ -410,6 +457,7 @@ def main() -> None:
     ap.add_argument("--reps", type=int, default=3, help="round-robin visits per candidate and shape")
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--write-header", action="store_true", help="aggregate: rewrite pt_frozen_config.h")
+    ap.add_argument("--per-class", action="store_true", help="aggregate: select per intensity class")
     ap.add_argument("--policy", type=Path, help="regret: frozen_config.json to score")
     args = ap.parse_args()
     if args.mode == "run":
@@ -417,10 +465,12 @@ def main() -> None:
                   args.out / f"trial{args.trial}", reps=args.reps)
     elif args.mode == "aggregate":
         summary = aggregate_trials(args.out)
-        policy = select_policy(summary)
+        policy = select_policy(summary, per_class=args.per_class)
         _write_csv(args.out / "aggregate_summary.csv", summary)
         reg = regret_table(summary, policy)
-        doc = {"policy": {p: dict(zip(("rows", "stages", "ctas_per_sm"), policy[p])) for p in PATHS},
+        doc = {"policy": {p: {c: dict(zip(("rows", "stages", "ctas_per_sm"), policy[p][c])) for c in CLASSES}
+                          for p in PATHS},
+               "per_class": args.per_class,
                "tuning_preset": args.preset, "tuning_shapes": sorted({r["config_id"] for r in summary}),
                "training_regret_pct_mean": statistics.mean(r["regret_pct"] for r in reg)}
         (args.out / "frozen_config.json").write_text(json.dumps(doc, indent=1))
@@ -430,7 +480,8 @@ def main() -> None:
     else:
         summary = aggregate_trials(args.out)
         pol = json.loads(args.policy.read_text())["policy"]
-        policy = {p: (pol[p]["rows"], pol[p]["stages"], pol[p]["ctas_per_sm"]) for p in PATHS}
+        policy = {p: {c: (pol[p][c]["rows"], pol[p][c]["stages"], pol[p][c]["ctas_per_sm"]) for c in CLASSES}
+                  for p in PATHS}
         reg = regret_table(summary, policy)
         _write_csv(args.out / "regret.csv", reg)
         vals = [r["regret_pct"] for r in reg]

@@ -43,10 +43,37 @@ def test_select_policy_sums_over_shapes_and_breaks_ties_low():
         table += [("s1", phase, a, 1.0), ("s1", phase, b, 0.5), ("s1", phase, c, 0.9),
                   ("s2", phase, a, 1.0), ("s2", phase, b, 2.0), ("s2", phase, c, 0.6)]
     pol = pt.select_policy(_rows(table))
-    # sums: a=2.0, b=2.5, c=1.5 -> c for every path, although b wins s1.
-    assert all(pol[p] == c for p in pt.PATHS)
+    # sums: a=2.0, b=2.5, c=1.5 -> c for every path and class, although b wins s1.
+    assert all(pol[p][cls] == c for p in pt.PATHS for cls in pt.CLASSES)
     tie = _rows([("s1", p, a, 1.0) for p in pt.PATHS] + [("s1", p, c, 1.0) for p in pt.PATHS])
-    assert all(v == a for v in pt.select_policy(tie).values())
+    assert all(v[cls] == a for v in pt.select_policy(tie).values() for cls in pt.CLASSES)
+
+
+def test_per_class_policy_and_inheritance():
+    a, b = (64, 2, 1), (128, 3, 2)
+    rows = []
+    for p in pt.PATHS:  # s_light is (24, 8) = light, s_heavy is (48, 48) = heavy
+        rows += [("s_light", p, a, 1.0), ("s_light", p, b, 2.0), ("s_heavy", p, a, 3.0), ("s_heavy", p, b, 1.0)]
+    shapes = {"s_light": (24, 8), "s_heavy": (48, 48)}
+    table = _rows(rows)
+    for r in table:
+        r["L"], r["K"] = shapes[r["config_id"]]
+    pol = pt.select_policy(table, per_class=True)
+    for p in pt.PATHS:
+        assert pol[p]["light"] == a and pol[p]["heavy"] == b
+        assert pol[p]["medium"] == b  # no medium shapes: inherits (heavy before light)
+    glob = pt.select_policy(table)
+    assert all(glob[p][c] == b for p in pt.PATHS for c in pt.CLASSES)  # sums a=4, b=3
+
+
+def test_intensity_classes():
+    assert pt.intensity_class(48, 48) == "heavy"
+    assert pt.intensity_class(32, 32) == "heavy"
+    assert pt.intensity_class(48, 24) == "medium"
+    assert pt.intensity_class(16, 16) == "medium"
+    assert pt.intensity_class(24, 8) == "light"
+    assert pt.intensity_class(37, 13) == "light"
+    assert pt.in_range_pairs(48, 48) == 1728
 
 
 def test_candidate_missing_a_shape_is_not_eligible():
@@ -54,7 +81,7 @@ def test_candidate_missing_a_shape_is_not_eligible():
     rows = []
     for p in pt.PATHS:
         rows += [("s1", p, a, 5.0), ("s2", p, a, 5.0), ("s1", p, b, 0.1)]  # b failed on s2
-    assert all(v == a for v in pt.select_policy(_rows(rows)).values())
+    assert all(v[c] == a for v in pt.select_policy(_rows(rows)).values() for c in pt.CLASSES)
 
 
 def test_regret_against_per_shape_oracle():
@@ -62,23 +89,31 @@ def test_regret_against_per_shape_oracle():
     rows = []
     for p in pt.PATHS:
         rows += [("s1", p, a, 1.0), ("s1", p, b, 0.8), ("s2", p, a, 1.0), ("s2", p, b, 1.25)]
-    pol = {p: a for p in pt.PATHS}
-    reg = {r["config_id"]: r["regret_pct"] for r in pt.regret_table(_rows(rows), pol)}
+    table = _rows(rows)
+    for r in table:
+        r["L"], r["K"] = 48, 48
+    pol = {p: {c: a for c in pt.CLASSES} for p in pt.PATHS}
+    reg = {r["config_id"]: r["regret_pct"] for r in pt.regret_table(table, pol)}
     assert reg["s1"] == pytest.approx(25.0)
     assert reg["s2"] == pytest.approx(0.0)
 
 
+HEADER_ROW = r"\{(\{\d+, \d+, \d+\}), (\{\d+, \d+, \d+\}), (\{\d+, \d+, \d+\})\},\s+// (FWD|DX|DK)"
+
+
 def test_render_header_is_parseable_table():
-    pol = {"fwd": (128, 3, 2), "bwd_input": (64, 4, 3), "bwd_weight": (256, 2, 1)}
+    pol = {"fwd": {"light": (64, 4, 3), "medium": (128, 3, 2), "heavy": (128, 2, 3)},
+           "bwd_input": {c: (64, 4, 3) for c in pt.CLASSES},
+           "bwd_weight": {c: (256, 2, 1) for c in pt.CLASSES}}
     text = pt.render_header(pol, "unit test")
-    entries = re.findall(r"\{(\d+), (\d+), (\d+)\},\s+// (FWD|DX|DK)", text)
-    assert entries == [("128", "3", "2", "FWD"), ("64", "4", "3", "DX"), ("256", "2", "1", "DK")]
+    entries = re.findall(HEADER_ROW, text)
+    assert entries[0] == ("{64, 4, 3}", "{128, 3, 2}", "{128, 2, 3}", "FWD")
+    assert [e[3] for e in entries] == ["FWD", "DX", "DK"]
     assert 'kFrozenCfgSource = "unit test"' in text
 
 
 def test_committed_header_matches_renderer_layout():
-    text = pt.HEADER.read_text()
-    assert len(re.findall(r"\{(\d+), (\d+), (\d+)\},\s+// (FWD|DX|DK)", text)) == 3
+    assert len(re.findall(HEADER_ROW, pt.HEADER.read_text())) == 3
 
 
 def test_case_seed_rule():
