@@ -19,8 +19,8 @@ struct LaunchCfg {
 
 // kFrozenCfg[path][class]: path PT_PATH_FWD/DX/DK, class light/medium/heavy.
 constexpr LaunchCfg kFrozenCfg[3][3] = {
-    {{128, 2, 3}, {128, 2, 3}, {128, 2, 3}},  // FWD: light, medium, heavy
-    {{128, 2, 3}, {128, 2, 3}, {128, 2, 3}},  // DX: light, medium, heavy
+    {{128, 3, 2}, {128, 3, 2}, {128, 3, 2}},  // FWD: light, medium, heavy
+    {{128, 3, 2}, {128, 3, 2}, {128, 3, 2}},  // DX: light, medium, heavy
     {{256, 3, 1}, {256, 3, 1}, {256, 3, 1}},  // DK: light, medium, heavy
 };
 

@@ -351,7 +351,7 @@ def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: 
                 ops.set_config(p, *cand)
             for p in PATHS:
                 info = ops.kernel_info(p, case.B, case.H, case.L, case.K)
-                key = (p, cand[0], info["grid"], info["dynamic_smem_bytes"], info["threads_per_block"])
+                key = (p, info["grid"], info["dynamic_smem_bytes"], info["threads_per_block"])
                 alias[(cand, p)] = effective.setdefault(key, cand)
         visits: dict[tuple, list[float]] = {}
         for rep in range(reps):
