@@ -120,9 +120,10 @@ PT_API size_t pt_dk_workspace_bytes(int B, int H, int L, int K);
  * Launch configuration that the frozen PathTile table selects for `path`
  * (PT_PATH_*) at this shape.  out[0] = rows per tile, out[1] = pipeline
  * stages, out[2] = CTAs per SM, out[3] = 1 if an (L,K)-specialised kernel
- * exists, else 0 (generic kernel), and if `n` >= 5, out[4] = the shape's
+ * exists, else 0 (generic kernel); if `n` >= 5, out[4] = the shape's
  * arithmetic-intensity class keying the table (0 light, 1 medium, 2 heavy:
- * in-range FMAs per output element < 12, < 24, else).  `n` >= 4.
+ * in-range FMAs per output element < 12, < 24, else); if `n` >= 6, out[5] =
+ * consumer threads per row (1, or 2 when two threads split a row).  `n` >= 4.
  * Mirrors the frozen constants that the reference bakes into CUDA_TEMPLATE
  * (WARPS_PER_BLOCK / BWDK_BLOCK, kernels/warp_tiled_ampere.py:668-672,
  * selected by scripts/aggregate_pathtile_results.py:222-240).
@@ -131,13 +132,14 @@ PT_API int pt_config(int path, int B, int H, int L, int K, int* out, int n);
 
 /*
  * Override the launch configuration of `path` for all shapes (rows_per_tile in
- * {32,64,128,256}, stages in {2,3,4}, ctas_per_sm in {1,2,3,4}); passing
- * rows_per_tile = 0 restores the frozen table.  Used by the offline PathTile
+ * {32,64,128,256}, stages in {2,3,4}, ctas_per_sm in {1,2,3,4}, threads_per_row
+ * in {1,2}); passing rows_per_tile = 0 restores the frozen table.  Used by the offline PathTile
  * candidate sweep, the counterpart of recompiling CUDA_TEMPLATE per candidate
  * (benchmark/benchmark_pathtile_candidate_sweep.py:493-560).  Not thread-safe
  * with concurrent launches.
  */
-PT_API int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm);
+PT_API int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm,
+                         int threads_per_row);
 
 /*
  * Resources of the kernel `path` would launch for this shape: out[0] registers

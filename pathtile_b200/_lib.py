@@ -43,7 +43,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_dk_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
     "pt_dk_noalloc": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "pt_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int]),
-    "pt_set_config": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
+    "pt_set_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "pt_kernel_info": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int]),
     "pt_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint), _c_int]),
     "pt_status_string": (ctypes.c_char_p, [_c_int]),

@@ -204,8 +204,11 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
   g.stage_bytes = static_cast<unsigned>(stage);
   g.tx_bytes = static_cast<unsigned>(tile_bytes);
   p.smem = static_cast<size_t>(n_buf(g.stages)) * stage + static_cast<size_t>(bar_bytes) + 1024;
-  p.threads = round_up(T, 32) + 32;  // consumer warps + one producer warp
-  p.func = (path == PT_PATH_FWD) ? e.fwd : (path == PT_PATH_DX) ? e.dx : e.dk;
+  // Two consumer threads per row only while the CTA stays within 288 threads
+  // (the kernels' launch bound); larger tiles run one thread per row.
+  const int tpr = (cfg.tpr == 2 && 2 * round_up(T, 32) + 32 <= 288) ? 2 : 1;
+  p.threads = tpr * round_up(T, 32) + 32;  // consumer warps (tpr per row) + one producer warp
+  p.func = (path == PT_PATH_FWD) ? e.fwd[tpr - 1] : (path == PT_PATH_DX) ? e.dx[tpr - 1] : e.dk[tpr - 1];
   p.exact = true;
   int rc = ensure_smem_attr(di, p.func, p.smem);
   if (rc != PT_OK) return rc;
@@ -424,6 +427,7 @@ int pt_config(int path, int B, int H, int L, int K, int* out, int n) {
   out[2] = c.ctas_per_sm;
   out[3] = (e && (e->loader == pt::LOAD_TMA3D || (static_cast<long long>(H) * L) % 4 == 0)) ? 1 : 0;
   if (n >= 5) out[4] = intensity_class(L, K);
+  if (n >= 6) out[5] = c.tpr;
   return PT_OK;
 }
 
@@ -473,7 +477,7 @@ int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n) {
   return PT_OK;
 }
 
-int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm) {
+int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm, int threads_per_row) {
   if (path < 0 || path > 2) return PT_ERR_ARGS;
   if (rows_per_tile == 0) {
     g_has_override[path] = false;
@@ -481,7 +485,8 @@ int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm) {
   }
   if (rows_per_tile < 32 || rows_per_tile > 256 || rows_per_tile % 32 != 0) return PT_ERR_ARGS;
   if (stages < 2 || stages > 4 || ctas_per_sm < 1 || ctas_per_sm > 4) return PT_ERR_ARGS;
-  g_override[path] = pt::LaunchCfg{rows_per_tile, stages, ctas_per_sm};
+  if (threads_per_row != 1 && threads_per_row != 2) return PT_ERR_ARGS;
+  g_override[path] = pt::LaunchCfg{rows_per_tile, stages, ctas_per_sm, threads_per_row};
   g_has_override[path] = true;
   return PT_OK;
 }

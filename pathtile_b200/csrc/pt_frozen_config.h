@@ -3,7 +3,7 @@
 // Written by `python -m pathtile_b200.pathtile --mode aggregate --write-header`:
 // per path and per arithmetic-intensity class (in-range FMAs per output
 // element: light < 12 <= medium < 24 <= heavy), the candidate (rows per tile,
-// ring stages, CTAs per SM) with the minimum sum of mean latency over that
+// ring stages, CTAs per SM, threads per row) with the minimum sum of mean latency over that
 // class's tuning shapes, ties to the smaller candidate -- the reference's
 // selection rule (scripts/aggregate_pathtile_results.py:222-240) applied per
 // class.  Deployment looks the class up; it does no per-shape search.
@@ -15,13 +15,14 @@ struct LaunchCfg {
   int rows;         // rows per tile = threads doing math per CTA (32..256)
   int stages;       // shared-memory ring depth (2..4)
   int ctas_per_sm;  // persistent CTAs per SM (1..4), clamped by occupancy
+  int tpr;          // consumer threads per row (1 or 2)
 };
 
 // kFrozenCfg[path][class]: path PT_PATH_FWD/DX/DK, class light/medium/heavy.
 constexpr LaunchCfg kFrozenCfg[3][3] = {
-    {{128, 3, 2}, {128, 3, 2}, {128, 3, 2}},  // FWD: light, medium, heavy
-    {{128, 3, 2}, {128, 3, 2}, {128, 3, 2}},  // DX: light, medium, heavy
-    {{256, 3, 1}, {256, 3, 1}, {256, 3, 1}},  // DK: light, medium, heavy
+    {{128, 3, 2, 1}, {128, 3, 2, 1}, {128, 3, 2, 1}},  // FWD: light, medium, heavy
+    {{128, 3, 2, 1}, {128, 3, 2, 1}, {128, 3, 2, 1}},  // DX: light, medium, heavy
+    {{256, 3, 1, 1}, {256, 3, 1, 1}, {256, 3, 1, 1}},  // DK: light, medium, heavy
 };
 
 constexpr const char* kFrozenCfgSource = "B200 sweep of preset pathtile-train (2 trials x 3 visits), global policy per path";

@@ -221,20 +221,20 @@ __device__ __forceinline__ void row_load(const float* __restrict__ p, float (&v)
   }
 }
 
-template <int L, int LOADER>
+template <int L, int LOADER, int T0 = 0, int T1 = L>
 __device__ __forceinline__ void row_store(float* __restrict__ p, const float (&v)[L]) {
   if constexpr (LOADER == LOAD_TMA3D) {
 #pragma unroll
-    for (int c = 0; c < L / 4; ++c)
+    for (int c = T0 / 4; c < T1 / 4; ++c)
       reinterpret_cast<float4*>(p)[c] =
           make_float4(v[4 * c + 0], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-  } else if constexpr (L % 2 == 0) {
+  } else if constexpr (L % 2 == 0 && T0 % 2 == 0 && T1 % 2 == 0) {
 #pragma unroll
-    for (int c = 0; c < L / 2; ++c)
+    for (int c = T0 / 2; c < T1 / 2; ++c)
       reinterpret_cast<float2*>(p)[c] = make_float2(v[2 * c + 0], v[2 * c + 1]);
   } else {
 #pragma unroll
-    for (int i = 0; i < L; ++i) p[i] = v[i];
+    for (int i = T0; i < T1; ++i) p[i] = v[i];
   }
 }
 
@@ -242,12 +242,12 @@ __device__ __forceinline__ void row_store(float* __restrict__ p, const float (&v
 // (the out-of-range pairs are dropped at compile time: no predicates).  Four
 // outputs advance together so consecutive FFMAs are independent; each output
 // still sums its taps in ascending j.
-template <int L, int K, int PAD>
+template <int L, int K, int PAD, int T0 = 0, int T1 = L>
 __device__ __forceinline__ void conv_row(const float (&in)[L], const float (&taps)[K],
                                          float (&y)[L]) {
   constexpr int G = 4;
 #pragma unroll
-  for (int t0 = 0; t0 < L; t0 += G) {
+  for (int t0 = T0; t0 < T1; t0 += G) {
     float acc[G];
 #pragma unroll
     for (int u = 0; u < G; ++u) acc[u] = 0.0f;
@@ -257,27 +257,37 @@ __device__ __forceinline__ void conv_row(const float (&in)[L], const float (&tap
       for (int u = 0; u < G; ++u) {
         const int t = t0 + u;
         const int i = t + j - PAD;
-        if (t < L && i >= 0 && i < L) acc[u] = fmaf(in[i], taps[j], acc[u]);
+        if (t < T1 && i >= 0 && i < L) acc[u] = fmaf(in[i], taps[j], acc[u]);
       }
     }
 #pragma unroll
     for (int u = 0; u < G; ++u)
-      if (t0 + u < L) y[t0 + u] = acc[u];
+      if (t0 + u < T1) y[t0 + u] = acc[u];
   }
+}
+
+// Output split for two threads per row: the first thread computes outputs
+// [0, kSplit), the second [kSplit, L).  A multiple of 4 (128-bit stores) near
+// L/2; the in-range FFMA counts of the halves differ by a few percent.
+template <int L>
+constexpr int row_split() {
+  return (L % 4 == 0) ? ((L / 2 + 2) / 4) * 4 : L / 2;
 }
 
 // One row's contribution to the filter gradient: acc[j] += sum_t dy[t] x[t+j-PAD].
 // t outer / j inner: consecutive FFMAs update different accumulators, so the
 // K per-tap chains interleave instead of stalling on FFMA latency.
-template <int L, int K, int PAD>
+// With two threads per row (STRIDE = 2) a thread owns the taps j = J0, J0+2, ...
+// and acc[m] accumulates tap J0 + STRIDE*m.
+template <int L, int K, int PAD, int J0 = 0, int STRIDE = 1>
 __device__ __forceinline__ void xcorr_row(const float (&dy)[L], const float (&x)[L],
-                                          float (&acc)[K]) {
+                                          float (&acc)[(K + STRIDE - 1) / STRIDE]) {
 #pragma unroll
   for (int t = 0; t < L; ++t) {
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
+    for (int j = J0; j < K; j += STRIDE) {
       const int i = t + j - PAD;
-      if (i >= 0 && i < L) acc[j] = fmaf(dy[t], x[i], acc[j]);
+      if (i >= 0 && i < L) acc[(j - J0) / STRIDE] = fmaf(dy[t], x[i], acc[(j - J0) / STRIDE]);
     }
   }
 }
@@ -374,7 +384,7 @@ __device__ __forceinline__ void producer_drain(const PipeBars& bars, int stages,
 // thread overwrites its input row with its output row; the producer stores the
 // tile from the same stage, waits until the store has read it, then refills it.
 // ---------------------------------------------------------------------------
-template <int L, int K, int OP, int LOADER>
+template <int L, int K, int OP, int LOADER, int TPR>
 __global__ void __launch_bounds__(288, 1)
     conv_rows_kernel(const __grid_constant__ CUtensorMap tm_in,
                      const __grid_constant__ CUtensorMap tm_out, const float* __restrict__ in,
@@ -443,12 +453,18 @@ __global__ void __launch_bounds__(288, 1)
     return;
   }
 
-  // ---------------- consumer threads: one row each ----------------
+  // ---------------- consumer threads: TPR per row ----------------
+  // With TPR = 2 the consumer warps form two halves over the same rows; the
+  // first computes outputs [0, SPLIT), the second [SPLIT, L).
+  constexpr int SPLIT = row_split<L>();
+  const int tw = nc / TPR;        // threads per half: whole warps
+  const int part = tid / tw;      // warp-uniform
+  const int r = tid - part * tw;  // row of the tile
   const int T = g.Th * g.Tb;
-  const int h_local = tid % g.Th;
-  const int b_local = tid / g.Th;
+  const int h_local = r % g.Th;
+  const int b_local = r / g.Th;
   const int h = cur.hb * g.Th + h_local;
-  const bool thread_has_row = (tid < T) && (h < g.H);
+  const bool thread_has_row = (r < T) && (h < g.H);
   float taps[K];  // this thread's taps for the whole kernel (reversed for DX)
 #pragma unroll
   for (int j = 0; j < K; ++j) {
@@ -460,13 +476,32 @@ __global__ void __launch_bounds__(288, 1)
     if (!mbar_wait_bounded(smem_u32(&bars.full[s]), static_cast<uint32_t>(it / S) & 1u, err,
                            DEVERR_TIMEOUT_FULL))
       return;
-    if (thread_has_row && cur.q(it) * g.Tb + b_local < g.B) {
-      float* rowp = stage_ptr(s) + static_cast<size_t>(tid) * g.pitch;
+    const bool row_valid = thread_has_row && cur.q(it) * g.Tb + b_local < g.B;
+    float* rowp = stage_ptr(s) + static_cast<size_t>(r) * g.pitch;
+    float yout[L];
+    if (row_valid) {
       float xin[L];
-      float yout[L];
       row_load<L, LOADER>(rowp, xin);
-      conv_row<L, K, PAD>(xin, taps, yout);
-      row_store<L, LOADER>(rowp, yout);
+      if constexpr (TPR == 1) {
+        conv_row<L, K, PAD>(xin, taps, yout);
+      } else if (part == 0) {
+        conv_row<L, K, PAD, 0, SPLIT>(xin, taps, yout);
+      } else {
+        conv_row<L, K, PAD, SPLIT, L>(xin, taps, yout);
+      }
+    }
+    if constexpr (TPR == 1) {
+      if (row_valid) row_store<L, LOADER>(rowp, yout);
+    } else {
+      // Both halves have read the rows (in place, one half's outputs would
+      // overwrite the other's inputs): meet, then write.
+      named_barrier(1 + r / 32, 64);
+      if (row_valid) {
+        if (part == 0)
+          row_store<L, LOADER, 0, SPLIT>(rowp, yout);
+        else
+          row_store<L, LOADER, SPLIT, L>(rowp, yout);
+      }
     }
     fence_proxy_async_smem();
     mbar_arrive(smem_u32(&bars.done[s]));
@@ -480,7 +515,7 @@ __global__ void __launch_bounds__(288, 1)
 // slots of each channel (fixed order) and either one float atomic per
 // (CTA, h, j) or one partial per (CTA, j, h).
 // ---------------------------------------------------------------------------
-template <int L, int K, int LOADER>
+template <int L, int K, int LOADER, int TPR>
 __global__ void __launch_bounds__(288, 1)
     dk_rows_kernel(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_x,
                    const float* __restrict__ dy, const float* __restrict__ x,
@@ -534,15 +569,21 @@ __global__ void __launch_bounds__(288, 1)
     return;
   }
 
-  // ---------------- consumer threads: one row each ----------------
+  // ---------------- consumer threads: TPR per row ----------------
+  // With TPR = 2 the two halves of the consumer warps read the same rows; the
+  // first accumulates the even taps, the second the odd taps.
+  constexpr int NACC = (K + TPR - 1) / TPR;
+  const int tw = nc / TPR;
+  const int part = tid / tw;
+  const int r = tid - part * tw;
   const int T = g.Th * g.Tb;
-  const int h_local = tid % g.Th;
-  const int b_local = tid / g.Th;
+  const int h_local = r % g.Th;
+  const int b_local = r / g.Th;
   const int h = cur.hb * g.Th + h_local;
-  const bool thread_has_row = (tid < T) && (h < g.H);
-  float acc[K];
+  const bool thread_has_row = (r < T) && (h < g.H);
+  float acc[NACC];
 #pragma unroll
-  for (int j = 0; j < K; ++j) acc[j] = 0.0f;
+  for (int m = 0; m < NACC; ++m) acc[m] = 0.0f;
   bool failed = false;
   for (int it = 0; it < cur.n_it; ++it) {
     const int s = it % S;
@@ -554,9 +595,15 @@ __global__ void __launch_bounds__(288, 1)
     if (thread_has_row && cur.q(it) * g.Tb + b_local < g.B) {
       float gyr[L];
       float xr[L];
-      row_load<L, LOADER>(buf(s, 0) + static_cast<size_t>(tid) * g.pitch, gyr);
-      row_load<L, LOADER>(buf(s, 1) + static_cast<size_t>(tid) * g.pitch, xr);
-      xcorr_row<L, K, PAD>(gyr, xr, acc);
+      row_load<L, LOADER>(buf(s, 0) + static_cast<size_t>(r) * g.pitch, gyr);
+      row_load<L, LOADER>(buf(s, 1) + static_cast<size_t>(r) * g.pitch, xr);
+      if constexpr (TPR == 1) {
+        xcorr_row<L, K, PAD>(gyr, xr, acc);
+      } else if (part == 0) {
+        xcorr_row<L, K, PAD, 0, 2>(gyr, xr, acc);
+      } else {
+        xcorr_row<L, K, PAD, 1, 2>(gyr, xr, acc);
+      }
     }
     fence_proxy_async_smem();  // reads of the stage precede its async-proxy refill
     mbar_arrive(smem_u32(&bars.done[s]));
@@ -565,9 +612,12 @@ __global__ void __launch_bounds__(288, 1)
   if (named_barrier_or(1, nc, failed)) return;
 
   float* red = reinterpret_cast<float*>(smem);  // [K][T]; every load was consumed
-  if (tid < T) {
+  if (r < T) {
 #pragma unroll
-    for (int j = 0; j < K; ++j) red[j * T + tid] = acc[j];
+    for (int m = 0; m < NACC; ++m) {
+      const int j = part + TPR * m;
+      if (j < K) red[j * T + r] = acc[m];
+    }
   }
   named_barrier(1, nc);
   const int nh = min(g.Th, g.H - cur.hb * g.Th);

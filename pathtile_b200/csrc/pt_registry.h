@@ -10,10 +10,10 @@ namespace pt {
 
 struct Entry {
   int L, K;
-  int loader;       // LOAD_TMA3D or LOAD_BULK1D
-  const void* fwd;  // conv_rows_kernel<L,K,OP_FWD,loader>
-  const void* dx;   // conv_rows_kernel<L,K,OP_DX,loader>
-  const void* dk;   // dk_rows_kernel<L,K,loader>
+  int loader;          // LOAD_TMA3D or LOAD_BULK1D
+  const void* fwd[2];  // conv_rows_kernel<L,K,OP_FWD,loader,TPR>, TPR = 1, 2
+  const void* dx[2];   // conv_rows_kernel<L,K,OP_DX,loader,TPR>
+  const void* dk[2];   // dk_rows_kernel<L,K,loader,TPR>
 };
 
 template <int L, int K>
@@ -22,9 +22,12 @@ Entry make_entry() {
   return Entry{L,
                K,
                LD,
-               reinterpret_cast<const void*>(&conv_rows_kernel<L, K, OP_FWD, LD>),
-               reinterpret_cast<const void*>(&conv_rows_kernel<L, K, OP_DX, LD>),
-               reinterpret_cast<const void*>(&dk_rows_kernel<L, K, LD>)};
+               {reinterpret_cast<const void*>(&conv_rows_kernel<L, K, OP_FWD, LD, 1>),
+                reinterpret_cast<const void*>(&conv_rows_kernel<L, K, OP_FWD, LD, 2>)},
+               {reinterpret_cast<const void*>(&conv_rows_kernel<L, K, OP_DX, LD, 1>),
+                reinterpret_cast<const void*>(&conv_rows_kernel<L, K, OP_DX, LD, 2>)},
+               {reinterpret_cast<const void*>(&dk_rows_kernel<L, K, LD, 1>),
+                reinterpret_cast<const void*>(&dk_rows_kernel<L, K, LD, 2>)}};
 }
 
 void register_shard_0(std::vector<Entry>& v);

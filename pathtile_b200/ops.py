@@ -206,10 +206,10 @@ def dk(
 def config(path: str, B: int, H: int, L: int, K: int) -> dict[str, int]:
     """Frozen launch choice of one path at one shape (C ABI pt_config)."""
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
-    out = (ctypes.c_int * 5)()
-    _lib.check(_lib.load().pt_config(code, B, H, L, K, out, 5), "pt_config")
+    out = (ctypes.c_int * 6)()
+    _lib.check(_lib.load().pt_config(code, B, H, L, K, out, 6), "pt_config")
     return {"rows_per_tile": out[0], "stages": out[1], "ctas_per_sm": out[2], "specialised": out[3],
-            "intensity_class": ("light", "medium", "heavy")[out[4]]}
+            "intensity_class": ("light", "medium", "heavy")[out[4]], "threads_per_row": out[5]}
 
 
 def kernel_info(path: str, B: int, H: int, L: int, K: int, device: torch.device | int | None = None) -> dict[str, int]:
@@ -228,10 +228,12 @@ def kernel_info(path: str, B: int, H: int, L: int, K: int, device: torch.device 
     return dict(zip(keys, (int(v) for v in out)))
 
 
-def set_config(path: str, rows_per_tile: int = 0, stages: int = 3, ctas_per_sm: int = 2) -> None:
+def set_config(path: str, rows_per_tile: int = 0, stages: int = 3, ctas_per_sm: int = 2,
+               threads_per_row: int = 1) -> None:
     """Override one path's launch configuration (rows_per_tile=0 restores the frozen table)."""
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
-    _lib.check(_lib.load().pt_set_config(code, rows_per_tile, stages, ctas_per_sm), "pt_set_config")
+    _lib.check(_lib.load().pt_set_config(code, rows_per_tile, stages, ctas_per_sm, threads_per_row),
+               "pt_set_config")
 
 
 def device_error(clear: bool = False, device: torch.device | int | None = None) -> int:

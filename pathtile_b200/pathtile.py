@@ -35,6 +35,7 @@ PATHS = ("fwd", "bwd_input", "bwd_weight")
 ROWS = (64, 128, 256)
 STAGES = (2, 3, 4)
 CTAS = (1, 2, 3, 4)
+TPRS = (1, 2)
 HEADER = Path(__file__).resolve().parent / "csrc" / "pt_frozen_config.h"
 
 
@@ -155,17 +156,22 @@ def intensity_class(L: int, K: int) -> str:
     return "light" if f < 12 else ("medium" if f < 24 else "heavy")
 
 
-def candidates() -> list[tuple[int, int, int]]:
-    return [(r, s, c) for r in ROWS for s in STAGES for c in CTAS]
+def candidates() -> list[tuple[int, int, int, int]]:
+    return [(r, s, c, t) for t in TPRS for r in ROWS for s in STAGES for c in CTAS]
 
 
-def candidate_id(c: tuple[int, int, int]) -> str:
-    return f"r{c[0]}s{c[1]}c{c[2]}"
+def candidate_id(c: tuple) -> str:
+    return f"r{c[0]}s{c[1]}c{c[2]}t{c[3]}"
 
 
 # ---------------------------------------------------------------------------
 # Selection logic (pure; unit-tested on CPU)
 # ---------------------------------------------------------------------------
+def _cand(row: dict) -> tuple[int, int, int, int]:
+    """(rows, stages, ctas_per_sm, threads_per_row) of a summary row."""
+    return (int(row["rows"]), int(row["stages"]), int(row["ctas_per_sm"]), int(row.get("threads_per_row") or 1))
+
+
 def _class_of(row: dict) -> str:
     return intensity_class(int(row["L"]), int(row["K"]))
 
@@ -189,7 +195,7 @@ def select_policy(summary: list[dict], per_class: bool = False) -> dict[str, dic
             totals: dict[tuple[int, int, int], float] = {}
             seen: dict[tuple[int, int, int], set] = {}
             for r in rows:
-                c = (int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))
+                c = _cand(r)
                 totals[c] = totals.get(c, 0.0) + float(r["mean_ms"])
                 seen.setdefault(c, set()).add(r["config_id"])
             eligible = [(t, c) for c, t in totals.items() if seen[c] == shapes]
@@ -226,8 +232,7 @@ def regret_table(summary: list[dict], policy: dict[str, dict[str, tuple[int, int
     lookup = {}
     cls_of = {}
     for r in summary:
-        lookup[(r["config_id"], r["phase"], int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))] = float(
-            r["mean_ms"])
+        lookup[(r["config_id"], r["phase"], *_cand(r))] = float(r["mean_ms"])
         cls_of[r["config_id"]] = _class_of(r)
     best = oracle_totals(summary)
     rows = []
@@ -247,7 +252,7 @@ def render_header(policy: dict[str, dict[str, tuple[int, int, int]]], source: st
         "// Written by `python -m pathtile_b200.pathtile --mode aggregate --write-header`:",
         "// per path and per arithmetic-intensity class (in-range FMAs per output",
         "// element: light < 12 <= medium < 24 <= heavy), the candidate (rows per tile,",
-        "// ring stages, CTAs per SM) with the minimum sum of mean latency over that",
+        "// ring stages, CTAs per SM, threads per row) with the minimum sum of mean latency over that",
         "// class's tuning shapes, ties to the smaller candidate -- the reference's",
         "// selection rule (scripts/aggregate_pathtile_results.py:222-240) applied per",
         "// class.  Deployment looks the class up; it does no per-shape search.",
@@ -259,13 +264,14 @@ def render_header(policy: dict[str, dict[str, tuple[int, int, int]]], source: st
         "  int rows;         // rows per tile = threads doing math per CTA (32..256)",
         "  int stages;       // shared-memory ring depth (2..4)",
         "  int ctas_per_sm;  // persistent CTAs per SM (1..4), clamped by occupancy",
+        "  int tpr;          // consumer threads per row (1 or 2)",
         "};",
         "",
         "// kFrozenCfg[path][class]: path PT_PATH_FWD/DX/DK, class light/medium/heavy.",
         "constexpr LaunchCfg kFrozenCfg[3][3] = {",
     ]
     for p, name in zip(PATHS, ("FWD", "DX", "DK")):
-        cells = ", ".join("{%d, %d, %d}" % policy[p][c] for c in CLASSES)
+        cells = ", ".join("{%d, %d, %d, %d}" % tuple(policy[p][c]) for c in CLASSES)
         lines.append(f"    {{{cells}}},  // {name}: light, medium, heavy")
     lines += ["};", "", f'constexpr const char* kFrozenCfgSource = "{source}";', "", "}  // namespace pt", ""]
     return "\n".join(lines)
@@ -383,7 +389,7 @@ def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: 
                 for q in PATHS:
                     ops.set_config(q, *cand)
                 base = {**asdict(case), "trial": trial, "phase": p, "rows": cand[0], "stages": cand[1],
-                        "ctas_per_sm": cand[2], "max_norm_err": valid[cand][p]}
+                        "ctas_per_sm": cand[2], "threads_per_row": cand[3], "max_norm_err": valid[cand][p]}
                 src = alias[(cand, p)]
                 if (src, p) not in visits:
                     summ.append({**base, "valid": False})
@@ -439,10 +445,11 @@ def aggregate_trials(root: Path) -> list[dict]:
             shape[r["config_id"]] = (int(r["L"]), int(r["K"]))
             if r.get("valid") != "True":
                 continue
-            key = (r["config_id"], r["phase"], int(r["rows"]), int(r["stages"]), int(r["ctas_per_sm"]))
+            key = (r["config_id"], r["phase"], *_cand(r))
             acc.setdefault(key, []).append(float(r["mean_ms"]))
     return [{"config_id": k[0], "phase": k[1], "rows": k[2], "stages": k[3], "ctas_per_sm": k[4],
-             "L": shape[k[0]][0], "K": shape[k[0]][1], "mean_ms": statistics.mean(v), "trials": len(v)}
+             "threads_per_row": k[5], "L": shape[k[0]][0], "K": shape[k[0]][1],
+             "mean_ms": statistics.mean(v), "trials": len(v)}
             for k, v in sorted(acc.items())]
 
 
@@ -468,7 +475,8 @@ def main() -> None:
         policy = select_policy(summary, per_class=args.per_class)
         _write_csv(args.out / "aggregate_summary.csv", summary)
         reg = regret_table(summary, policy)
-        doc = {"policy": {p: {c: dict(zip(("rows", "stages", "ctas_per_sm"), policy[p][c])) for c in CLASSES}
+        doc = {"policy": {p: {c: dict(zip(("rows", "stages", "ctas_per_sm", "threads_per_row"), policy[p][c]))
+                              for c in CLASSES}
                           for p in PATHS},
                "per_class": args.per_class,
                "tuning_preset": args.preset, "tuning_shapes": sorted({r["config_id"] for r in summary}),
@@ -480,7 +488,8 @@ def main() -> None:
     else:
         summary = aggregate_trials(args.out)
         pol = json.loads(args.policy.read_text())["policy"]
-        policy = {p: {c: (pol[p][c]["rows"], pol[p][c]["stages"], pol[p][c]["ctas_per_sm"]) for c in CLASSES}
+        policy = {p: {c: (pol[p][c]["rows"], pol[p][c]["stages"], pol[p][c]["ctas_per_sm"],
+                          pol[p][c].get("threads_per_row", 1)) for c in CLASSES}
                   for p in PATHS}
         reg = regret_table(summary, policy)
         _write_csv(args.out / "regret.csv", reg)

@@ -279,6 +279,7 @@ class B200WarpRuntime:
         fast_math: bool = False,
         stages: int | None = None,
         ctas_per_sm: int | None = None,
+        threads_per_row: int = 1,
         dk_mode: str = "deterministic",
         device: int | None = None,
     ) -> None:
@@ -302,6 +303,9 @@ class B200WarpRuntime:
         self.bwdk_block = bwdk_block
         self.stages = stages
         self.ctas_per_sm = ctas_per_sm
+        if threads_per_row not in (1, 2):
+            raise ValueError("threads_per_row must be 1 or 2")
+        self.threads_per_row = threads_per_row
         self.dk_mode = dk_mode
         self.fast_math = False
         self._closed = False
@@ -311,9 +315,10 @@ class B200WarpRuntime:
         if self.warps_per_block is not None or self.stages is not None or self.ctas_per_sm is not None:
             rows = 32 * (self.warps_per_block or 4)
             for path in ("fwd", "bwd_input"):
-                ops.set_config(path, rows, self.stages or 3, self.ctas_per_sm or 2)
+                ops.set_config(path, rows, self.stages or 3, self.ctas_per_sm or 2, self.threads_per_row)
         if self.bwdk_block is not None or self.stages is not None or self.ctas_per_sm is not None:
-            ops.set_config("bwd_weight", self.bwdk_block or 128, self.stages or 2, self.ctas_per_sm or 2)
+            ops.set_config("bwd_weight", self.bwdk_block or 128, self.stages or 2, self.ctas_per_sm or 2,
+                           self.threads_per_row)
 
     @staticmethod
     def _check_shapes(x: torch.Tensor, k: torch.Tensor) -> tuple[int, int, int, int]:

@@ -73,14 +73,15 @@ def test_dk_argument_checks(native_lib):
 
 
 def test_set_config_validation(native_lib):
-    assert native_lib.pt_set_config(0, 100, 3, 2) == _lib.PT_ERR_ARGS
-    assert native_lib.pt_set_config(0, 128, 5, 2) == _lib.PT_ERR_ARGS
-    assert native_lib.pt_set_config(0, 128, 3, 9) == _lib.PT_ERR_ARGS
-    assert native_lib.pt_set_config(3, 128, 3, 2) == _lib.PT_ERR_ARGS
-    assert native_lib.pt_set_config(0, 64, 2, 1) == _lib.PT_OK
+    assert native_lib.pt_set_config(0, 100, 3, 2, 1) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_set_config(0, 128, 5, 2, 1) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_set_config(0, 128, 3, 9, 1) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_set_config(3, 128, 3, 2, 1) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_set_config(0, 128, 3, 2, 3) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_set_config(0, 64, 2, 1, 2) == _lib.PT_OK
     cfg = ops.config("fwd", 16384, 128, 48, 48)
-    assert cfg["rows_per_tile"] == 64 and cfg["stages"] == 2
-    assert native_lib.pt_set_config(0, 0, 0, 0) == _lib.PT_OK
+    assert cfg["rows_per_tile"] == 64 and cfg["stages"] == 2 and cfg["threads_per_row"] == 2
+    assert native_lib.pt_set_config(0, 0, 0, 0, 0) == _lib.PT_OK
 
 
 def test_frozen_config_and_specialisation_flags(native_lib):

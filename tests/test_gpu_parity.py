@@ -127,11 +127,12 @@ def test_mid_shapes_full_oracle(cuda_device, B, H, L, K, mode):
 @pytest.mark.parametrize("rows", [32, 64, 128, 256])
 @pytest.mark.parametrize("stages", [2, 3, 4])
 @pytest.mark.parametrize("ctas", [1, 2, 4])
-def test_every_launch_configuration(cuda_device, rows, stages, ctas):
-    shapes = [(700, 128, 48, 48), (301, 300, 48, 48), (257, 64, 37, 13), (65, 20, 40, 40)]
+@pytest.mark.parametrize("tpr", [1, 2])
+def test_every_launch_configuration(cuda_device, rows, stages, ctas, tpr):
+    shapes = [(700, 128, 48, 48), (301, 300, 48, 48), (257, 64, 37, 13), (65, 20, 40, 40), (99, 64, 33, 33)]
     try:
         for path in ("fwd", "bwd_input", "bwd_weight"):
-            ops.set_config(path, rows, stages, ctas)
+            ops.set_config(path, rows, stages, ctas, tpr)
         for B, H, L, K in shapes:
             x, k, dy, cpu = _inputs(B, H, L, K, 7, cuda_device)
             y, gx, gk = run_path(x, k, dy)
