@@ -32,12 +32,12 @@ def _rows(table):
     out = []
     for cid, phase, cand, ms in table:
         out.append({"config_id": cid, "phase": phase, "rows": cand[0], "stages": cand[1],
-                    "ctas_per_sm": cand[2], "mean_ms": ms})
+                    "ctas_per_sm": cand[2], "threads_per_row": cand[3], "mean_ms": ms})
     return out
 
 
 def test_select_policy_sums_over_shapes_and_breaks_ties_low():
-    a, b, c = (64, 2, 1), (128, 3, 2), (256, 2, 1)
+    a, b, c = (64, 2, 1, 1), (128, 3, 2, 1), (256, 2, 1, 2)
     table = []
     for phase in pt.PATHS:
         table += [("s1", phase, a, 1.0), ("s1", phase, b, 0.5), ("s1", phase, c, 0.9),
@@ -50,7 +50,7 @@ def test_select_policy_sums_over_shapes_and_breaks_ties_low():
 
 
 def test_per_class_policy_and_inheritance():
-    a, b = (64, 2, 1), (128, 3, 2)
+    a, b = (64, 2, 1, 1), (128, 3, 2, 2)
     rows = []
     for p in pt.PATHS:  # s_light is (24, 8) = light, s_heavy is (48, 48) = heavy
         rows += [("s_light", p, a, 1.0), ("s_light", p, b, 2.0), ("s_heavy", p, a, 3.0), ("s_heavy", p, b, 1.0)]
@@ -77,7 +77,7 @@ def test_intensity_classes():
 
 
 def test_candidate_missing_a_shape_is_not_eligible():
-    a, b = (64, 2, 1), (128, 3, 2)
+    a, b = (64, 2, 1, 1), (128, 3, 2, 2)
     rows = []
     for p in pt.PATHS:
         rows += [("s1", p, a, 5.0), ("s2", p, a, 5.0), ("s1", p, b, 0.1)]  # b failed on s2
@@ -85,7 +85,7 @@ def test_candidate_missing_a_shape_is_not_eligible():
 
 
 def test_regret_against_per_shape_oracle():
-    a, b = (64, 2, 1), (128, 3, 2)
+    a, b = (64, 2, 1, 1), (128, 3, 2, 2)
     rows = []
     for p in pt.PATHS:
         rows += [("s1", p, a, 1.0), ("s1", p, b, 0.8), ("s2", p, a, 1.0), ("s2", p, b, 1.25)]
@@ -98,16 +98,17 @@ def test_regret_against_per_shape_oracle():
     assert reg["s2"] == pytest.approx(0.0)
 
 
-HEADER_ROW = r"\{(\{\d+, \d+, \d+\}), (\{\d+, \d+, \d+\}), (\{\d+, \d+, \d+\})\},\s+// (FWD|DX|DK)"
+HEADER_ROW = (r"\{(\{\d+, \d+, \d+, \d+\}), (\{\d+, \d+, \d+, \d+\}), (\{\d+, \d+, \d+, \d+\})\},"
+              r"\s+// (FWD|DX|DK)")
 
 
 def test_render_header_is_parseable_table():
-    pol = {"fwd": {"light": (64, 4, 3), "medium": (128, 3, 2), "heavy": (128, 2, 3)},
-           "bwd_input": {c: (64, 4, 3) for c in pt.CLASSES},
-           "bwd_weight": {c: (256, 2, 1) for c in pt.CLASSES}}
+    pol = {"fwd": {"light": (64, 4, 3, 2), "medium": (128, 3, 2, 1), "heavy": (128, 2, 3, 1)},
+           "bwd_input": {c: (64, 4, 3, 1) for c in pt.CLASSES},
+           "bwd_weight": {c: (256, 2, 1, 1) for c in pt.CLASSES}}
     text = pt.render_header(pol, "unit test")
     entries = re.findall(HEADER_ROW, text)
-    assert entries[0] == ("{64, 4, 3}", "{128, 3, 2}", "{128, 2, 3}", "FWD")
+    assert entries[0] == ("{64, 4, 3, 2}", "{128, 3, 2, 1}", "{128, 2, 3, 1}", "FWD")
     assert [e[3] for e in entries] == ["FWD", "DX", "DK"]
     assert 'kFrozenCfgSource = "unit test"' in text
 
