@@ -389,6 +389,59 @@ def run_reference(args, rank: int) -> dict | None:
     }
 
 
+def run_s4_train(args) -> dict:
+    """S4ConvD training step (the reference's model and training configuration,
+    kernels/warp_tiled_ampere.py:1122-1215 and :1432-1560: batch 16384, L = 48,
+    H = 128, 4 blocks, SGD, RMSLE) on synthetic windows, device-timed.  The same
+    model on PyTorch's grouped conv1d (cuDNN; the reference's "pytorch" backend,
+    TF32 off as in its configure_torch) is timed beside it."""
+    import torch.nn.functional as F
+
+    from pathtile_b200 import build, s4conv
+
+    build.build()
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    B = args.batch
+    x, target = s4conv.synthetic_batch(B, device=dev, seed=0)
+
+    def cudnn_conv(xx, kk):
+        K_ = int(kk.shape[1])
+        left = K_ // 2
+        return F.conv1d(F.pad(xx, (left, K_ - 1 - left)), kk.unsqueeze(1), groups=int(xx.shape[1]))
+
+    out = {}
+    for name, conv in (("pathtile_b200", None), ("pytorch_cudnn", cudnn_conv)):
+        torch.manual_seed(0)
+        model = s4conv.Model().to(dev)
+        if conv is not None:
+            for blk in model.blocks:
+                blk.kernel_layer.conv = conv
+        opt = s4conv.make_optimizer(model)
+        for _ in range(args.warmup):
+            s4conv.train_step(model, opt, x, target)
+        ms = time_loop(lambda: s4conv.train_step(model, opt, x, target), args.steps, torch.cuda.current_stream(dev))
+        out[name] = ms
+        del model, opt
+        torch.cuda.empty_cache()
+    return {
+        "metric": "S4ConvD training step (B=16384, L=48, H=128, 4 blocks, SGD, RMSLE), device-timed",
+        "workload": "s4-train",
+        "value": out["pathtile_b200"],
+        "unit": "ms/step",
+        "higher_is_better": False,
+        "pytorch_cudnn_ms": out["pytorch_cudnn"],
+        "speedup_vs_pytorch_cudnn": out["pytorch_cudnn"] / out["pathtile_b200"],
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "batch": B,
+        "dtype": "f32",
+        "data": "synthetic windows (the reference's ASHRAE data is not shipped): x ~ N(0,1), target ~ 3|N(0,1)|",
+        "note": "each block's depthwise conv is the primary shape (B, 128, 48, K=48); skip term folded into the centre tap",
+    }
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -403,6 +456,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=B_PER_GPU,
                     help="batch per GPU (default: the primary workload; smaller only for profiling)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement (profiling)")
+    ap.add_argument("--workload", choices=("primary", "s4-train"), default="primary",
+                    help="s4-train: time the S4ConvD training step instead (single GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -410,6 +465,11 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.workload == "s4-train":
+        if rank == 0:
+            print(json.dumps(run_s4_train(args)), flush=True)
+        return
 
     if args.impl == "reference":
         res = run_reference(args, rank)
