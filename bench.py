@@ -449,7 +449,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--e2e-chunk", type=int, default=2048)
+    ap.add_argument("--e2e-chunk", type=int, default=1024)
     ap.add_argument("--cpu-seconds", type=float, default=3.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-sample-b", type=int, default=256)

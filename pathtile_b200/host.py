@@ -19,7 +19,7 @@ from . import ops
 class HostPipeline:
     """Reusable staging buffers and streams for one device and one [H, L, K] shape."""
 
-    def __init__(self, H: int, L: int, K: int, chunk_b: int = 2048, device: int | torch.device = 0,
+    def __init__(self, H: int, L: int, K: int, chunk_b: int = 1024, device: int | torch.device = 0,
                  depth: int = 3) -> None:
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         self.H, self.L, self.K = H, L, K
