@@ -59,6 +59,10 @@ extern "C" {
 #define PT_PATH_DX 1
 #define PT_PATH_DK 2
 
+/* Engines (pt_set_engine, pt_config out[6]). */
+#define PT_ENGINE_FFMA 0    /* CUDA-core FP32 FMA kernels: every path and shape */
+#define PT_ENGINE_TENSOR 1  /* tcgen05 tensor cores, FP32-accurate 3xTF32 split: FWD/DX with L % 4 == 0 */
+
 /*
  * Forward pass.  Replaces the reference launch of dwconv1d_warptile_fwd via
  * AmpereWarpRuntime.launch_fwd (kernels/warp_tiled_ampere.py:723-747, kernel
@@ -123,7 +127,8 @@ PT_API size_t pt_dk_workspace_bytes(int B, int H, int L, int K);
  * exists, else 0 (generic kernel); if `n` >= 5, out[4] = the shape's
  * arithmetic-intensity class keying the table (0 light, 1 medium, 2 heavy:
  * in-range FMAs per output element < 12, < 24, else); if `n` >= 6, out[5] =
- * consumer threads per row (1, or 2 when two threads split a row).  `n` >= 4.
+ * consumer threads per row (1, or 2 when two threads split a row); if `n` >= 7,
+ * out[6] = the engine that runs (PT_ENGINE_*).  `n` >= 4.
  * Mirrors the frozen constants that the reference bakes into CUDA_TEMPLATE
  * (WARPS_PER_BLOCK / BWDK_BLOCK, kernels/warp_tiled_ampere.py:668-672,
  * selected by scripts/aggregate_pathtile_results.py:222-240).
@@ -142,6 +147,14 @@ PT_API int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_s
                          int threads_per_row);
 
 /*
+ * Engine of `path` for all shapes: PT_ENGINE_FFMA, PT_ENGINE_TENSOR, or -1 to
+ * restore the frozen table.  PT_ENGINE_TENSOR applies to FWD and DX at L % 4 ==
+ * 0 only; other shapes keep the FFMA kernels.  No reference counterpart (the
+ * reference has CUDA-core kernels only).  Not thread-safe with concurrent launches.
+ */
+PT_API int pt_set_engine(int path, int engine);
+
+/*
  * Resources of the kernel `path` would launch for this shape: out[0] registers
  * per thread, out[1] static shared bytes, out[2] local (spill) bytes per
  * thread, out[3] threads per CTA, out[4] dynamic shared bytes, out[5] resident
@@ -156,7 +169,9 @@ PT_API int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n)
  * Device-side error word: kernels never spin without bound; a wait that runs
  * past its limit (2 s) sets a bit here and the kernel returns early: bit 0 a
  * consumer waited for a tile, bit 1 the producer waited for an in-flight copy
- * to drain, bit 2 the producer waited for consumers to finish a stage.  Reads (and
+ * to drain, bit 2 the producer waited for consumers to finish a stage; the
+ * tensor-core kernels add bit 3 (converter waits), bit 4 (MMA issuer waits) and
+ * bit 5 (epilogue waits).  Reads (and
  * with clear != 0, resets) the word of the current device; synchronises the
  * device.  The reference has no device-side error channel (its kernels return
  * silently on L > 48, kernels/warp_tiled_ampere.py:390).

@@ -31,6 +31,9 @@ PT_PATH_FWD = 0
 PT_PATH_DX = 1
 PT_PATH_DK = 2
 
+PT_ENGINE_FFMA = 0
+PT_ENGINE_TENSOR = 1
+
 PT_MAX_L = 48
 PT_MAX_K = 48
 
@@ -44,6 +47,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_dk_noalloc": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "pt_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int]),
     "pt_set_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "pt_set_engine": (_c_int, [_c_int, _c_int]),
     "pt_kernel_info": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int]),
     "pt_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint), _c_int]),
     "pt_status_string": (ctypes.c_char_p, [_c_int]),

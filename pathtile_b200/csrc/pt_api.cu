@@ -15,6 +15,7 @@
 #include "pt_frozen_config.h"
 #include "pt_kernels.cuh"
 #include "pt_registry.h"
+#include "pt_tc.h"
 
 // Device error word (one per device context); kernels receive its address.
 __device__ unsigned int g_pt_device_error;
@@ -46,6 +47,7 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 bool g_padded_box_ok = true;
 pt::LaunchCfg g_override[3];
 bool g_has_override[3] = {false, false, false};
+int g_engine_override[3] = {-1, -1, -1};  // -1: the frozen table decides
 
 int cuda_fail(cudaError_t e) {
   t_last_cuda_error = static_cast<int>(e);
@@ -133,6 +135,51 @@ pt::LaunchCfg cfg_for(int path, int L, int K) {
   return g_has_override[path] ? g_override[path] : pt::kFrozenCfg[path][intensity_class(L, K)];
 }
 
+int gcd_int(int a, int b) {
+  while (b) {
+    const int r = a % b;
+    a = b;
+    b = r;
+  }
+  return a;
+}
+
+// Grid of the tensor-core kernel.  Tiles are dealt round-robin, so CTA g visits
+// channels (g + i*G) mod H with period P = H / gcd(G, H).  Take the largest G
+// up to min(SMs, tiles) with P <= 2 (the CTA's one or two Toeplitz operands
+// then stay resident) as long as it keeps >= 3/4 of that many SMs busy;
+// otherwise every SM, with a per-tile rebuild (period 0).
+void tensor_grid(int H, long long tiles, int sm_count, int& G, int& period) {
+  const int gmax = static_cast<int>(tiles < sm_count ? tiles : sm_count);
+  for (int c = gmax; c >= 1 && 4LL * c >= 3LL * gmax; --c) {
+    const int P = H / gcd_int(c, H);
+    if (P <= 2) {
+      G = c;
+      period = P;
+      return;
+    }
+  }
+  G = gmax;
+  period = 0;
+}
+
+long long tensor_tiles(int B, int H) {
+  return static_cast<long long>((B + pt::tc::kRowsPerTile - 1) / pt::tc::kRowsPerTile) * H;
+}
+
+// Engine of a path at a shape: PT_ENGINE_TENSOR (tcgen05, FWD/DX with L % 4 == 0
+// and a TMA encoder) or PT_ENGINE_FFMA (CUDA-core kernels, every shape).  The
+// frozen table's tensor choice also needs a grid with resident Toeplitz
+// operands; an explicit pt_set_engine override does not.
+int engine_for(int path, int B, int H, int L, int K, int sm_count) {
+  if (path == PT_PATH_DK || L % 4 != 0 || g_encode == nullptr) return PT_ENGINE_FFMA;
+  if (g_engine_override[path] >= 0) return g_engine_override[path];
+  if (pt::kFrozenEngine[path][intensity_class(L, K)] != PT_ENGINE_TENSOR) return PT_ENGINE_FFMA;
+  int G = 0, period = 0;
+  tensor_grid(H, tensor_tiles(B, H), sm_count > 0 ? sm_count : 148, G, period);
+  return period > 0 ? PT_ENGINE_TENSOR : PT_ENGINE_FFMA;
+}
+
 const pt::Entry* find_entry(int L, int K) {
   for (const pt::Entry& e : *g_entries)
     if (e.L == L && e.K == K) return &e;
@@ -145,6 +192,8 @@ int round_up(int v, int q) { return (v + q - 1) / q * q; }
 
 struct Plan {
   bool exact = false;
+  bool tensor = false;  // tcgen05 FWD/DX kernel (grid g.G)
+  int period = 0;       // tensor kernel: channels per CTA (1, 2), or 0 for per-tile Toeplitz rebuilds
   int loader = 0;
   const void* func = nullptr;
   pt::TileGeom g{};
@@ -242,7 +291,33 @@ void plan_generic_dk(int B, int H, int L, int K, const DeviceInfo& di, Plan& p) 
   p.exact = false;
 }
 
+int plan_tensor(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
+  pt::TileGeom& g = p.g;
+  g.B = B;
+  g.H = H;
+  g.L = L;
+  g.K = K;
+  const int lb = pt::tc::layout_class(L);
+  p.func = pt::tc::conv_func(path, lb);
+  p.smem = pt::tc::conv_smem(lb);
+  p.threads = pt::tc::kThreads;
+  if (!p.func || static_cast<long long>(p.smem) > di.max_smem) return PT_ERR_UNSUPPORTED;
+  int rc = ensure_smem_attr(di, p.func, p.smem);
+  if (rc != PT_OK) return rc;
+  const long long tiles = tensor_tiles(B, H);
+  g.Q = static_cast<int>(tiles);  // tiles of 128 batch rows of one channel
+  tensor_grid(H, tiles, di.sm_count, g.G, p.period);
+  g.Th = 1;
+  g.Tb = pt::tc::kRowsPerTile;
+  g.nhb = H;
+  p.exact = true;
+  p.tensor = true;
+  return PT_OK;
+}
+
 int plan(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
+  if (engine_for(path, B, H, L, K, di.sm_count) == PT_ENGINE_TENSOR)
+    return plan_tensor(path, B, H, L, K, di, p);
   const pt::Entry* e = find_entry(L, K);
   const bool tma_ok = g_encode != nullptr;
   if (e && ((e->loader == pt::LOAD_TMA3D && tma_ok) ||
@@ -286,6 +361,52 @@ int encode_pair(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p, C
   return rc;
 }
 
+// Tensor map of the tensor-core path: box of `cols` floats x 1 channel x 128
+// batch rows with the 128-B (cols 32) or 64-B (cols 16) swizzle.
+int encode_tc_tmap(CUtensorMap* tm, const float* base, int B, int H, int L, int cols) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(L), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(L) * 4, static_cast<cuuint64_t>(L) * H * 4};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(cols), 1u,
+                       static_cast<cuuint32_t>(pt::tc::kRowsPerTile)};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                        strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = static_cast<int>(r);
+    return PT_ERR_CUDA;
+  }
+  return PT_OK;
+}
+
+int launch_tensor(const Plan& p, const float* in, const float* taps, float* out, unsigned* err,
+                  cudaStream_t stream) {
+  const pt::TileGeom& g = p.g;
+  const int lb = pt::tc::layout_class(g.L);
+  CUtensorMap in128, in64, out128, out64;
+  std::memset(&in128, 0, sizeof(in128));
+  std::memset(&in64, 0, sizeof(in64));
+  std::memset(&out128, 0, sizeof(out128));
+  std::memset(&out64, 0, sizeof(out64));
+  int rc = PT_OK;
+  if (lb >= 2) {
+    if ((rc = encode_tc_tmap(&in128, in, g.B, g.H, g.L, 32)) != PT_OK) return rc;
+    if ((rc = encode_tc_tmap(&out128, out, g.B, g.H, g.L, 32)) != PT_OK) return rc;
+  }
+  if (lb & 1) {
+    if ((rc = encode_tc_tmap(&in64, in, g.B, g.H, g.L, 16)) != PT_OK) return rc;
+    if ((rc = encode_tc_tmap(&out64, out, g.B, g.H, g.L, 16)) != PT_OK) return rc;
+  }
+  int H = g.H, L = g.L, K = g.K, n_tiles = g.Q, period = p.period;
+  void* args[] = {&in128, &in64, &out128, &out64, const_cast<float**>(&taps), &H, &L, &K, &n_tiles,
+                  &period, &err};
+  const cudaError_t ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  return PT_OK;
+}
+
 // act1/act2 are [B,H,L] activations (may be null when B == 0, as an empty
 // tensor has no storage); hk is the [H,K] filter or filter gradient.
 int check_common(const void* act1, const void* act2, const void* hk, int B, int H, int L, int K) {
@@ -307,6 +428,7 @@ int launch_rows(int path, const float* in, const float* taps, float* out, int B,
   Plan p;
   if ((rc = plan(path, B, H, L, K, *di, p)) != PT_OK) return rc;
   cudaError_t ce;
+  if (p.tensor) return launch_tensor(p, in, taps, out, di->err, stream);
   if (p.exact) {
     CUtensorMap tm_in, tm_out;
     std::memset(&tm_in, 0, sizeof(tm_in));
@@ -428,6 +550,14 @@ int pt_config(int path, int B, int H, int L, int K, int* out, int n) {
   out[3] = (e && (e->loader == pt::LOAD_TMA3D || (static_cast<long long>(H) * L) % 4 == 0)) ? 1 : 0;
   if (n >= 5) out[4] = intensity_class(L, K);
   if (n >= 6) out[5] = c.tpr;
+  if (n >= 7) {
+    int sm = 0, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sm = 0;
+    (void)cudaGetLastError();
+    out[6] = engine_for(path, B, H, L, K, sm);
+  }
   return PT_OK;
 }
 
@@ -488,6 +618,14 @@ int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm, int 
   if (threads_per_row != 1 && threads_per_row != 2) return PT_ERR_ARGS;
   g_override[path] = pt::LaunchCfg{rows_per_tile, stages, ctas_per_sm, threads_per_row};
   g_has_override[path] = true;
+  return PT_OK;
+}
+
+int pt_set_engine(int path, int engine) {
+  if (path < 0 || path > 2) return PT_ERR_ARGS;
+  if (engine != -1 && engine != PT_ENGINE_FFMA && engine != PT_ENGINE_TENSOR) return PT_ERR_ARGS;
+  if (path == PT_PATH_DK && engine == PT_ENGINE_TENSOR) return PT_ERR_UNSUPPORTED;
+  g_engine_override[path] = engine;
   return PT_OK;
 }
 

@@ -25,6 +25,14 @@ constexpr LaunchCfg kFrozenCfg[3][3] = {
     {{256, 3, 1, 1}, {256, 3, 1, 1}, {256, 3, 1, 1}},  // DK: light, medium, heavy
 };
 
+// kFrozenEngine[path][class]: PT_ENGINE_FFMA (0) or PT_ENGINE_TENSOR (1); the
+// tensor engine only ever applies to FWD/DX at L % 4 == 0.
+constexpr int kFrozenEngine[3][3] = {
+    {0, 0, 0},  // FWD: light, medium, heavy
+    {0, 0, 0},  // DX: light, medium, heavy
+    {0, 0, 0},  // DK: light, medium, heavy
+};
+
 constexpr const char* kFrozenCfgSource = "B200 sweep of preset pathtile-train (2 trials x 3 visits), global policy per path";
 
 }  // namespace pt

@@ -206,10 +206,11 @@ def dk(
 def config(path: str, B: int, H: int, L: int, K: int) -> dict[str, int]:
     """Frozen launch choice of one path at one shape (C ABI pt_config)."""
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
-    out = (ctypes.c_int * 6)()
-    _lib.check(_lib.load().pt_config(code, B, H, L, K, out, 6), "pt_config")
+    out = (ctypes.c_int * 7)()
+    _lib.check(_lib.load().pt_config(code, B, H, L, K, out, 7), "pt_config")
     return {"rows_per_tile": out[0], "stages": out[1], "ctas_per_sm": out[2], "specialised": out[3],
-            "intensity_class": ("light", "medium", "heavy")[out[4]], "threads_per_row": out[5]}
+            "intensity_class": ("light", "medium", "heavy")[out[4]], "threads_per_row": out[5],
+            "engine": ENGINES[out[6]]}
 
 
 def kernel_info(path: str, B: int, H: int, L: int, K: int, device: torch.device | int | None = None) -> dict[str, int]:
@@ -234,6 +235,17 @@ def set_config(path: str, rows_per_tile: int = 0, stages: int = 3, ctas_per_sm: 
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
     _lib.check(_lib.load().pt_set_config(code, rows_per_tile, stages, ctas_per_sm, threads_per_row),
                "pt_set_config")
+
+
+ENGINES = ("ffma", "tensor")
+
+
+def set_engine(path: str, engine: str | None) -> None:
+    """Select the engine of one path for all shapes: "ffma" (CUDA-core kernels), "tensor"
+    (tcgen05, FWD/DX at L % 4 == 0; other shapes stay on FFMA), or None for the frozen table."""
+    code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
+    eng = -1 if engine is None else ENGINES.index(engine)
+    _lib.check(_lib.load().pt_set_engine(code, eng), "pt_set_engine")
 
 
 def device_error(clear: bool = False, device: torch.device | int | None = None) -> int:
