@@ -163,20 +163,30 @@ void tensor_grid(int H, long long tiles, int sm_count, int& G, int& period) {
   period = 0;
 }
 
-long long tensor_tiles(int B, int H) {
-  return static_cast<long long>((B + pt::tc::kRowsPerTile - 1) / pt::tc::kRowsPerTile) * H;
+// Channel groups (super-rows of Hc channels) of the tensor-core kernel.
+int tensor_groups(int H, int L) {
+  const int hc = pt::tc::layout_for(L).hc;
+  return (H + hc - 1) / hc;
+}
+
+long long tensor_tiles(int B, int groups) {
+  return static_cast<long long>((B + pt::tc::kRowsPerTile - 1) / pt::tc::kRowsPerTile) * groups;
 }
 
 // Engine of a path at a shape: PT_ENGINE_TENSOR (tcgen05, FWD/DX with L % 4 == 0
 // and a TMA encoder) or PT_ENGINE_FFMA (CUDA-core kernels, every shape).  The
-// frozen table's tensor choice also needs a grid with resident Toeplitz
-// operands; an explicit pt_set_engine override does not.
+// frozen table's tensor choice applies only to full tiles (48 % L == 0: one
+// 48-column channel or 48 / L packed channels per tile row; partially filled
+// tiles measured faster on the FFMA kernels) and needs a grid with resident
+// Toeplitz operands; an explicit pt_set_engine override needs neither.
 int engine_for(int path, int B, int H, int L, int K, int sm_count) {
   if (path == PT_PATH_DK || L % 4 != 0 || g_encode == nullptr) return PT_ENGINE_FFMA;
   if (g_engine_override[path] >= 0) return g_engine_override[path];
-  if (pt::kFrozenEngine[path][intensity_class(L, K)] != PT_ENGINE_TENSOR) return PT_ENGINE_FFMA;
+  if (48 % L != 0 || pt::kFrozenEngine[path][intensity_class(L, K)] != PT_ENGINE_TENSOR)
+    return PT_ENGINE_FFMA;
   int G = 0, period = 0;
-  tensor_grid(H, tensor_tiles(B, H), sm_count > 0 ? sm_count : 148, G, period);
+  const int groups = tensor_groups(H, L);
+  tensor_grid(groups, tensor_tiles(B, groups), sm_count > 0 ? sm_count : 148, G, period);
   return period > 0 ? PT_ENGINE_TENSOR : PT_ENGINE_FFMA;
 }
 
@@ -193,7 +203,9 @@ int round_up(int v, int q) { return (v + q - 1) / q * q; }
 struct Plan {
   bool exact = false;
   bool tensor = false;  // tcgen05 FWD/DX kernel (grid g.G)
-  int period = 0;       // tensor kernel: channels per CTA (1, 2), or 0 for per-tile Toeplitz rebuilds
+  int period = 0;       // tensor kernel: channel groups per CTA (1, 2), or 0 for per-tile Toeplitz rebuilds
+  int groups = 0;       // tensor kernel: channel groups of hc channels
+  pt::tc::Layout lay{1, 3, false};
   int loader = 0;
   const void* func = nullptr;
   pt::TileGeom g{};
@@ -297,16 +309,17 @@ int plan_tensor(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   g.H = H;
   g.L = L;
   g.K = K;
-  const int lb = pt::tc::layout_class(L);
-  p.func = pt::tc::conv_func(path, lb);
-  p.smem = pt::tc::conv_smem(lb);
+  p.lay = pt::tc::layout_for(L);
+  p.func = pt::tc::conv_func(path, p.lay);
+  p.smem = pt::tc::conv_smem(p.lay);
   p.threads = pt::tc::kThreads;
   if (!p.func || static_cast<long long>(p.smem) > di.max_smem) return PT_ERR_UNSUPPORTED;
   int rc = ensure_smem_attr(di, p.func, p.smem);
   if (rc != PT_OK) return rc;
-  const long long tiles = tensor_tiles(B, H);
-  g.Q = static_cast<int>(tiles);  // tiles of 128 batch rows of one channel
-  tensor_grid(H, tiles, di.sm_count, g.G, p.period);
+  p.groups = tensor_groups(H, L);
+  const long long tiles = tensor_tiles(B, p.groups);
+  g.Q = static_cast<int>(tiles);  // tiles of 128 batch rows of one channel group
+  tensor_grid(p.groups, tiles, di.sm_count, g.G, p.period);
   g.Th = 1;
   g.Tb = pt::tc::kRowsPerTile;
   g.nhb = H;
@@ -361,17 +374,22 @@ int encode_pair(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p, C
   return rc;
 }
 
-// Tensor map of the tensor-core path: box of `cols` floats x 1 channel x 128
-// batch rows with the 128-B (cols 32) or 64-B (cols 16) swizzle.
-int encode_tc_tmap(CUtensorMap* tm, const float* base, int B, int H, int L, int cols) {
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(L), static_cast<cuuint64_t>(H),
-                        static_cast<cuuint64_t>(B)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(L) * 4, static_cast<cuuint64_t>(L) * H * 4};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(cols), 1u,
-                       static_cast<cuuint32_t>(pt::tc::kRowsPerTile)};
+// Tensor map of the tensor-core path: box of `cols` floats x 128 batch rows
+// with the 128-B (cols 32) or 64-B (cols 16) swizzle; 3-D over (L, H, B) with
+// one channel per box, or 2-D over [B, H*L] for packed super-rows.
+int encode_tc_tmap(CUtensorMap* tm, const float* base, int B, int H, int L, int cols, bool packed) {
+  cuuint64_t dims3[3] = {static_cast<cuuint64_t>(L), static_cast<cuuint64_t>(H),
+                         static_cast<cuuint64_t>(B)};
+  cuuint64_t strides3[2] = {static_cast<cuuint64_t>(L) * 4, static_cast<cuuint64_t>(L) * H * 4};
+  cuuint32_t box3[3] = {static_cast<cuuint32_t>(cols), 1u,
+                        static_cast<cuuint32_t>(pt::tc::kRowsPerTile)};
+  cuuint64_t dims2[2] = {static_cast<cuuint64_t>(L) * H, static_cast<cuuint64_t>(B)};
+  cuuint64_t strides2[1] = {static_cast<cuuint64_t>(L) * H * 4};
+  cuuint32_t box2[2] = {static_cast<cuuint32_t>(cols), static_cast<cuuint32_t>(pt::tc::kRowsPerTile)};
   cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
-                        strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, packed ? 2 : 3, const_cast<float*>(base),
+                        packed ? dims2 : dims3, packed ? strides2 : strides3, packed ? box2 : box3, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
                         cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -384,7 +402,8 @@ int encode_tc_tmap(CUtensorMap* tm, const float* base, int B, int H, int L, int 
 int launch_tensor(const Plan& p, const float* in, const float* taps, float* out, unsigned* err,
                   cudaStream_t stream) {
   const pt::TileGeom& g = p.g;
-  const int lb = pt::tc::layout_class(g.L);
+  const int lb = p.lay.lb;
+  const bool packed = p.lay.packed;
   CUtensorMap in128, in64, out128, out64;
   std::memset(&in128, 0, sizeof(in128));
   std::memset(&in64, 0, sizeof(in64));
@@ -392,16 +411,16 @@ int launch_tensor(const Plan& p, const float* in, const float* taps, float* out,
   std::memset(&out64, 0, sizeof(out64));
   int rc = PT_OK;
   if (lb >= 2) {
-    if ((rc = encode_tc_tmap(&in128, in, g.B, g.H, g.L, 32)) != PT_OK) return rc;
-    if ((rc = encode_tc_tmap(&out128, out, g.B, g.H, g.L, 32)) != PT_OK) return rc;
+    if ((rc = encode_tc_tmap(&in128, in, g.B, g.H, g.L, 32, packed)) != PT_OK) return rc;
+    if ((rc = encode_tc_tmap(&out128, out, g.B, g.H, g.L, 32, packed)) != PT_OK) return rc;
   }
   if (lb & 1) {
-    if ((rc = encode_tc_tmap(&in64, in, g.B, g.H, g.L, 16)) != PT_OK) return rc;
-    if ((rc = encode_tc_tmap(&out64, out, g.B, g.H, g.L, 16)) != PT_OK) return rc;
+    if ((rc = encode_tc_tmap(&in64, in, g.B, g.H, g.L, 16, packed)) != PT_OK) return rc;
+    if ((rc = encode_tc_tmap(&out64, out, g.B, g.H, g.L, 16, packed)) != PT_OK) return rc;
   }
-  int H = g.H, L = g.L, K = g.K, n_tiles = g.Q, period = p.period;
-  void* args[] = {&in128, &in64, &out128, &out64, const_cast<float**>(&taps), &H, &L, &K, &n_tiles,
-                  &period, &err};
+  int H = g.H, L = g.L, K = g.K, hc = p.lay.hc, groups = p.groups, n_tiles = g.Q, period = p.period;
+  void* args[] = {&in128, &in64, &out128, &out64, const_cast<float**>(&taps), &H, &L, &K, &hc,
+                  &groups, &n_tiles, &period, &err};
   const cudaError_t ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
   if (ce != cudaSuccess) return cuda_fail(ce);
   return PT_OK;

@@ -8,22 +8,24 @@ namespace tc {
 
 static_assert(kRowsPerTile == M && kThreads == THREADS, "pt_tc.h and pt_tc_kernels.cuh disagree");
 
-const void* conv_func(int path, int lb) {
-  if (path == PT_PATH_FWD) {
-    if (lb == 1) return reinterpret_cast<const void*>(&tc_conv_kernel<OP_FWD, 1>);
-    if (lb == 2) return reinterpret_cast<const void*>(&tc_conv_kernel<OP_FWD, 2>);
-    if (lb == 3) return reinterpret_cast<const void*>(&tc_conv_kernel<OP_FWD, 3>);
-  } else if (path == PT_PATH_DX) {
-    if (lb == 1) return reinterpret_cast<const void*>(&tc_conv_kernel<OP_DX, 1>);
-    if (lb == 2) return reinterpret_cast<const void*>(&tc_conv_kernel<OP_DX, 2>);
-    if (lb == 3) return reinterpret_cast<const void*>(&tc_conv_kernel<OP_DX, 3>);
-  }
+template <int OP>
+static const void* func_for(const Layout& lay) {
+  if (lay.packed) return lay.lb == 3 ? reinterpret_cast<const void*>(&tc_conv_kernel<OP, 3, true>) : nullptr;
+  if (lay.lb == 1) return reinterpret_cast<const void*>(&tc_conv_kernel<OP, 1, false>);
+  if (lay.lb == 2) return reinterpret_cast<const void*>(&tc_conv_kernel<OP, 2, false>);
+  if (lay.lb == 3) return reinterpret_cast<const void*>(&tc_conv_kernel<OP, 3, false>);
   return nullptr;
 }
 
-size_t conv_smem(int lb) {
-  if (lb == 1) return Geo<1>::SMEM;
-  if (lb == 2) return Geo<2>::SMEM;
+const void* conv_func(int path, const Layout& lay) {
+  if (path == PT_PATH_FWD) return func_for<OP_FWD>(lay);
+  if (path == PT_PATH_DX) return func_for<OP_DX>(lay);
+  return nullptr;
+}
+
+size_t conv_smem(const Layout& lay) {
+  if (lay.lb == 1) return Geo<1>::SMEM;
+  if (lay.lb == 2) return Geo<2>::SMEM;
   return Geo<3>::SMEM;
 }
 

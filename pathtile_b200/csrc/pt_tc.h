@@ -6,17 +6,29 @@
 namespace pt {
 namespace tc {
 
-// Box layout class of a row length: 1 (L <= 16), 2 (L <= 32), 3 (L <= 48).
-inline int layout_class(int L) { return L <= 16 ? 1 : (L <= 32 ? 2 : 3); }
-
-// Kernel for path PT_PATH_FWD / PT_PATH_DX and layout class lb, or nullptr.
-const void* conv_func(int path, int lb);
-
-// Dynamic shared memory (bytes) of that kernel.
-size_t conv_smem(int lb);
-
 constexpr int kRowsPerTile = 128;
 constexpr int kThreads = 448;
+
+// Tile layout of a row length L (L % 4 == 0): Hc adjacent channels per
+// super-row (48 / L when that divides and L <= 24, else 1), the super-row's
+// box class lb (1: 16 columns, 2: 32, 3: 48) and whether the tensor maps are
+// 2-D over [B, H*L] (packed) or 3-D over (L, H, B).
+struct Layout {
+  int hc;
+  int lb;
+  bool packed;
+};
+
+inline Layout layout_for(int L) {
+  if (L <= 24 && 48 % L == 0) return Layout{48 / L, 3, true};
+  return Layout{1, L <= 16 ? 1 : (L <= 32 ? 2 : 3), false};
+}
+
+// Kernel for path PT_PATH_FWD / PT_PATH_DX and a layout, or nullptr.
+const void* conv_func(int path, const Layout& lay);
+
+// Dynamic shared memory (bytes) of that kernel.
+size_t conv_smem(const Layout& lay);
 
 }  // namespace tc
 }  // namespace pt

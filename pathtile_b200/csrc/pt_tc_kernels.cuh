@@ -4,9 +4,12 @@
 // L inputs times an L x L Toeplitz matrix whose entries are the channel's taps,
 //   FWD  y[t]  = sum_s x[s]  T[s][t],  T[s][t] = k[s - t + K/2]   (0 <= . < K)
 //   DX   dx[t] = sum_s dy[s] T[s][t],  T[s][t] = k[t - s + K/2]
-// so a tile of 128 batch rows of one channel is a 128 x N x N GEMM with
-// N = L rounded up to 16 (padding rows of A are zero, padding outputs are
-// clipped by the store).
+// A tile is 128 batch rows (the MMA M) of a "super-row" of W columns: one
+// channel (W = L rounded up to 16, padding columns read as zero), or, when
+// 48 % L == 0 and L <= 24, Hc = 48 / L adjacent channels (W = 48; the
+// channels of one batch row are contiguous in HBM).  The GEMM is then
+// 128 x W x W with a block-diagonal Toeplitz operand, one L x L block per
+// channel, so every tile moves the same bytes whatever L is.
 //
 // FP32 accuracy from TF32 tensor cores (the "3xTF32" split): every operand
 // value v is written as hi + lo with hi = v rounded to TF32 (10 mantissa bits,
@@ -20,35 +23,35 @@
 // both sit in shared memory, so A lives in tensor memory: converter threads
 // read their tile row from the TMA stage, split it, and write hi and lo to
 // TMEM (lane = row, column = k); the stage is free again as soon as it has
-// been read.  B (the Toeplitz operand) stays in shared memory as one N2 = 2N
-// row operand [T_hi; T_lo], so each 8-wide k step is two MMAs:
+// been read.  Only the Toeplitz operand is read from shared memory: one
+// 2N-row operand [T_hi; T_lo], so each 8-wide k step is two MMAs,
 //   D[:, 0:2N] (+)= A_hi [T_hi; T_lo]^T     D[:, 0:N] += A_lo T_hi^T
-// and the epilogue adds D[:, t] + D[:, N + t].
+// and the epilogue adds D[:, t] + D[:, N + t] (fewer, wider MMAs measured
+// faster than three N-wide ones).
 //
-// Data movement: a tile's rows are TMA-loaded as one box of 32 floats with the
+// Data movement: tile rows are TMA-loaded as one box of 32 floats with the
 // 128-byte swizzle (columns 0..31) and/or one box of 16 floats with the 64-byte
-// swizzle (columns 32..47, or 0..15 when L <= 16); columns past L and rows past
-// B read as zeros.  The Toeplitz operand is written in the K-major canonical
-// layouts the MMA shared-memory descriptors describe (same swizzles).  Tiles
-// are ordered batch-major (channel fastest) and dealt round-robin to
-// persistent CTAs, so the CTAs in flight together stream contiguous
-// [128, H, L] slabs of HBM.  CTA g then visits channels (g + i*G) mod H, a
-// sequence of period P = H / gcd(G, H); the host picks G with P <= 2 where it
-// can, and the CTA builds its one or two Toeplitz operands once and keeps
-// them.  Otherwise (P = 0 passed) the operand is rebuilt for every tile into a
-// ring of two slots.
+// swizzle (columns 32..47, or 0..15 when W = 16); a 3-D map (L, H, B) per
+// channel, or a 2-D map over [B, H*L] for packed super-rows.  Columns past
+// the channel (or past H*L) and rows past B read as zeros and are clipped on
+// store.  The Toeplitz operand is written in the K-major canonical layouts
+// of the MMA shared-memory descriptors (same swizzles).  Tiles are ordered
+// batch-major (channel group fastest) and dealt round-robin to persistent
+// CTAs, so the CTAs in flight together stream contiguous slabs of HBM.  CTA g
+// then visits groups (g + i*G) mod Hg, a sequence of period P = Hg / gcd(G,
+// Hg); the host picks G with P <= 2 where it can, and the CTA builds its one
+// or two Toeplitz operands once and keeps them.  Otherwise (P = 0 passed) the
+// operand is rebuilt for every tile into a ring of two slots.
 //
 // Roles (448 threads, one CTA per SM):
 //   warp 0       TMA producer: ring of 5 raw stages
-//   warp 1       allocates 512 TMEM columns (2 accumulators of 2N columns, 2 A
-//                slots of hi + lo); lane 0 issues the MMAs and commits them to
-//                mbarriers
+//   warp 1       allocates 512 TMEM columns (2 A slots of hi + lo, 2
+//                accumulators of 2N columns); lane 0 issues the MMAs and
+//                commits them to mbarriers
 //   warps 2-9    converters: two threads per tile row (warp quadrant = TMEM lane
 //                group), half a row each; they also build the Toeplitz operand
-//                from a zero-padded hi/lo tap array (each Toeplitz row is a
-//                shifted window of it)
 //   warps 10-13  epilogue: TMEM -> registers -> one of 2 swizzled staging
-//                buffers -> TMA store; rows past B and columns past L are clipped
+//                buffers -> TMA store
 // Every wait is bounded (%globaltimer); on expiry the kernel records a bit in
 // the device error word, stops issuing, drains its own copies and MMAs, frees
 // its tensor memory and returns.
@@ -65,26 +68,23 @@ constexpr int OUT_SLOTS = 2;     // output staging for the TMA store
 constexpr int B_SLOTS = 2;       // Toeplitz operand [T_hi; T_lo]
 constexpr int A_SLOTS = 2;       // A hi/lo in tensor memory
 constexpr int ACC_SLOTS = 2;     // accumulators in tensor memory
-constexpr int TMEM_COLS = 512;   // D0 @0, D1 @128, A0 @256 (hi, lo @+64), A1 @384
-constexpr int D_COL0 = 0;
-constexpr int A_COL0 = 256;
-constexpr int SLOT_COLS = 128;
+constexpr int TMEM_COLS = 512;   // A slots @0, 128 (lo @+64); D @256, 384
+constexpr int A_COL0 = 0;
+constexpr int A_SLOT_COLS = 128;
 constexpr int LO_COLS = 64;      // A_lo sits 64 columns after A_hi
+constexpr int D_COL0 = A_SLOTS * A_SLOT_COLS;
+constexpr int D_SLOT_COLS = 128;
 constexpr int CONVERTERS = 256;  // warps 2-9
 constexpr int EPI0 = 64 + CONVERTERS;  // first epilogue thread (warps 10-13)
 constexpr int THREADS = EPI0 + 128;
-// Zero-padded tap arrays: Toeplitz entry (t, s) is taps[KP_OFF + shift + s - t]
-// with shift = K/2 (FWD, taps in order) or K-1-K/2 (DX, taps reversed); the
-// index stays within [KP_OFF - 47, KP_OFF + 94] for L, K <= 48.
-constexpr int KP_OFF = 48;
-constexpr int KP_LEN = 160;
+static_assert(D_COL0 + ACC_SLOTS * D_SLOT_COLS <= TMEM_COLS, "tensor memory budget");
 
 constexpr unsigned DEVERR_TC_CONVERT = 8u;   // converters: a tile, A slot or operand never freed
 constexpr unsigned DEVERR_TC_MMA = 16u;      // MMA issuer: converted A or a free accumulator never came
 constexpr unsigned DEVERR_TC_EPILOGUE = 32u; // epilogue: an accumulator was never completed
 
-// Shared-memory geometry for LB = 1 (L <= 16: one 64-B box), 2 (L <= 32: one
-// 128-B box), 3 (L <= 48: a 128-B box and a 64-B box).
+// Shared-memory geometry for LB = 1 (W = 16: one 64-B box), 2 (W = 32: one
+// 128-B box), 3 (W = 48: a 128-B box and a 64-B box).
 template <int LB>
 struct Geo {
   static constexpr int RB128 = (LB >= 2) ? 128 : 0;  // bytes per row, 128-B swizzled box
@@ -92,24 +92,25 @@ struct Geo {
   static constexpr int C128 = RB128 / 16;            // 16-B chunks per row in each box
   static constexpr int C64 = RB64 / 16;
   static constexpr int S64 = (LB >= 2) ? 32 : 0;     // first column held by the 64-B box
-  static constexpr int N = 16 * LB;                  // MMA N = padded reduction extent
-  static constexpr int N2 = 2 * N;                   // rows of [T_hi; T_lo]
+  static constexpr int N = 16 * LB;                  // MMA N = W = padded reduction extent
   static constexpr int KSTEPS = N / 8;               // tf32 MMAs reduce over 8 columns
   static constexpr int K128 = C128 / 2;              // k steps inside the 128-B box
   static constexpr int TILE = M * (RB128 + RB64);    // one raw or staged tile
   static constexpr int BOX64 = M * RB128;            // offset of the 64-B box in a tile
-  static constexpr int BMAT = N2 * (RB128 + RB64);   // one Toeplitz operand
-  static constexpr int BBOX64 = N2 * RB128;          // offset of its 64-B box
+  static constexpr int BMAT = 2 * N * (RB128 + RB64);  // [T_hi; T_lo]: 2N rows
+  static constexpr int BLO128 = N * RB128;           // T_lo rows in the 128-B box
+  static constexpr int BBOX64 = 2 * N * RB128;       // offset of the 64-B box
+  static constexpr int BLO64 = N * RB64;             // T_lo rows in the 64-B box
   static constexpr int OFF_OUT = STAGES * TILE;
   static constexpr int OFF_B = OFF_OUT + OUT_SLOTS * TILE;
-  static constexpr int OFF_KP = OFF_B + B_SLOTS * BMAT;  // [B_SLOTS][hi, lo][KP_LEN] floats
-  static constexpr int OFF_BAR = OFF_KP + B_SLOTS * 2 * KP_LEN * 4;
+  static constexpr int OFF_BAR = OFF_B + B_SLOTS * BMAT;
   static constexpr int N_BARS = 2 * STAGES + 2 * A_SLOTS + 2 * ACC_SLOTS;
   static constexpr int OFF_TMEM = OFF_BAR + N_BARS * 8;
   static constexpr int SMEM = OFF_TMEM + 16 + 1024;  // + slack for 1024-B alignment
-  static_assert(TILE % 1024 == 0 && BMAT % 1024 == 0 && BBOX64 % 1024 == 0 && BOX64 % 1024 == 0,
+  static_assert(TILE % 1024 == 0 && BMAT % 1024 == 0 && BBOX64 % 1024 == 0 && BOX64 % 1024 == 0 &&
+                    BLO128 % 1024 == 0 && BLO64 % 1024 == 0,
                 "swizzled operands must start on 1024-byte boundaries");
-  static_assert(N2 <= SLOT_COLS && N <= LO_COLS, "accumulator and A slots must fit their columns");
+  static_assert(N <= LO_COLS && 2 * N <= D_SLOT_COLS, "A and accumulator slots must fit their columns");
 };
 
 // ---------------------------------------------------------------------------
@@ -236,17 +237,20 @@ __device__ __forceinline__ uint32_t sw64_off(int r, int c) {
 }
 
 // ---------------------------------------------------------------------------
-// The kernel.  n_tiles = ceil(B / 128) * H; tile tau covers channel tau % H and
-// batch rows [128 * (tau / H), +128).  CTA g takes tiles g, g + G, g + 2G, ...
-// bperiod = number of distinct channels CTA g visits (1 or 2), or 0.
+// The kernel.  Hc channels per super-row (1 unless PACKED), Hg = ceil(H / Hc)
+// channel groups, n_tiles = ceil(B / 128) * Hg; tile tau covers group tau % Hg
+// and batch rows [128 * (tau / Hg), +128).  CTA g takes tiles g, g + G, ...
+// bperiod = number of distinct groups CTA g visits (1 or 2), or 0.
+// PACKED: 2-D tensor maps over [B, H*L] (coordinates: column, batch);
+// otherwise 3-D maps (L, H, B) (coordinates: column, channel, batch).
 // ---------------------------------------------------------------------------
-template <int OP, int LB>
+template <int OP, int LB, bool PACKED>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tm_in128,
                    const __grid_constant__ CUtensorMap tm_in64,
                    const __grid_constant__ CUtensorMap tm_out128,
                    const __grid_constant__ CUtensorMap tm_out64, const float* __restrict__ taps,
-                   int H, int L, int K, int n_tiles, int bperiod, unsigned* err) {
+                   int H, int L, int K, int Hc, int Hg, int n_tiles, int bperiod, unsigned* err) {
   using GG = Geo<LB>;
   constexpr int N = GG::N;
   extern __shared__ unsigned char smem_raw[];
@@ -268,9 +272,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int G = static_cast<int>(gridDim.x);
   const int g = static_cast<int>(blockIdx.x);
   const int n_it = (g < n_tiles) ? (n_tiles - 1 - g) / G + 1 : 0;
+  const int W = Hc * L;  // packed super-row width (PACKED only)
 
-  float* kp_all = reinterpret_cast<float*>(sm + GG::OFF_KP);
-  for (int u = static_cast<int>(threadIdx.x); u < B_SLOTS * 2 * KP_LEN; u += THREADS) kp_all[u] = 0.f;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full(s), 1);
@@ -307,12 +310,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             !mbar_wait_bounded(sfree(s), ((i / STAGES) - 1) & 1, err, DEVERR_TIMEOUT_DONE))
           break;
         const int tau = g + i * G;
-        const int h = tau % H;
-        const int b0 = (tau / H) * M;
+        const int grp = tau % Hg;
+        const int b0 = (tau / Hg) * M;
         const uint32_t dst = base + static_cast<uint32_t>(s * GG::TILE);
         mbar_arrive_expect_tx(full(s), GG::TILE);
-        if constexpr (LB >= 2) tma_load_3d(dst, &tm_in128, 0, h, b0, full(s));
-        if constexpr (LB & 1) tma_load_3d(dst + GG::BOX64, &tm_in64, GG::S64, h, b0, full(s));
+        if constexpr (PACKED) {
+          if constexpr (LB >= 2) tma_load_2d(dst, &tm_in128, grp * W, b0, full(s));
+          if constexpr (LB & 1) tma_load_2d(dst + GG::BOX64, &tm_in64, grp * W + GG::S64, b0, full(s));
+        } else {
+          if constexpr (LB >= 2) tma_load_3d(dst, &tm_in128, 0, grp, b0, full(s));
+          if constexpr (LB & 1) tma_load_3d(dst + GG::BOX64, &tm_in64, GG::S64, grp, b0, full(s));
+        }
         issued = i + 1;
       }
       // Every issued load must land before the CTA may exit.
@@ -322,7 +330,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc_n2 = idesc_tf32_m128<GG::N2>();
+      constexpr uint32_t idesc_n2 = idesc_tf32_m128<2 * N>();
       constexpr uint32_t idesc_n = idesc_tf32_m128<N>();
       int issued = 0;
       for (int i = 0; i < n_it; ++i) {
@@ -333,13 +341,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             !mbar_wait_bounded(accfree(d), ((i / ACC_SLOTS) - 1) & 1, err, DEVERR_TC_MMA))
           break;
         tc_fence_after();
-        const uint32_t a_hi = tmem + static_cast<uint32_t>(A_COL0 + a * SLOT_COLS);
+        const uint32_t a_hi = tmem + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS);
         const uint32_t a_lo = a_hi + LO_COLS;
         const uint32_t bmat = base + static_cast<uint32_t>(GG::OFF_B + bs * GG::BMAT);
-        const uint32_t dacc = tmem + static_cast<uint32_t>(D_COL0 + d * SLOT_COLS);
+        const uint32_t dacc = tmem + static_cast<uint32_t>(D_COL0 + d * D_SLOT_COLS);
 #pragma unroll
         for (int kk = 0; kk < GG::KSTEPS; ++kk) {
           const bool in128 = kk < GG::K128;
+          // [T_hi; T_lo] rows 0..2N-1 (the 2N-wide MMA), T_hi alone = rows 0..N-1.
           const uint64_t bdesc = kmajor_desc(
               bmat + (in128 ? 32u * kk : GG::BBOX64 + 32u * (kk - GG::K128)), in128);
           mma_tf32_ts(dacc, a_hi + 8u * kk, bdesc, idesc_n2, kk > 0);  // A_hi [T_hi; T_lo]
@@ -363,49 +372,53 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int half = (warp - 2) >> 2;                   // which half of the row
     constexpr int CH = (GG::C128 + GG::C64) / 2;        // 16-byte chunks per half row
     const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
-    const int shift = (OP == OP_FWD) ? K / 2 : K - 1 - K / 2;
-    // Taps run one tile ahead in a register so their load latency hides behind a tile.
-    float tap_next = 0.f;
-    if (ct < K && n_it > 0) tap_next = __ldg(taps + static_cast<size_t>(g % H) * K + ct);
+    const int pad = K / 2;
     for (int i = 0; i < n_it; ++i) {
       const int s = i % STAGES, a = i % A_SLOTS;
       const bool rebuild = (bperiod == 0) || (i < bperiod);
       const int bs = bperiod ? i % bperiod : i % B_SLOTS;
-      const float tap = tap_next;
-      if (ct < K && i + 1 < n_it && (bperiod == 0 || i + 1 < bperiod))
-        tap_next = __ldg(taps + static_cast<size_t>((g + (i + 1) * G) % H) * K + ct);
-      // The A slot (and a rebuilt Toeplitz slot) was last read by the MMAs of
-      // tile i - 2; the tile itself must have landed.
+      // The A slot was last read by the MMAs of tile i - A_SLOTS, a rebuilt
+      // Toeplitz slot by those of tile i - B_SLOTS; the tile must have landed.
       bool ok = true;
       if (i >= A_SLOTS)
         ok = mbar_wait_bounded(adone(a), ((i / A_SLOTS) - 1) & 1, err, DEVERR_TC_CONVERT);
+      if (ok && rebuild && bperiod == 0 && i >= B_SLOTS) {
+        const int ip = i - B_SLOTS;
+        ok = mbar_wait_bounded(adone(ip % A_SLOTS), (ip / A_SLOTS) & 1, err, DEVERR_TC_CONVERT);
+      }
       if (ok) ok = mbar_wait_bounded(full(s), (i / STAGES) & 1, err, DEVERR_TIMEOUT_FULL);
       if (rebuild) {
-        float* kp = kp_all + bs * 2 * KP_LEN;  // hi at kp, lo at kp + KP_LEN
-        if (ok && ct < K) {
-          const int pos = KP_OFF + ((OP == OP_FWD) ? ct : K - 1 - ct);
-          const float hi = tf32_round(tap);
-          kp[pos] = hi;
-          kp[KP_LEN + pos] = tf32_round(tap - hi);
-        }
         if (named_barrier_or(2, CONVERTERS, !ok)) break;  // all converters leave together
-        // [T_hi; T_lo]: row t (hi) and row N + t (lo) of B^T, chunk c = taps
-        // window at KP_OFF + shift + 4c - t.
+        // Block-diagonal [T_hi; T_lo] of group grp: row t' (hi) and N + t' (lo);
+        // block c of channel grp*Hc + c covers rows and columns [c*L, c*L + L).
+        const int grp = (g + i * G) % Hg;
         unsigned char* bm = sm + GG::OFF_B + bs * GG::BMAT;
         constexpr int CPR = N / 4;  // 16-byte chunks per Toeplitz row
         for (int task = ct; task < N * CPR; task += CONVERTERS) {
-          const int c = task / N;  // row-fastest: 8 consecutive rows share a chunk column
-          const int t = task - c * N;
-          const int w = KP_OFF + shift + 4 * c - t;
-          const float4 hi = make_float4(kp[w], kp[w + 1], kp[w + 2], kp[w + 3]);
-          const float4 lo = make_float4(kp[KP_LEN + w], kp[KP_LEN + w + 1], kp[KP_LEN + w + 2],
-                                        kp[KP_LEN + w + 3]);
-          if (c < GG::C128) {
-            *reinterpret_cast<float4*>(bm + sw128_off(t, c)) = hi;
-            *reinterpret_cast<float4*>(bm + sw128_off(N + t, c)) = lo;
+          const int c4 = task / N;  // row-fastest: 8 consecutive rows share a chunk column
+          const int tp = task - c4 * N;
+          const int sp = 4 * c4;
+          const int cb = tp / L;  // L % 4 == 0: a 4-column chunk never straddles blocks
+          const int ch = grp * Hc + cb;
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+          if (cb == sp / L && cb < Hc && ch < H) {
+            const int t = tp - cb * L;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int sx = sp + q - cb * L;
+              const int j = (OP == OP_FWD) ? sx - t + pad : t - sx + pad;
+              if (sx < L && t < L && j >= 0 && j < K) v[q] = __ldg(taps + static_cast<size_t>(ch) * K + j);
+            }
+          }
+          float4 hi, lo;
+          split4(make_float4(v[0], v[1], v[2], v[3]), hi, lo);
+          if (c4 < GG::C128) {
+            *reinterpret_cast<float4*>(bm + sw128_off(tp, c4)) = hi;
+            *reinterpret_cast<float4*>(bm + GG::BLO128 + sw128_off(tp, c4)) = lo;
           } else {
-            *reinterpret_cast<float4*>(bm + GG::BBOX64 + sw64_off(t, c - GG::C128)) = hi;
-            *reinterpret_cast<float4*>(bm + GG::BBOX64 + sw64_off(N + t, c - GG::C128)) = lo;
+            unsigned char* b64 = bm + GG::BBOX64;
+            *reinterpret_cast<float4*>(b64 + sw64_off(tp, c4 - GG::C128)) = hi;
+            *reinterpret_cast<float4*>(b64 + GG::BLO64 + sw64_off(tp, c4 - GG::C128)) = lo;
           }
         }
         fence_proxy_async_smem();  // the MMAs read the operand through the async proxy
@@ -435,7 +448,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         lo[e] = tf32_round(v[e] - hi);
         v[e] = hi;
       }
-      const uint32_t acol = tmem + lane_base + static_cast<uint32_t>(A_COL0 + a * SLOT_COLS + half * 4 * CH);
+      const uint32_t acol =
+          tmem + lane_base + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + half * 4 * CH);
 #pragma unroll
       for (int u = 0; u < CH / 2; ++u) {
         tmem_st8(acol + 8u * u, v + 8 * u);
@@ -458,11 +472,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool ok = mbar_wait_bounded(mdone(d), (j / ACC_SLOTS) & 1, err, DEVERR_TC_EPILOGUE);
       if (named_barrier_or(1, 128, !ok)) break;  // all epilogue threads leave together
       tc_fence_after();
-      float acc[GG::N2];
+      float acc[2 * N];
       const uint32_t ta = tmem + (static_cast<uint32_t>(32 * quad) << 16) +
-                          static_cast<uint32_t>(D_COL0 + d * SLOT_COLS);
+                          static_cast<uint32_t>(D_COL0 + d * D_SLOT_COLS);
 #pragma unroll
-      for (int u = 0; u < GG::N2 / 16; ++u) tmem_ld16(ta + 16u * u, acc + 16 * u);
+      for (int u = 0; u < 2 * N / 16; ++u) tmem_ld16(ta + 16u * u, acc + 16 * u);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(accfree(d));
@@ -478,11 +492,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       fence_proxy_async_smem();
       named_barrier(1, 128);
       if (et == 0) {
-        const int h = tau % H;
-        const int b0 = (tau / H) * M;
+        const int grp = tau % Hg;
+        const int b0 = (tau / Hg) * M;
         const uint32_t os = base + static_cast<uint32_t>(GG::OFF_OUT + o * GG::TILE);
-        if constexpr (LB >= 2) tma_store_3d(&tm_out128, os, 0, h, b0);
-        if constexpr (LB & 1) tma_store_3d(&tm_out64, os + GG::BOX64, GG::S64, h, b0);
+        if constexpr (PACKED) {
+          if constexpr (LB >= 2) tma_store_2d(&tm_out128, os, grp * W, b0);
+          if constexpr (LB & 1) tma_store_2d(&tm_out64, os + GG::BOX64, grp * W + GG::S64, b0);
+        } else {
+          if constexpr (LB >= 2) tma_store_3d(&tm_out128, os, 0, grp, b0);
+          if constexpr (LB & 1) tma_store_3d(&tm_out64, os + GG::BOX64, GG::S64, grp, b0);
+        }
         bulk_commit();
       }
     }

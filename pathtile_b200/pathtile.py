@@ -14,11 +14,21 @@ persistent CTAs per SM, per path.  Every candidate is validated before it is
 timed, at a batch of at most 128, against PyTorch's own conv1d on the GPU with
 TF32 off (the reference's validation recipe, :153-243).
 
+A second axis is the engine of FWD and dX: the CUDA-core FFMA kernels (the
+candidates above) or the tcgen05 tensor-core kernels (FP32-accurate 3xTF32
+split, L % 4 == 0 only, no launch knobs).  The engine sweep times, per
+shape, the frozen FFMA launch against the tensor engine (both validated the
+same way, visits alternating); per path and intensity class the engine with
+the smaller summed latency over that class's shapes is frozen -- the same
+selection rule applied to the engine axis.
+
 Modes:
   run        sweep one preset, one trial -> <out>/trialN/raw.csv, summary.csv
   aggregate  average trials, select the frozen policy -> frozen_config.json and
-             the C header pathtile_b200/csrc/pt_frozen_config.h
+             the C header pathtile_b200/csrc/pt_frozen_config.h (with
+             --engines, the engine table of an engine sweep goes into it too)
   regret     score the frozen policy on a held-out sweep against its per-shape oracle
+  engines    engine sweep of one preset -> <out>/engines.csv, engine_policy.json
 """
 from __future__ import annotations
 
@@ -156,6 +166,18 @@ def intensity_class(L: int, K: int) -> str:
     return "light" if f < 12 else ("medium" if f < 24 else "heavy")
 
 
+ENGINES = ("ffma", "tensor")
+ENGINE_PATHS = ("fwd", "bwd_input")  # dK has no tensor-core kernel
+
+
+def tensor_applicable(L: int) -> bool:
+    """Shapes the frozen table may send to the tensor engine: L % 4 == 0 (TMA
+    boxes of 16 or 32 floats) and 48 % L == 0, so that every tile row is a
+    full 48-column super-row (one L = 48 channel or 48 / L packed channels);
+    partially filled tiles stay on the FFMA kernels, which measured faster."""
+    return L % 4 == 0 and 48 % L == 0
+
+
 def candidates() -> list[tuple[int, int, int, int]]:
     return [(r, s, c, t) for t in TPRS for r in ROWS for s in STAGES for c in CTAS]
 
@@ -245,7 +267,51 @@ def regret_table(summary: list[dict], policy: dict[str, dict[str, tuple[int, int
     return rows
 
 
-def render_header(policy: dict[str, dict[str, tuple[int, int, int]]], source: str) -> str:
+def select_engines(rows: list[dict]) -> dict[str, dict[str, str]]:
+    """Engine per path and intensity class from engine-sweep rows (config_id,
+    phase, engine, L, K, mean_ms): "tensor" where its summed latency over the
+    class's shapes (those measured on both engines) is strictly smaller than
+    the FFMA kernels', else "ffma"; dK and classes without shapes stay "ffma"."""
+    out: dict[str, dict[str, str]] = {p: {c: "ffma" for c in CLASSES} for p in PATHS}
+    times: dict[tuple, float] = {}
+    cls_of: dict[str, str] = {}
+    for r in rows:
+        times[(r["config_id"], r["phase"], r["engine"])] = float(r["mean_ms"])
+        cls_of[r["config_id"]] = _class_of(r)
+    for path in ENGINE_PATHS:
+        for cls in CLASSES:
+            both = [cid for cid, c in cls_of.items() if c == cls
+                    and (cid, path, "ffma") in times and (cid, path, "tensor") in times]
+            if not both:
+                continue
+            tf = sum(times[(cid, path, "ffma")] for cid in both)
+            tt = sum(times[(cid, path, "tensor")] for cid in both)
+            out[path][cls] = "tensor" if tt < tf else "ffma"
+    return out
+
+
+def engine_regret(rows: list[dict], engines: dict[str, dict[str, str]]) -> list[dict]:
+    """Per shape: FWD + dX time of the frozen engines vs the faster engine per path."""
+    times: dict[tuple, float] = {}
+    cls_of: dict[str, str] = {}
+    for r in rows:
+        times[(r["config_id"], r["phase"], r["engine"])] = float(r["mean_ms"])
+        cls_of[r["config_id"]] = _class_of(r)
+    out = []
+    for cid in sorted(cls_of):
+        cls = cls_of[cid]
+        if not all((cid, p, e) in times for p in ENGINE_PATHS for e in ENGINES):
+            continue
+        frozen = sum(times[(cid, p, engines[p][cls])] for p in ENGINE_PATHS)
+        best = sum(min(times[(cid, p, e)] for e in ENGINES) for p in ENGINE_PATHS)
+        ffma = sum(times[(cid, p, "ffma")] for p in ENGINE_PATHS)
+        out.append({"config_id": cid, "class": cls, "frozen_ms": frozen, "best_ms": best, "ffma_ms": ffma,
+                    "regret_pct": 100.0 * (frozen / best - 1.0), "gain_vs_ffma_pct": 100.0 * (ffma / frozen - 1.0)})
+    return out
+
+
+def render_header(policy: dict[str, dict[str, tuple[int, int, int]]], source: str,
+                  engines: dict[str, dict[str, str]] | None = None) -> str:
     lines = [
         "// pt_frozen_config.h -- launch configuration per path and intensity class, frozen offline.",
         "//",
@@ -272,6 +338,13 @@ def render_header(policy: dict[str, dict[str, tuple[int, int, int]]], source: st
     ]
     for p, name in zip(PATHS, ("FWD", "DX", "DK")):
         cells = ", ".join("{%d, %d, %d, %d}" % tuple(policy[p][c]) for c in CLASSES)
+        lines.append(f"    {{{cells}}},  // {name}: light, medium, heavy")
+    lines += ["};", "",
+              "// kFrozenEngine[path][class]: PT_ENGINE_FFMA (0) or PT_ENGINE_TENSOR (1); the",
+              "// tensor engine only ever applies to FWD/DX at L % 4 == 0.",
+              "constexpr int kFrozenEngine[3][3] = {"]
+    for p, name in zip(PATHS, ("FWD", "DX", "DK")):
+        cells = ", ".join(str(ENGINES.index(engines[p][c]) if engines else 0) for c in CLASSES)
         lines.append(f"    {{{cells}}},  // {name}: light, medium, heavy")
     lines += ["};", "", f'constexpr const char* kFrozenCfgSource = "{source}";', "", "}  // namespace pt", ""]
     return "\n".join(lines)
@@ -420,6 +493,77 @@ def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: 
         indent=1))
 
 
+def run_engine_sweep(cases: list[ShapeCase], warmup: int, runs: int, seed: int, out: Path,
+                     reps: int = 3) -> list[dict]:
+    """Time FWD and dX of every shape with L % 4 == 0 on both engines (FFMA at
+    its frozen launch), visits alternating between engines; figure = median
+    over visits of the per-visit mean."""
+    import torch
+
+    from . import ops
+
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", torch.cuda.current_device())
+    out.mkdir(parents=True, exist_ok=True)
+    stream = torch.cuda.current_stream()
+    rows = []
+    try:
+        for case in cases:
+            if not tensor_applicable(case.L):
+                continue
+            sd = case_seed(seed, case)
+            valid = {}
+            for e in ENGINES:
+                for p in ENGINE_PATHS:
+                    ops.set_engine(p, e)
+                valid[e] = _validate(case, sd, dev)
+            x, k, dy = _make_inputs(case, sd, case.B, dev)
+            y, gx = torch.empty_like(x), torch.empty_like(x)
+            launch = {"fwd": lambda: ops.fwd(x, k, y), "bwd_input": lambda: ops.dx(dy, k, gx)}
+            visits: dict[tuple, list[float]] = {}
+            for rep in range(reps):
+                for e in (ENGINES if rep % 2 == 0 else tuple(reversed(ENGINES))):
+                    for p in ENGINE_PATHS:
+                        ops.set_engine(p, e)
+                        if valid[e][p] > 1e-5:
+                            continue
+                        for _ in range(warmup):
+                            launch[p]()
+                        ev = []
+                        for _ in range(runs):
+                            s, f = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                            s.record(stream)
+                            launch[p]()
+                            f.record(stream)
+                            ev.append((s, f))
+                        torch.cuda.synchronize()
+                        visits.setdefault((e, p), []).append(statistics.mean(s.elapsed_time(f) for s, f in ev))
+            for (e, p), v in sorted(visits.items()):
+                rows.append({"config_id": case.config_id, "B": case.B, "H": case.H, "L": case.L, "K": case.K,
+                             "class": intensity_class(case.L, case.K), "phase": p, "engine": e,
+                             "mean_ms": statistics.median(v), "visits": len(v), "max_norm_err": valid[e][p]})
+            del x, k, dy, y, gx
+            torch.cuda.empty_cache()
+    finally:
+        for p in ENGINE_PATHS:
+            ops.set_engine(p, None)
+    _write_csv(out / "engines.csv", rows)
+    return rows
+
+
+def apply_engines_to_header(text: str, engines: dict[str, dict[str, str]]) -> str:
+    """Rewrite only the kFrozenEngine table of an existing frozen-config header."""
+    start = text.index("constexpr int kFrozenEngine[3][3] = {")
+    end = text.index("};", start) + 2
+    rows = ["constexpr int kFrozenEngine[3][3] = {"]
+    for p, name in zip(PATHS, ("FWD", "DX", "DK")):
+        cells = ", ".join(str(ENGINES.index(engines[p][c])) for c in CLASSES)
+        rows.append(f"    {{{cells}}},  // {name}: light, medium, heavy")
+    rows.append("};")
+    return text[:start] + "\n".join(rows) + text[end:]
+
+
 def _write_csv(path: Path, rows: list[dict]) -> None:
     if not rows:
         path.write_text("")
@@ -455,7 +599,7 @@ def aggregate_trials(root: Path) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--mode", choices=("run", "aggregate", "regret"), required=True)
+    ap.add_argument("--mode", choices=("run", "aggregate", "regret", "engines"), required=True)
     ap.add_argument("--preset", default="pathtile-train", choices=sorted(PRESETS))
     ap.add_argument("--out", type=Path, required=True, help="results directory of this preset")
     ap.add_argument("--trial", type=int, default=1)
@@ -463,11 +607,27 @@ def main() -> None:
     ap.add_argument("--runs", type=int, default=20)
     ap.add_argument("--reps", type=int, default=3, help="round-robin visits per candidate and shape")
     ap.add_argument("--seed", type=int, default=42)
-    ap.add_argument("--write-header", action="store_true", help="aggregate: rewrite pt_frozen_config.h")
+    ap.add_argument("--write-header", action="store_true",
+                    help="aggregate: rewrite pt_frozen_config.h; engines: rewrite its engine table")
     ap.add_argument("--per-class", action="store_true", help="aggregate: select per intensity class")
     ap.add_argument("--policy", type=Path, help="regret: frozen_config.json to score")
+    ap.add_argument("--engines", type=Path, help="aggregate: engine_policy.json to include in the header")
     args = ap.parse_args()
-    if args.mode == "run":
+    if args.mode == "engines":
+        rows = run_engine_sweep(cases_for_preset(args.preset), args.warmup, args.runs, args.seed, args.out,
+                                reps=args.reps)
+        engines = select_engines(rows)
+        reg = engine_regret(rows, engines)
+        doc = {"engines": engines, "tuning_preset": args.preset,
+               "shapes": sorted({r["config_id"] for r in rows}),
+               "regret_pct_mean": statistics.mean(r["regret_pct"] for r in reg) if reg else None,
+               "gain_vs_ffma_pct_mean": statistics.mean(r["gain_vs_ffma_pct"] for r in reg) if reg else None}
+        _write_csv(args.out / "engine_regret.csv", reg)
+        (args.out / "engine_policy.json").write_text(json.dumps(doc, indent=1))
+        print(json.dumps(doc, indent=1))
+        if args.write_header:
+            HEADER.write_text(apply_engines_to_header(HEADER.read_text(), engines))
+    elif args.mode == "run":
         run_sweep(cases_for_preset(args.preset), args.warmup, args.runs, args.trial, args.seed,
                   args.out / f"trial{args.trial}", reps=args.reps)
     elif args.mode == "aggregate":
@@ -484,7 +644,8 @@ def main() -> None:
         (args.out / "frozen_config.json").write_text(json.dumps(doc, indent=1))
         print(json.dumps(doc, indent=1))
         if args.write_header:
-            HEADER.write_text(render_header(policy, f"B200 sweep of preset {args.preset}"))
+            engines = json.loads(args.engines.read_text())["engines"] if args.engines else None
+            HEADER.write_text(render_header(policy, f"B200 sweep of preset {args.preset}", engines))
     else:
         summary = aggregate_trials(args.out)
         pol = json.loads(args.policy.read_text())["policy"]

@@ -2,8 +2,9 @@
 
 The tensor engine must meet the same FP32 bar as the CUDA-core kernels:
 rtol = atol = 1e-5 against the FP64 C oracle, on every layout class of the
-engine (L <= 16: one 64-B swizzled box; L <= 32: one 128-B box; L <= 48:
-both), ragged batch tiles (B not a multiple of 128), K > L, even and odd
+engine (one channel per tile row with L <= 16: one 64-B swizzled box, L <=
+32: one 128-B box, L <= 48: both; and packed super-rows of 48 / L channels
+for L in {4, 8, 12, 16, 24}, including a partial last group), ragged batch tiles (B not a multiple of 128), K > L, even and odd
 taps, H above the 256-channel TMA box limit of the CUDA-core tiles, and the
 three Toeplitz operand regimes (one or two resident channels per CTA, or a
 rebuild per tile).
@@ -47,10 +48,18 @@ SHAPES = [
     (1000, 96, 48, 48),   # grid 144: two resident channels per CTA
     (257, 5, 32, 32),     # one 128-B box
     (129, 7, 20, 7),      # 128-B box, L = 20 (12 zero columns)
-    (64, 9, 16, 16),      # one 64-B box
+    (100, 7, 28, 28),     # 128-B box, L = 28
+    (64, 3, 36, 36),      # both boxes, L = 36
+    # packed super-rows of 48 / L channels (2-D maps, block-diagonal Toeplitz)
+    (500, 10, 24, 24),    # 2 channels per super-row
+    (777, 13, 16, 9),     # 3 per super-row, last group partial (13 = 4 * 3 + 1)
+    (64, 9, 16, 16),
+    (260, 50, 12, 12),    # 4 per super-row, last group partial
     (33, 4, 12, 5),
-    (3, 2, 8, 48),        # K > L
-    (1, 1, 4, 1),
+    (3, 2, 8, 48),        # 6 per super-row, K > L, one partial group
+    (129, 31, 8, 3),
+    (1, 1, 4, 1),         # 12 per super-row, one channel present
+    (300, 40, 4, 4),
 ]
 
 

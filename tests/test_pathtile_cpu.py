@@ -122,3 +122,65 @@ def test_case_seed_rule():
     import zlib
 
     assert pt.case_seed(42, c) == 42 + zlib.crc32(c.config_id.encode())
+
+
+def _erow(cid, L, K, phase, engine, ms):
+    return {"config_id": cid, "L": L, "K": K, "phase": phase, "engine": engine, "mean_ms": ms}
+
+
+def test_select_engines_per_class_on_summed_latency():
+    rows = []
+    # heavy shapes (L = K = 48): tensor faster in total although slower on h2
+    for cid, f, t in (("h1", 1.0, 0.8), ("h2", 1.0, 1.1)):
+        for p in pt.ENGINE_PATHS:
+            rows += [_erow(cid, 48, 48, p, "ffma", f), _erow(cid, 48, 48, p, "tensor", t)]
+    # light shape (K = 3): FFMA faster
+    for p in pt.ENGINE_PATHS:
+        rows += [_erow("l1", 48, 3, p, "ffma", 0.5), _erow("l1", 48, 3, p, "tensor", 0.6)]
+    eng = pt.select_engines(rows)
+    assert eng["fwd"]["heavy"] == "tensor" and eng["bwd_input"]["heavy"] == "tensor"
+    assert eng["fwd"]["light"] == "ffma"
+    assert eng["fwd"]["medium"] == "ffma"  # no shapes: stays on the CUDA-core kernels
+    assert all(v == "ffma" for v in eng["bwd_weight"].values())
+    reg = {r["config_id"]: r for r in pt.engine_regret(rows, eng)}
+    assert reg["h2"]["regret_pct"] == pytest.approx(10.0)
+    assert reg["h1"]["regret_pct"] == pytest.approx(0.0)
+    assert reg["h1"]["gain_vs_ffma_pct"] == pytest.approx(25.0)
+
+
+def test_select_engines_tie_keeps_ffma():
+    rows = [_erow("s", 32, 32, p, e, 1.0) for p in pt.ENGINE_PATHS for e in pt.ENGINES]
+    assert pt.select_engines(rows)["fwd"]["heavy"] == "ffma"
+
+
+def test_tensor_engine_applicability():
+    assert pt.tensor_applicable(48) and pt.tensor_applicable(4)
+    assert not pt.tensor_applicable(37) and not pt.tensor_applicable(2)
+
+
+ENGINE_ROW = r"\{(\d), (\d), (\d)\},\s+// (FWD|DX|DK)"
+
+
+def test_render_header_engine_table():
+    pol = {p: {c: (128, 3, 2, 1) for c in pt.CLASSES} for p in pt.PATHS}
+    eng = {p: {c: "ffma" for c in pt.CLASSES} for p in pt.PATHS}
+    eng["fwd"]["heavy"] = "tensor"
+    eng["bwd_input"]["medium"] = "tensor"
+    rows = re.findall(ENGINE_ROW, pt.render_header(pol, "t", eng))
+    assert rows == [("0", "0", "1", "FWD"), ("0", "1", "0", "DX"), ("0", "0", "0", "DK")]
+    assert re.findall(ENGINE_ROW, pt.render_header(pol, "t"))[0][:3] == ("0", "0", "0")
+    assert len(re.findall(ENGINE_ROW, pt.HEADER.read_text())) == 3
+
+
+def test_apply_engines_rewrites_only_the_engine_table():
+    text = pt.HEADER.read_text()
+    eng = {p: {c: "ffma" for c in pt.CLASSES} for p in pt.PATHS}
+    eng["fwd"]["light"] = eng["bwd_input"]["heavy"] = "tensor"
+    out = pt.apply_engines_to_header(text, eng)
+    assert re.findall(ENGINE_ROW, out) == [("1", "0", "0", "FWD"), ("0", "0", "1", "DX"), ("0", "0", "0", "DK")]
+    assert re.findall(HEADER_ROW, out) == re.findall(HEADER_ROW, text)
+    assert out.count("constexpr int kFrozenEngine") == 1
+
+
+def test_tensor_applicable_means_full_tiles():
+    assert [L for L in range(1, 49) if pt.tensor_applicable(L)] == [4, 8, 12, 16, 24, 48]
