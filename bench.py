@@ -292,8 +292,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                                             float(sm_mhz))
     roof_ms = runtime.roofline_ms(B, H, L, K, hbm, fma_peak)
     traffic = load_traffic()
-    kernel_names = {"fwd": "conv_rows_kernel<48,48,FWD,TMA3D>", "bwd_input": "conv_rows_kernel<48,48,DX,TMA3D>",
-                    "bwd_weight": "dk_rows_kernel<48,48,TMA3D> + dk_reduce_kernel"}
+    engines = {p: ops.config(p, B, H, L, K)["engine"] for p in ("fwd", "bwd_input", "bwd_weight")}
+    kernel_names = {
+        "fwd": ("tc_conv_kernel<FWD> (tcgen05, 3xTF32, A in TMEM)" if engines["fwd"] == "tensor"
+                else "conv_rows_kernel<48,48,FWD,TMA3D>"),
+        "bwd_input": ("tc_conv_kernel<DX> (tcgen05, 3xTF32, A in TMEM)" if engines["bwd_input"] == "tensor"
+                      else "conv_rows_kernel<48,48,DX,TMA3D>"),
+        "bwd_weight": "dk_rows_kernel<48,48,TMA3D> + dk_reduce_kernel",
+    }
     result = {
         "metric": METRIC,
         "value": total_bytes / (step_ms / 1e3) / 1e9,
@@ -312,6 +318,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "B_per_gpu": B, "global_batch": B * world, "H": H, "L": L, "K": K,
             "parallelism": f"dp{world}" + (" + NCCL all_reduce(dK)" if world > 1 else ""),
             "dk_mode": "deterministic two-pass",
+            "engines": engines,
             "l2": "inputs larger than L2 (402,653,184 B per activation tensor vs 126 MB L2)",
         },
         "aggregate_ms": sum(phase_ms.values()),

@@ -28,8 +28,8 @@ constexpr LaunchCfg kFrozenCfg[3][3] = {
 // kFrozenEngine[path][class]: PT_ENGINE_FFMA (0) or PT_ENGINE_TENSOR (1); the
 // tensor engine only ever applies to FWD/DX at L % 4 == 0.
 constexpr int kFrozenEngine[3][3] = {
-    {0, 0, 0},  // FWD: light, medium, heavy
-    {0, 0, 0},  // DX: light, medium, heavy
+    {1, 1, 1},  // FWD: light, medium, heavy
+    {1, 1, 1},  // DX: light, medium, heavy
     {0, 0, 0},  // DK: light, medium, heavy
 };
 
