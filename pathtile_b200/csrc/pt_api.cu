@@ -26,6 +26,11 @@ constexpr int kMaxDevices = 64;
 constexpr int kGenericRows = 128;
 
 thread_local int t_last_cuda_error = 0;
+// Device whose primary context this host thread has made current.  Driver
+// calls such as cuTensorMapEncodeTiled need a current context, which a fresh
+// thread (autograd's backward worker, a data-loader thread) does not have
+// until some runtime call binds it.
+thread_local int t_bound_device = -1;
 
 struct DeviceInfo {
   bool ready = false;
@@ -81,6 +86,10 @@ int current_device(DeviceInfo*& di) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
   if (dev < 0 || dev >= kMaxDevices) return PT_ERR_DEVICE;
+  if (t_bound_device != dev) {
+    if ((e = cudaSetDevice(dev)) != cudaSuccess) return cuda_fail(e);  // binds the primary context
+    t_bound_device = dev;
+  }
   std::lock_guard<std::mutex> lk(g_mu);
   DeviceInfo& d = g_dev[dev];
   if (!d.ready) {
