@@ -61,7 +61,7 @@ extern "C" {
 
 /* Engines (pt_set_engine, pt_config out[6]). */
 #define PT_ENGINE_FFMA 0    /* CUDA-core FP32 FMA kernels: every path and shape */
-#define PT_ENGINE_TENSOR 1  /* tcgen05 tensor cores, FP32-accurate 3xTF32 split: FWD/DX with L % 4 == 0 */
+#define PT_ENGINE_TENSOR 1  /* tcgen05 tensor cores, FP32-accurate 3xTF32 split, L % 4 == 0 */
 
 /*
  * Forward pass.  Replaces the reference launch of dwconv1d_warptile_fwd via
@@ -148,9 +148,11 @@ PT_API int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_s
 
 /*
  * Engine of `path` for all shapes: PT_ENGINE_FFMA, PT_ENGINE_TENSOR, or -1 to
- * restore the frozen table.  PT_ENGINE_TENSOR applies to FWD and DX at L % 4 ==
- * 0 only; other shapes keep the FFMA kernels.  No reference counterpart (the
- * reference has CUDA-core kernels only).  Not thread-safe with concurrent launches.
+ * restore the frozen table.  PT_ENGINE_TENSOR applies at L % 4 == 0 only (and,
+ * for dK, where every CTA's channel groups stay resident: the grid has a
+ * multiple of half the group count CTAs); other shapes keep the FFMA kernels.
+ * No reference counterpart (the reference has CUDA-core kernels only).  Not
+ * thread-safe with concurrent launches.
  */
 PT_API int pt_set_engine(int path, int engine);
 

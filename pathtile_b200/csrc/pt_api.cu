@@ -178,24 +178,33 @@ int tensor_groups(int H, int L) {
   return (H + hc - 1) / hc;
 }
 
-long long tensor_tiles(int B, int groups) {
-  return static_cast<long long>((B + pt::tc::kRowsPerTile - 1) / pt::tc::kRowsPerTile) * groups;
+// Tiles of the tensor-core kernels: 128 batch rows (FWD/DX) or 64 (dK) of one group.
+int tensor_rows(int path) { return path == PT_PATH_DK ? pt::tc::kDkRowsPerTile : pt::tc::kRowsPerTile; }
+
+long long tensor_tiles(int path, int B, int groups) {
+  const int r = tensor_rows(path);
+  return static_cast<long long>((B + r - 1) / r) * groups;
 }
 
-// Engine of a path at a shape: PT_ENGINE_TENSOR (tcgen05, FWD/DX with L % 4 == 0
-// and a TMA encoder) or PT_ENGINE_FFMA (CUDA-core kernels, every shape).  The
-// frozen table's tensor choice applies only to full tiles (48 % L == 0: one
+// Engine of a path at a shape: PT_ENGINE_TENSOR (tcgen05, L % 4 == 0 and a TMA
+// encoder) or PT_ENGINE_FFMA (CUDA-core kernels, every shape).  The frozen
+// table's tensor choice applies only to full tiles (48 % L == 0: one
 // 48-column channel or 48 / L packed channels per tile row; partially filled
-// tiles measured faster on the FFMA kernels) and needs a grid with resident
-// Toeplitz operands; an explicit pt_set_engine override needs neither.
+// tiles measured faster on the FFMA kernels) and needs a grid in which every
+// CTA visits at most two channel groups; an explicit pt_set_engine override
+// needs neither for FWD/DX (they rebuild the Toeplitz operand per tile
+// otherwise), while dK always needs its accumulators resident.
 int engine_for(int path, int B, int H, int L, int K, int sm_count) {
-  if (path == PT_PATH_DK || L % 4 != 0 || g_encode == nullptr) return PT_ENGINE_FFMA;
-  if (g_engine_override[path] >= 0) return g_engine_override[path];
+  if (L % 4 != 0 || g_encode == nullptr) return PT_ENGINE_FFMA;
+  const int groups = tensor_groups(H, L);
+  int G = 0, period = 0;
+  tensor_grid(groups, tensor_tiles(path, B, groups), sm_count > 0 ? sm_count : 148, G, period);
+  if (g_engine_override[path] >= 0) {
+    if (path == PT_PATH_DK && period == 0) return PT_ENGINE_FFMA;
+    return g_engine_override[path];
+  }
   if (48 % L != 0 || pt::kFrozenEngine[path][intensity_class(L, K)] != PT_ENGINE_TENSOR)
     return PT_ENGINE_FFMA;
-  int G = 0, period = 0;
-  const int groups = tensor_groups(H, L);
-  tensor_grid(groups, tensor_tiles(B, groups), sm_count > 0 ? sm_count : 148, G, period);
   return period > 0 ? PT_ENGINE_TENSOR : PT_ENGINE_FFMA;
 }
 
@@ -319,18 +328,19 @@ int plan_tensor(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   g.L = L;
   g.K = K;
   p.lay = pt::tc::layout_for(L);
-  p.func = pt::tc::conv_func(path, p.lay);
-  p.smem = pt::tc::conv_smem(p.lay);
-  p.threads = pt::tc::kThreads;
+  p.func = (path == PT_PATH_DK) ? pt::tc::dk_func(p.lay) : pt::tc::conv_func(path, p.lay);
+  p.smem = (path == PT_PATH_DK) ? pt::tc::dk_smem(p.lay) : pt::tc::conv_smem(p.lay);
+  p.threads = (path == PT_PATH_DK) ? pt::tc::kDkThreads : pt::tc::kThreads;
   if (!p.func || static_cast<long long>(p.smem) > di.max_smem) return PT_ERR_UNSUPPORTED;
   int rc = ensure_smem_attr(di, p.func, p.smem);
   if (rc != PT_OK) return rc;
   p.groups = tensor_groups(H, L);
-  const long long tiles = tensor_tiles(B, p.groups);
-  g.Q = static_cast<int>(tiles);  // tiles of 128 batch rows of one channel group
+  const long long tiles = tensor_tiles(path, B, p.groups);
+  g.Q = static_cast<int>(tiles);  // tiles of 128 (64 for dK) batch rows of one channel group
   tensor_grid(p.groups, tiles, di.sm_count, g.G, p.period);
+  if (path == PT_PATH_DK && p.period == 0) return PT_ERR_UNSUPPORTED;
   g.Th = 1;
-  g.Tb = pt::tc::kRowsPerTile;
+  g.Tb = tensor_rows(path);
   g.nhb = H;
   p.exact = true;
   p.tensor = true;
@@ -386,20 +396,21 @@ int encode_pair(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p, C
 // Tensor map of the tensor-core path: box of `cols` floats x 128 batch rows
 // with the 128-B (cols 32) or 64-B (cols 16) swizzle; 3-D over (L, H, B) with
 // one channel per box, or 2-D over [B, H*L] for packed super-rows.
-int encode_tc_tmap(CUtensorMap* tm, const float* base, int B, int H, int L, int cols, bool packed) {
+int encode_tc_tmap(CUtensorMap* tm, const float* base, int B, int H, int L, int cols, bool packed,
+                   int rows = pt::tc::kRowsPerTile, bool atom32 = false) {
   cuuint64_t dims3[3] = {static_cast<cuuint64_t>(L), static_cast<cuuint64_t>(H),
                          static_cast<cuuint64_t>(B)};
   cuuint64_t strides3[2] = {static_cast<cuuint64_t>(L) * 4, static_cast<cuuint64_t>(L) * H * 4};
-  cuuint32_t box3[3] = {static_cast<cuuint32_t>(cols), 1u,
-                        static_cast<cuuint32_t>(pt::tc::kRowsPerTile)};
+  cuuint32_t box3[3] = {static_cast<cuuint32_t>(cols), 1u, static_cast<cuuint32_t>(rows)};
   cuuint64_t dims2[2] = {static_cast<cuuint64_t>(L) * H, static_cast<cuuint64_t>(B)};
   cuuint64_t strides2[1] = {static_cast<cuuint64_t>(L) * H * 4};
-  cuuint32_t box2[2] = {static_cast<cuuint32_t>(cols), static_cast<cuuint32_t>(pt::tc::kRowsPerTile)};
+  cuuint32_t box2[2] = {static_cast<cuuint32_t>(cols), static_cast<cuuint32_t>(rows)};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, packed ? 2 : 3, const_cast<float*>(base),
                         packed ? dims2 : dims3, packed ? strides2 : strides3, packed ? box2 : box3, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                               : (cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B),
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     t_last_cuda_error = static_cast<int>(r);
@@ -432,6 +443,47 @@ int launch_tensor(const Plan& p, const float* in, const float* taps, float* out,
                   &groups, &n_tiles, &period, &err};
   const cudaError_t ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
   if (ce != cudaSuccess) return cuda_fail(ce);
+  return PT_OK;
+}
+
+// Workspace of the tensor-core dK: per CTA and resident group, Hc*K partials,
+// then the group id of each (CTA, slot).
+size_t tensor_dk_ws_bytes(const Plan& p) {
+  const size_t slots = static_cast<size_t>(p.g.G) * pt::tc::kDkMaxGroups;
+  const size_t part = (slots * p.lay.hc * p.g.K * sizeof(float) + 255) / 256 * 256;
+  return part + slots * sizeof(int);
+}
+
+int launch_tensor_dk(const Plan& p, const float* dy, const float* x, float* dk, int mode, void* ws,
+                     unsigned* err, cudaStream_t stream) {
+  const pt::TileGeom& g = p.g;
+  const int lb = p.lay.lb;
+  const bool packed = p.lay.packed;
+  const int rows = pt::tc::kDkRowsPerTile;
+  CUtensorMap dy128, dy64, x32b;
+  std::memset(&dy128, 0, sizeof(dy128));
+  std::memset(&dy64, 0, sizeof(dy64));
+  std::memset(&x32b, 0, sizeof(x32b));
+  int rc = PT_OK;
+  if (lb >= 2 && (rc = encode_tc_tmap(&dy128, dy, g.B, g.H, g.L, 32, packed, rows)) != PT_OK) return rc;
+  if ((lb & 1) && (rc = encode_tc_tmap(&dy64, dy, g.B, g.H, g.L, 16, packed, rows)) != PT_OK) return rc;
+  // x feeds the MMAs as an MN-major tf32 operand: 32-column boxes, 128-B swizzle of 32-B atoms.
+  if ((rc = encode_tc_tmap(&x32b, x, g.B, g.H, g.L, 32, packed, rows, true)) != PT_OK) return rc;
+  const int atomic = (mode == PT_DK_ATOMIC) ? 1 : 0;
+  float* out = atomic ? dk : static_cast<float*>(ws);
+  const size_t slots = static_cast<size_t>(g.G) * pt::tc::kDkMaxGroups;
+  const size_t part_bytes = (slots * p.lay.hc * g.K * sizeof(float) + 255) / 256 * 256;
+  int* group_of = atomic ? nullptr : reinterpret_cast<int*>(static_cast<unsigned char*>(ws) + part_bytes);
+  int H = g.H, L = g.L, K = g.K, hc = p.lay.hc, groups = p.groups, n_tiles = g.Q, period = p.period;
+  void* args[] = {&dy128, &dy64, &x32b, &out, &group_of, &H, &L, &K, &hc, &groups, &n_tiles, &period,
+                  const_cast<int*>(&atomic), &err};
+  cudaError_t ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  if (!atomic) {
+    pt::tc::dk_reduce(out, group_of, static_cast<int>(slots), H, K, hc, dk,
+                      mode == PT_DK_DETERMINISTIC_ACCUMULATE ? 1 : 0, stream);
+    if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_fail(ce);
+  }
   return PT_OK;
 }
 
@@ -507,7 +559,7 @@ size_t pt_dk_workspace_bytes(int B, int H, int L, int K) {
   if (current_device(di) != PT_OK) return 0;
   Plan p;
   if (plan(PT_PATH_DK, B, H, L, K, *di, p) != PT_OK) return 0;
-  return dk_ws_bytes(p);
+  return p.tensor ? tensor_dk_ws_bytes(p) : dk_ws_bytes(p);
 }
 
 int pt_dk(const float* dy, const float* x, float* dk, int B, int H, int L, int K, int mode, void* ws,
@@ -530,6 +582,13 @@ int pt_dk(const float* dy, const float* x, float* dk, int B, int H, int L, int K
   Plan p;
   if ((rc = plan(PT_PATH_DK, B, H, L, K, *di, p)) != PT_OK) return rc;
   const int atomic_mode = (mode == PT_DK_ATOMIC) ? 1 : 0;
+  if (p.tensor) {
+    if (!atomic_mode) {
+      if (!ws || ws_bytes < tensor_dk_ws_bytes(p)) return PT_ERR_WORKSPACE;
+      if (!aligned16(ws)) return PT_ERR_ALIGN;
+    }
+    return launch_tensor_dk(p, dy, x, dk, mode, ws, di->err, stream);
+  }
   float* dst = dk;
   if (!atomic_mode) {
     if (!ws || ws_bytes < dk_ws_bytes(p)) return PT_ERR_WORKSPACE;
@@ -652,7 +711,6 @@ int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm, int 
 int pt_set_engine(int path, int engine) {
   if (path < 0 || path > 2) return PT_ERR_ARGS;
   if (engine != -1 && engine != PT_ENGINE_FFMA && engine != PT_ENGINE_TENSOR) return PT_ERR_ARGS;
-  if (path == PT_PATH_DK && engine == PT_ENGINE_TENSOR) return PT_ERR_UNSUPPORTED;
   g_engine_override[path] = engine;
   return PT_OK;
 }

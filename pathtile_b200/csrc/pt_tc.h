@@ -32,3 +32,22 @@ size_t conv_smem(const Layout& lay);
 
 }  // namespace tc
 }  // namespace pt
+
+namespace pt {
+namespace tc {
+
+constexpr int kDkRowsPerTile = 64;
+constexpr int kDkThreads = 320;
+constexpr int kDkMaxGroups = 2;
+
+// tcgen05 dK kernel for a layout, or nullptr.
+const void* dk_func(const Layout& lay);
+size_t dk_smem(const Layout& lay);
+
+// dk[h][j] (= or +=) the sum, in CTA order, of the partials of every CTA
+// accumulator that held h's channel group.
+void dk_reduce(const float* partial, const int* group_of, int n_slots, int H, int K, int hc, float* dk,
+               int accumulate, void* stream);
+
+}  // namespace tc
+}  // namespace pt

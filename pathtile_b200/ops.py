@@ -242,7 +242,8 @@ ENGINES = ("ffma", "tensor")
 
 def set_engine(path: str, engine: str | None) -> None:
     """Select the engine of one path for all shapes: "ffma" (CUDA-core kernels), "tensor"
-    (tcgen05, FWD/DX at L % 4 == 0; other shapes stay on FFMA), or None for the frozen table."""
+    (tcgen05 at L % 4 == 0; other shapes, and dK shapes whose accumulators cannot stay
+    resident, stay on FFMA), or None for the frozen table."""
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
     eng = -1 if engine is None else ENGINES.index(engine)
     _lib.check(_lib.load().pt_set_engine(code, eng), "pt_set_engine")

@@ -1,7 +1,8 @@
-"""GPU parity of the tensor-core FWD / dX kernels (tcgen05, 3xTF32 split).
+"""GPU parity of the tensor-core FWD / dX / dK kernels (tcgen05, 3xTF32 split).
 
 The tensor engine must meet the same FP32 bar as the CUDA-core kernels:
-rtol = atol = 1e-5 against the FP64 C oracle, on every layout class of the
+rtol = atol = 1e-5 against the FP64 C oracle for FWD / dX and 1e-4 relative
+of the FP64 dK (|dK - dK64| <= 1e-4 |dK64| + 1e-4 max|dK64|), on every layout class of the
 engine (one channel per tile row with L <= 16: one 64-B swizzled box, L <=
 32: one 128-B box, L <= 48: both; and packed super-rows of 48 / L channels
 for L in {4, 8, 12, 16, 24}, including a partial last group), ragged batch tiles (B not a multiple of 128), K > L, even and odd
@@ -23,15 +24,24 @@ pytestmark = pytest.mark.gpu
 FWD_TOL = dict(rtol=1e-5, atol=1e-5)
 
 
+DK_RTOL = 1e-4
+PATHS = ("fwd", "bwd_input", "bwd_weight")
+
+
+def assert_dk_close(got: np.ndarray, ref64: np.ndarray) -> None:
+    scale = float(np.abs(ref64).max()) if ref64.size else 0.0
+    np.testing.assert_allclose(got, ref64, rtol=DK_RTOL, atol=DK_RTOL * max(scale, 1e-30))
+
+
 @pytest.fixture
 def tensor_engine(cuda_device):
-    ops.set_engine("fwd", "tensor")
-    ops.set_engine("bwd_input", "tensor")
+    for p in PATHS:
+        ops.set_engine(p, "tensor")
     try:
         yield cuda_device
     finally:
-        ops.set_engine("fwd", None)
-        ops.set_engine("bwd_input", None)
+        for p in PATHS:
+            ops.set_engine(p, None)
 
 
 def _inputs(B, H, L, K, seed, device):
@@ -130,6 +140,51 @@ def test_tensor_engine_is_deterministic_and_stream_ordered(tensor_engine):
 
 def test_tensor_engine_shapes_it_does_not_cover_stay_on_ffma(tensor_engine):
     assert ops.config("fwd", 64, 8, 37, 13)["engine"] == "ffma"  # L % 4 != 0
-    assert ops.config("bwd_weight", 64, 8, 48, 48)["engine"] == "ffma"  # dK has no tensor kernel
-    with pytest.raises(Exception):
-        ops.set_engine("bwd_weight", "tensor")
+    assert ops.config("bwd_weight", 64, 8, 37, 13)["engine"] == "ffma"
+    # 300 groups on 148 SMs: no grid keeps dK's accumulators resident
+    assert ops.config("bwd_weight", 200, 300, 48, 47)["engine"] == "ffma"
+    assert ops.config("bwd_weight", 16384, 128, 48, 48)["engine"] == "tensor"
+
+
+@pytest.mark.parametrize("mode", ["deterministic", "atomic"])
+@pytest.mark.parametrize("B,H,L,K", SHAPES)
+def test_tensor_dk_against_fp64_oracle(tensor_engine, B, H, L, K, mode):
+    dev = tensor_engine
+    x, k, dy, cpu = _inputs(B, H, L, K, 404, dev)
+    gk = torch.zeros_like(k) if mode == "atomic" else torch.full_like(k, float("nan"))
+    ops.dk(dy, x, gk, mode=mode)
+    torch.cuda.synchronize()
+    assert ops.device_error(clear=True) == 0, "a kernel wait expired"
+    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+
+
+def test_tensor_dk_primary_workload(tensor_engine):
+    dev = tensor_engine
+    B, H, L, K = 16384, 128, 48, 48
+    x, k, dy, cpu = _inputs(B, H, L, K, 42, dev)
+    gk = torch.empty_like(k)
+    ops.dk(dy, x, gk)
+    torch.cuda.synchronize()
+    assert ops.device_error(clear=True) == 0
+    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+    # <dK(dy, x), k> = <FWD(x), dy> (size-independent identity)
+    y = ops.fwd(x, k)
+    a = float((gk.double() * k.double()).sum())
+    b = float((y.double() * dy.double()).sum())
+    assert abs(a - b) <= 1e-6 * (float(y.double().abs().sum()) + 1.0)
+
+
+def test_tensor_dk_deterministic_and_accumulate(tensor_engine):
+    dev = tensor_engine
+    x, k, dy, cpu = _inputs(4096, 96, 48, 48, 8, dev)
+    outs = []
+    for _ in range(3):
+        gk = torch.empty_like(k)
+        ops.dk(dy, x, gk, mode="deterministic")
+        outs.append(gk.clone())
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    gk = torch.ones_like(k)
+    ops.dk(dy, x, gk, mode="deterministic", accumulate=True)
+    torch.cuda.synchronize()
+    assert ops.device_error(clear=True) == 0
+    assert_dk_close(gk.cpu().numpy() - 1.0, c_oracle.dk(cpu[2], cpu[0], 48))
