@@ -457,9 +457,9 @@ size_t tensor_dk_ws_bytes(const Plan& p) {
 int launch_tensor_dk(const Plan& p, const float* dy, const float* x, float* dk, int mode, void* ws,
                      unsigned* err, cudaStream_t stream) {
   const pt::TileGeom& g = p.g;
-  const int lb = p.lay.lb;
   const bool packed = p.lay.packed;
   const int rows = pt::tc::kDkRowsPerTile;
+  const int lb = p.lay.lb;
   CUtensorMap dy128, dy64, x32b;
   std::memset(&dy128, 0, sizeof(dy128));
   std::memset(&dy64, 0, sizeof(dy64));

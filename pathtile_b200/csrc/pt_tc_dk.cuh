@@ -10,29 +10,34 @@
 // of a channel group, so the per-tile work is: TMA the dy and x tiles, split,
 // MMA; the diagonal sums run once per CTA at the end.
 //
-// FP32 accuracy with TF32 MMAs: dy and x are split as hi + lo (TF32 round to
-// nearest of v, then of v - hi).  A (in tensor memory, lane = row) holds the
-// dy columns with hi and lo interleaved (lane 2t = dy_hi column t, lane 2t+1
-// = dy_lo column t); B (shared memory, MN-major) holds [x_hi | x_lo] along
-// N.  One M = 128 MMA per 8 batch rows then yields all four products, and
-// C[t][s] = D[2t][hi(s)] + D[2t][lo(s)] + D[2t+1][hi(s)] + D[2t+1][lo(s)]
-// (the lo*lo term is kept; it only adds accuracy).
+// FP32 accuracy with TF32 MMAs: the MMA reads a TF32 operand from an FP32
+// word by ignoring its low 13 mantissa bits, so v = hi + lo with hi = v as
+// stored (read as trunc(v)) and lo = v - trunc(v) (exact in FP32, read as
+// trunc(lo)); the split costs two instructions per value and no store for
+// hi.  A (in tensor memory, lane = row) holds the dy columns: lanes 0..63 =
+// dy_hi column t = lane, lanes 64..127 = dy_lo column t = lane - 64; B
+// (shared memory, MN-major) holds [x_hi | x_lo] along N.  One M = 128 MMA per
+// 8 batch rows then yields all four products, and C[t][s] = D[t][hi(s)] +
+// D[t][lo(s)] + D[64+t][hi(s)] + D[64+t][lo(s)] (the lo*lo term is kept).
+// Per product the error is below about 2^-19 of |dy x| (the truncation of lo),
+// far inside the 1e-4 relative bar of dK.
 //
 // B comes straight from TMA: MN-major tf32 operands need the 128-byte
 // swizzle with 32-byte atoms (4 batch rows of 128 bytes per atom), which the
 // TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B; x is loaded as one or
-// two boxes of 32 columns, split in place into x_hi, and x_lo goes to the
-// same offsets one block row further, so the four (or two) 32-column blocks
-// sit at a uniform stride (the descriptor's leading offset).  The dy tile is
+// two boxes of 32 columns (x_hi), and x_lo goes to the same offsets one block
+// row further, so the four (or two) 32-column blocks sit at a uniform stride
+// (the descriptor's leading offset).  The dy tile is
 // only read by the converters (128-B and 64-B swizzled boxes as in FWD/DX).
 //
 // Roles (320 threads, one CTA per SM):
 //   warp 0      TMA producer (dy and x tiles, ring of 5 stages)
 //   warp 1      allocates 512 TMEM columns (3 A slots of 64 columns, 2 accumulators
 //               of 128); lane 0 issues the MMAs and commits them
-//   warps 2-5   A converters, one per TMEM lane quadrant: lane pairs read one dy
-//               column (a broadcast), split it, write 64 columns of their rows
-//   warps 6-9   B converters: split the x tile into hi (in place) and lo
+//   warps 2-5   A converters, one per TMEM lane quadrant: each lane reads one dy
+//               column of the tile and writes it (hi rows) or its lo part (lo rows)
+//               as 64 TMEM columns
+//   warps 6-9   B converters: write x_lo beside the x tile (x_hi is the tile itself)
 //   then warps 2-9 run the epilogue: accumulators -> shared memory -> diagonal
 //   sums -> one partial per (CTA, group, channel, tap), or float atomics.
 // The channel groups a CTA visits must be resident (period 1 or 2); the host
@@ -74,7 +79,7 @@ struct DkGeo {
   static constexpr int SMEM = OFF_TMEM + 16 + 1024;
   static_assert(DY_TILE % 1024 == 0 && DY_BOX64 % 1024 == 0 && STAGE % 1024 == 0,
                 "swizzled tiles start on 1024-byte boundaries");
-  static_assert(W * W * 4 <= DK_STAGES * STAGE, "epilogue scratch fits the idle ring");
+  static_assert(2 * 64 * W * 4 <= DK_STAGES * STAGE, "epilogue scratch fits the idle ring");
 };
 
 // Shared-memory descriptor of an MN-major tf32 operand in the 128-byte swizzle
@@ -95,15 +100,9 @@ constexpr uint32_t idesc_tf32_m128_bmn() {
          (static_cast<uint32_t>(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ bool lo_row_of(int lane) { return (lane & 1) != 0; }
-
-// Byte offset of column col of row r in the dy tile (128-B box, then 64-B box).
-template <int LB>
-__device__ __forceinline__ uint32_t dk_dy_off(int r, int col) {
-  using GG = DkGeo<LB>;
-  if (LB >= 2 && col < 32) return sw128_off(r, col >> 2) + 4u * (col & 3);
-  const int c = col - GG::S64;
-  return GG::DY_BOX64 + sw64_off(r, c >> 2) + 4u * (c & 3);
+// lo part of v in the truncation split: v - (v with its low 13 mantissa bits cleared).
+__device__ __forceinline__ float tf32_trunc_lo(float v) {
+  return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
 }
 
 // n_tiles = ceil(B / 64) * Hg; tile tau: group tau % Hg, batch rows [64 * (tau / Hg), +64).
@@ -141,7 +140,7 @@ __global__ void __launch_bounds__(DK_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < DK_STAGES; ++s) {
       mbar_init(full(s), 1);
-      mbar_init(conv(s), 256);
+      mbar_init(conv(s), 8);  // one arrival per converter warp
       mbar_init(sfree(s), 1);
     }
     for (int a = 0; a < DK_A_SLOTS; ++a) mbar_init(afree(a), 1);
@@ -217,33 +216,46 @@ __global__ void __launch_bounds__(DK_THREADS, 1)
   } else {
     const int ct = static_cast<int>(threadIdx.x) - 64;  // 0..255
     if (warp < 6) {
-      // ---------------- A converters: dy column -> TMEM rows 2t (hi), 2t+1 (lo) ----------------
+      // ---------------- A converters: dy column t -> TMEM row t (hi) or 64 + t (lo) ----------------
       const int quad = warp & 3;
-      const int t = 16 * quad + (lane >> 1);  // dy column of this lane pair
-      const bool lo_row = lane & 1;
+      const int t = 32 * (quad & 1) + lane;  // dy column of this lane
+      const bool lo_rows = quad >= 2;        // warp-uniform
       const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
       for (int i = 0; i < n_it; ++i) {
         const int s = i % DK_STAGES, a = i % DK_A_SLOTS;
-        if (i >= DK_A_SLOTS &&
-            !mbar_wait_bounded(afree(a), ((i / DK_A_SLOTS) - 1) & 1, err, DEVERR_TC_CONVERT)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait_bounded(full(s), (i / DK_STAGES) & 1, err, DEVERR_TIMEOUT_FULL)) {
+        if (i >= DK_A_SLOTS) ok = mbar_wait_bounded(afree(a), ((i / DK_A_SLOTS) - 1) & 1, err, DEVERR_TC_CONVERT);
+        if (ok) ok = mbar_wait_bounded(full(s), (i / DK_STAGES) & 1, err, DEVERR_TIMEOUT_FULL);
+        if (!__all_sync(0xffffffffu, ok)) {  // the warp leaves together (it arrives as one)
           ok = false;
           break;
         }
         // Every lane executes the (warp-collective) TMEM stores; columns past the
         // super-row width hold zeros and their accumulator rows are never read.
+        // Row r of column t sits at r * pitch + base[r % 8] in its box: the
+        // few bases are hoisted, so the 64 loads take immediate offsets.
         const unsigned char* dyt = sm + s * GG::STAGE;
         float v[DK_ROWS];
+        if (LB >= 2 && (quad & 1) == 0) {  // columns 0..31: 128-B box
+          uint32_t bse[8];
 #pragma unroll
-        for (int r = 0; r < DK_ROWS; ++r)
-          v[r] = (t < W) ? *reinterpret_cast<const float*>(dyt + dk_dy_off<LB>(r, t)) : 0.f;
+          for (int k = 0; k < 8; ++k) bse[k] = sw128_off(k, t >> 2) - 128u * k + 4u * (t & 3);
 #pragma unroll
-        for (int r = 0; r < DK_ROWS; ++r) {
-          const float hi = tf32_round(v[r]);
-          v[r] = lo_row ? tf32_round(v[r] - hi) : hi;
+          for (int r = 0; r < DK_ROWS; ++r)
+            v[r] = *reinterpret_cast<const float*>(dyt + 128u * r + bse[r & 7]);
+        } else {  // the 64-B box (columns 32..47, or 0..15 when W = 16)
+          const int c = t - GG::S64;
+          uint32_t bse[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            bse[k] = GG::DY_BOX64 + sw64_off(k, (c >> 2) & 3) - 64u * k + 4u * (c & 3);
+          const bool in = (t < W) && (LB & 1);
+#pragma unroll
+          for (int r = 0; r < DK_ROWS; ++r)
+            v[r] = in ? *reinterpret_cast<const float*>(dyt + 64u * r + bse[r & 7]) : 0.f;
+        }
+        if (lo_rows) {
+#pragma unroll
+          for (int r = 0; r < DK_ROWS; ++r) v[r] = tf32_trunc_lo(v[r]);
         }
         const uint32_t acol = tmem + lane_base + static_cast<uint32_t>(a * DK_A_COLS);
 #pragma unroll
@@ -251,41 +263,43 @@ __global__ void __launch_bounds__(DK_THREADS, 1)
         tmem_wait_st();
         tc_fence_before();
         fence_proxy_async_smem();  // dy reads ordered before the stage's next TMA write
-        mbar_arrive(conv(s));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(conv(s));
       }
     } else {
-      // ---------------- B converters: x blocks -> x_hi (in place) | x_lo ----------------
+      // ---------------- B converters: x blocks (x_hi as loaded) -> x_lo ----------------
       // Element-wise, so the swizzled layout needs no decoding: consecutive
       // threads take consecutive 16-byte chunks (conflict-free).
       const int bt = ct - 128;  // 0..127
       for (int i = 0; i < n_it; ++i) {
         const int s = i % DK_STAGES;
-        if (!mbar_wait_bounded(full(s), (i / DK_STAGES) & 1, err, DEVERR_TIMEOUT_FULL)) {
+        ok = mbar_wait_bounded(full(s), (i / DK_STAGES) & 1, err, DEVERR_TIMEOUT_FULL);
+        if (!__all_sync(0xffffffffu, ok)) {  // the warp leaves together (it arrives as one)
           ok = false;
           break;
         }
         unsigned char* xt = sm + s * GG::STAGE + GG::OFF_X;
 #pragma unroll 4
         for (int o = 16 * bt; o < GG::NB * GG::XBLOCK; o += 16 * 128) {
-          float4 hi, lo;
-          split4(*reinterpret_cast<const float4*>(xt + o), hi, lo);
-          *reinterpret_cast<float4*>(xt + o) = hi;
-          *reinterpret_cast<float4*>(xt + GG::XLO + o) = lo;
+          const float4 v = *reinterpret_cast<const float4*>(xt + o);
+          *reinterpret_cast<float4*>(xt + GG::XLO + o) =
+              make_float4(tf32_trunc_lo(v.x), tf32_trunc_lo(v.y), tf32_trunc_lo(v.z), tf32_trunc_lo(v.w));
         }
-        fence_proxy_async_smem();  // the MMAs read x_hi / x_lo through the async proxy
-        mbar_arrive(conv(s));
+        fence_proxy_async_smem();  // the MMAs read x_lo through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(conv(s));
       }
     }
     // ---------------- epilogue (warps 2-9) ----------------
     const bool fin = ok && mbar_wait_bounded(dfin, 0, err, DEVERR_TC_EPILOGUE);
     if (!named_barrier_or(2, 256, !fin)) {
-      // The ring is idle: stage memory becomes the W x W correlation of one slot.
+      // The ring is idle: stage memory becomes [hi rows 0..63 | lo rows 64..127] x W.
       float* scratch = reinterpret_cast<float*>(sm);
       const int n_slots = n_it < bperiod ? n_it : bperiod;
       for (int slot = 0; slot < n_slots; ++slot) {
         if (warp < 6) {
           const int quad = warp & 3;
-          const int t = 16 * quad + (lane >> 1);
+          const int lrow = 32 * quad + lane;  // accumulator row
           tc_fence_after();
           float dv[GG::N];
           const uint32_t ta = tmem + (static_cast<uint32_t>(32 * quad) << 16) +
@@ -293,13 +307,10 @@ __global__ void __launch_bounds__(DK_THREADS, 1)
 #pragma unroll
           for (int u = 0; u < GG::N / 16; ++u) tmem_ld16(ta + 16u * u, dv + 16 * u);
           tmem_wait_ld();
-          // C[t][s] = (hi row + lo row) x (x_hi part + x_lo part); the lane pair
-          // (2t, 2t+1) adds its rows with one shuffle.
+          // Row lrow times (x_hi part + x_lo part); hi and lo rows meet in the sums below.
+          if ((lrow & 63) < W) {
 #pragma unroll
-          for (int s2 = 0; s2 < W; ++s2) {
-            float c = dv[s2] + dv[GG::N / 2 + s2];
-            c += __shfl_xor_sync(0xffffffffu, c, 1);
-            if (!lo_row_of(lane) && t < W) scratch[t * W + s2] = c;
+            for (int s2 = 0; s2 < W; ++s2) scratch[lrow * W + s2] = dv[s2] + dv[GG::N / 2 + s2];
           }
         }
         named_barrier(2, 256);
@@ -313,7 +324,7 @@ __global__ void __launch_bounds__(DK_THREADS, 1)
           float acc = 0.f;
           for (int tt = 0; tt < L; ++tt) {
             const int ss = tt + j - K / 2;
-            if (ss >= 0 && ss < L) acc += scratch[(off + tt) * W + off + ss];
+            if (ss >= 0 && ss < L) acc += scratch[(off + tt) * W + off + ss] + scratch[(64 + off + tt) * W + off + ss];
           }
           if (atomic) {
             if (ch < H) atomicAdd(out + static_cast<size_t>(ch) * K + j, acc);

@@ -277,15 +277,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full(s), 1);
-      mbar_init(sfree(s), CONVERTERS);
+      mbar_init(sfree(s), CONVERTERS / 32);  // one arrival per converter warp
     }
     for (int a = 0; a < A_SLOTS; ++a) {
-      mbar_init(aready(a), CONVERTERS);
+      mbar_init(aready(a), CONVERTERS / 32);
       mbar_init(adone(a), 1);
     }
     for (int d = 0; d < ACC_SLOTS; ++d) {
       mbar_init(mdone(d), 1);
-      mbar_init(accfree(d), 128);
+      mbar_init(accfree(d), 4);  // one arrival per epilogue warp
     }
     fence_mbar_init();
   }
@@ -387,6 +387,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         ok = mbar_wait_bounded(adone(ip % A_SLOTS), (ip / A_SLOTS) & 1, err, DEVERR_TC_CONVERT);
       }
       if (ok) ok = mbar_wait_bounded(full(s), (i / STAGES) & 1, err, DEVERR_TIMEOUT_FULL);
+      ok = __all_sync(0xffffffffu, ok);  // each warp arrives as one, so it decides as one
       if (rebuild) {
         if (named_barrier_or(2, CONVERTERS, !ok)) break;  // all converters leave together
         // Block-diagonal [T_hi; T_lo] of group grp: row t' (hi) and N + t' (lo);
@@ -440,7 +441,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // The stage is read: order the reads before the next TMA write, release it.
       fence_proxy_async_smem();
-      mbar_arrive(sfree(s));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sfree(s));
       float lo[4 * CH];
 #pragma unroll
       for (int e = 0; e < 4 * CH; ++e) {
@@ -457,7 +459,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(aready(a));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(aready(a));
     }
   } else {
     // ---------------- epilogue ----------------
@@ -479,7 +482,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int u = 0; u < 2 * N / 16; ++u) tmem_ld16(ta + 16u * u, acc + 16 * u);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(accfree(d));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(accfree(d));
       unsigned char* ob = sm + GG::OFF_OUT + o * GG::TILE;
 #pragma unroll
       for (int c = 0; c < GG::C128 + GG::C64; ++c) {
