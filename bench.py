@@ -187,6 +187,14 @@ def load_traffic() -> dict | None:
     return None
 
 
+def apply_engine(ops, engine: str) -> None:
+    """--engine: "frozen" keeps the frozen table; "ffma" / "tensor" force every path onto
+    that engine where it applies (shapes it does not cover keep the FFMA kernels)."""
+    if engine != "frozen":
+        for p in ("fwd", "bwd_input", "bwd_weight"):
+            ops.set_engine(p, engine)
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     from pathtile_b200 import build, ops, runtime
     from pathtile_b200.host import HostPipeline
@@ -194,6 +202,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     build.build()
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    apply_engine(ops, args.engine)
     dist = None
     if world > 1:
         import torch.distributed as dist
@@ -404,9 +413,10 @@ def run_s4_train(args) -> dict:
     TF32 off as in its configure_torch) is timed beside it."""
     import torch.nn.functional as F
 
-    from pathtile_b200 import build, s4conv
+    from pathtile_b200 import build, ops, s4conv
 
     build.build()
+    apply_engine(ops, args.engine)
     torch.backends.cudnn.allow_tf32 = False
     torch.backends.cuda.matmul.allow_tf32 = False
     dev = torch.device("cuda", 0)
@@ -463,6 +473,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=B_PER_GPU,
                     help="batch per GPU (default: the primary workload; smaller only for profiling)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement (profiling)")
+    ap.add_argument("--engine", choices=("frozen", "ffma", "tensor"), default="frozen",
+                    help="kernels to run: the frozen per-shape table (default), or force one engine")
     ap.add_argument("--workload", choices=("primary", "s4-train"), default="primary",
                     help="s4-train: time the S4ConvD training step instead (single GPU)")
     args = ap.parse_args()
