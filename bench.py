@@ -216,10 +216,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     gk = torch.empty_like(k)
     stream = torch.cuda.current_stream(dev)
 
+    fused = args.backward == "fused"
+
     def step():
         ops.fwd(x, k, y)
-        ops.dx(dy, k, gx)
-        ops.dk(dy, x, gk, mode="deterministic")
+        if fused:
+            ops.dx_dk(dy, x, k, gk, gx=gx, mode="deterministic")
+        else:
+            ops.dx(dy, k, gx)
+            ops.dk(dy, x, gk, mode="deterministic")
         if dist is not None:
             dist.all_reduce(gk)
 
@@ -245,6 +250,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "bwd_input": time_loop(lambda: ops.dx(dy, k, gx), iters, stream),
         "bwd_weight": time_loop(lambda: ops.dk(dy, x, gk, mode="deterministic"), iters, stream),
     }
+    if fused:
+        phase_ms["bwd_fused"] = time_loop(lambda: ops.dx_dk(dy, x, k, gk, gx=gx, mode="deterministic"), iters,
+                                          stream)
     if dist is not None:
         t = torch.tensor(list(phase_ms.values()), device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -294,8 +302,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     hbm = float(peaks["hbm_gbs"])
     pb = phase_bytes(B)
     total_bytes = 3 * pb * world
-    dominant = max(phase_ms, key=phase_ms.get)
-    achieved = pb / (phase_ms[dominant] / 1e3) / 1e9
+    fused_on = fused and ops.fused_backward(B, H, L, K)
+    step_kernels = ("fwd", "bwd_fused") if fused_on else ("fwd", "bwd_input", "bwd_weight")
+    dominant = max(step_kernels, key=phase_ms.get)
+    # Algorithmic bytes of a launch: FWD / dX / dK move two activations + k; the
+    # fused backward reads dy and x, writes dx, reads k and writes dK.
+    kernel_bytes = {p: pb for p in ("fwd", "bwd_input", "bwd_weight")}
+    kernel_bytes["bwd_fused"] = (3 * B * H * L + 2 * H * K) * 4
+    achieved = kernel_bytes[dominant] / (phase_ms[dominant] / 1e3) / 1e9
     sm_mhz = clocks.summary()["sm_mhz"] or 1965.0
     fma_peak = runtime.fp32_fma_peak_tflops(torch.cuda.get_device_properties(dev).multi_processor_count,
                                             float(sm_mhz))
@@ -307,7 +321,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                 else "conv_rows_kernel<48,48,FWD,TMA3D>"),
         "bwd_input": ("tc_conv_kernel<DX> (tcgen05, 3xTF32, A in TMEM)" if engines["bwd_input"] == "tensor"
                       else "conv_rows_kernel<48,48,DX,TMA3D>"),
-        "bwd_weight": "dk_rows_kernel<48,48,TMA3D> + dk_reduce_kernel",
+        "bwd_weight": ("tc_dk_kernel (tcgen05) + tc_dk_reduce_kernel" if engines["bwd_weight"] == "tensor"
+                       else "dk_rows_kernel<48,48,TMA3D> + dk_reduce_kernel"),
+        "bwd_fused": "tc_bwd_kernel<48> (dX on tcgen05 3xTF32, dK on FFMA, one pass over dy and x)",
     }
     result = {
         "metric": METRIC,
@@ -326,14 +342,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "workload": "primary: B=16384 per GPU, H=128, L=48, K=48 (N=8: batch-sharded x[131072,128,48])",
             "B_per_gpu": B, "global_batch": B * world, "H": H, "L": L, "K": K,
             "parallelism": f"dp{world}" + (" + NCCL all_reduce(dK)" if world > 1 else ""),
-            "dk_mode": "deterministic two-pass",
+            "dk_mode": "deterministic",
+            "backward": ("fused dX+dK kernel (ops.dx_dk)" if fused_on else "dX then dK"),
             "engines": engines,
             "l2": "inputs larger than L2 (402,653,184 B per activation tensor vs 126 MB L2)",
         },
-        "aggregate_ms": sum(phase_ms.values()),
-        "phases": {p: {"ms": ms, "GB/s": pb / (ms / 1e3) / 1e9,
-                       "frac_of_roofline": roof_ms / ms} for p, ms in phase_ms.items()},
-        "aggregate_frac_of_roofline": 3 * roof_ms / sum(phase_ms.values()),
+        "aggregate_ms": sum(phase_ms[p] for p in ("fwd", "bwd_input", "bwd_weight")),
+        "phases": {p: {"ms": ms, "GB/s": kernel_bytes[p] / (ms / 1e3) / 1e9,
+                       **({"frac_of_roofline": roof_ms / ms} if p != "bwd_fused" else
+                          {"frac_of_hbm": kernel_bytes[p] / (ms / 1e3) / 1e9 / hbm})}
+                   for p, ms in phase_ms.items()},
+        "aggregate_frac_of_roofline": 3 * roof_ms / sum(phase_ms[p] for p in ("fwd", "bwd_input", "bwd_weight")),
         "roofline": {
             "bound": "hbm",
             "kernel": kernel_names[dominant],
@@ -342,7 +361,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "unit": "GB/s",
             "frac": achieved / hbm,
             "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured" else "fallback",
-            "algorithmic_bytes_per_launch": pb,
+            "algorithmic_bytes_per_launch": kernel_bytes[dominant],
             "traffic": (traffic or {}).get(dominant),
             "fp32_fma_peak_tflops_at_sampled_clock": fma_peak,
         },
@@ -354,7 +373,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "d2h_bytes_per_step": d2h,
             "api": "pathtile_b200.host.HostPipeline.run (pinned host tensors)",
         },
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": args.steps * (1 + (ops.dx_dk_launches(B, H, L, K) if fused else 3)),
         "clocks": clocks.summary(),
         "device_error_word": err,
     }
@@ -473,6 +492,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=B_PER_GPU,
                     help="batch per GPU (default: the primary workload; smaller only for profiling)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement (profiling)")
+    ap.add_argument("--backward", choices=("fused", "separate"), default="fused",
+                    help="backward of the step: ops.dx_dk (one fused kernel where it applies) or dX then dK")
     ap.add_argument("--engine", choices=("frozen", "ffma", "tensor"), default="frozen",
                     help="kernels to run: the frozen per-shape table (default), or force one engine")
     ap.add_argument("--workload", choices=("primary", "s4-train"), default="primary",

@@ -113,6 +113,25 @@ PT_API int pt_dk_noalloc(const float* dy, const float* x, float* dk, int B, int 
                          int accumulate, void* stream);
 
 /*
+ * Input and filter gradients in one call: dx as pt_dx, dk as pt_dk (same
+ * modes and workspace rules; query pt_dx_dk_workspace_bytes).  For L = 48 and
+ * K in {3, 8, 16, 24, 32, 48}, where dX runs on the tensor engine and the grid
+ * can give every CTA a single channel, one fused kernel reads dy and x once and
+ * writes dx (dX on the tensor cores, dK on the CUDA cores; no workspace when
+ * each channel has one CTA); other shapes run pt_dx then pt_dk.  The reference
+ * launches the two separately (DepthConvAmpere.backward,
+ * kernels/warp_tiled_ampere.py:882-898); no fused counterpart.
+ */
+PT_API int pt_dx_dk(const float* dy, const float* x, const float* k, float* dx, float* dk, int B, int H,
+                    int L, int K, int mode, void* ws, size_t ws_bytes, void* stream);
+
+/* 1 if pt_dx_dk runs the fused kernel for this shape on the current device, else 0. */
+PT_API int pt_dx_dk_fused(int B, int H, int L, int K);
+
+/* Workspace bytes pt_dx_dk needs for this shape (0 for invalid shapes or none needed). */
+PT_API size_t pt_dx_dk_workspace_bytes(int B, int H, int L, int K);
+
+/*
  * Bytes of deterministic-dK workspace for this shape under the active launch
  * configuration on the current device (the reference sizes its cached
  * [H,K,num_btiles] buffer at kernels/warp_tiled_noatomic_optimized.py:1448-1471).

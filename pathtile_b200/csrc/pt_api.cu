@@ -487,6 +487,78 @@ int launch_tensor_dk(const Plan& p, const float* dy, const float* x, float* dk, 
   return PT_OK;
 }
 
+// Fused backward (dX on the tensor cores, dK on the CUDA cores, one pass over dy
+// and x): L = 48 with a fused instantiation, dX on the tensor engine at this
+// shape, and a grid in which every CTA keeps one channel (a multiple of H that
+// keeps >= 3/4 of the SMs busy).  G == H makes each CTA's partial its channel's dK.
+bool plan_fused(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
+  const void* func = pt::tc::bwd_func(L, K);
+  if (!func || engine_for(PT_PATH_DX, B, H, L, K, di.sm_count) != PT_ENGINE_TENSOR) return false;
+  if (static_cast<long long>(pt::tc::bwd_smem()) > di.max_smem) return false;
+  const long long tiles = tensor_tiles(PT_PATH_DX, B, H);
+  const int gmax = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);
+  const int G = (gmax / H) * H;
+  if (G < 1 || 4LL * G < 3LL * gmax) return false;
+  if (ensure_smem_attr(di, func, pt::tc::bwd_smem()) != PT_OK) return false;
+  pt::TileGeom& g = p.g;
+  g.B = B;
+  g.H = H;
+  g.L = L;
+  g.K = K;
+  g.Q = static_cast<int>(tiles);
+  g.G = G;
+  g.Th = 1;
+  g.Tb = pt::tc::kRowsPerTile;
+  g.nhb = H;
+  p.func = func;
+  p.smem = pt::tc::bwd_smem();
+  p.threads = pt::tc::kThreads;
+  p.exact = true;
+  p.tensor = true;
+  p.period = 1;
+  p.groups = H;
+  p.lay = pt::tc::layout_for(L);
+  return true;
+}
+
+// Workspace of the fused backward: none when each channel has one CTA, else the
+// tensor-core dK layout (2 slots per CTA, one used, Hc = 1).
+size_t fused_ws_bytes(const Plan& p) {
+  if (p.g.G == p.g.H) return 0;
+  const size_t slots = static_cast<size_t>(p.g.G) * pt::tc::kDkMaxGroups;
+  const size_t part = (slots * p.g.K * sizeof(float) + 255) / 256 * 256;
+  return part + slots * sizeof(int);
+}
+
+int launch_fused(const Plan& p, const float* dy, const float* x, const float* k, float* dx, float* dk,
+                 int mode, void* ws, unsigned* err, cudaStream_t stream) {
+  const pt::TileGeom& g = p.g;
+  CUtensorMap dy128, dy64, x128, x64, dx128, dx64;
+  int rc = PT_OK;
+  if ((rc = encode_tc_tmap(&dy128, dy, g.B, g.H, g.L, 32, false)) != PT_OK) return rc;
+  if ((rc = encode_tc_tmap(&dy64, dy, g.B, g.H, g.L, 16, false)) != PT_OK) return rc;
+  if ((rc = encode_tc_tmap(&x128, x, g.B, g.H, g.L, 32, false)) != PT_OK) return rc;
+  if ((rc = encode_tc_tmap(&x64, x, g.B, g.H, g.L, 16, false)) != PT_OK) return rc;
+  if ((rc = encode_tc_tmap(&dx128, dx, g.B, g.H, g.L, 32, false)) != PT_OK) return rc;
+  if ((rc = encode_tc_tmap(&dx64, dx, g.B, g.H, g.L, 16, false)) != PT_OK) return rc;
+  int direct = (g.G == g.H) ? 1 : 0;
+  int accumulate = (mode == PT_DK_DETERMINISTIC) ? 0 : 1;  // atomic and *_ACCUMULATE add to dk
+  float* out = direct ? dk : static_cast<float*>(ws);
+  const size_t slots = static_cast<size_t>(g.G) * pt::tc::kDkMaxGroups;
+  const size_t part_bytes = (slots * g.K * sizeof(float) + 255) / 256 * 256;
+  int* group_of = direct ? nullptr : reinterpret_cast<int*>(static_cast<unsigned char*>(ws) + part_bytes);
+  int H = g.H, n_tiles = g.Q, acc_k = direct ? accumulate : 0;
+  void* args[] = {&dy128, &dy64, &x128, &x64, &dx128, &dx64, const_cast<float**>(&k), &out, &group_of,
+                  &H, &n_tiles, &direct, &acc_k, &err};
+  cudaError_t ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  if (!direct) {
+    pt::tc::dk_reduce(out, group_of, static_cast<int>(slots), H, g.K, 1, dk, accumulate, stream);
+    if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_fail(ce);
+  }
+  return PT_OK;
+}
+
 // act1/act2 are [B,H,L] activations (may be null when B == 0, as an empty
 // tensor has no storage); hk is the [H,K] filter or filter gradient.
 int check_common(const void* act1, const void* act2, const void* hk, int B, int H, int L, int K) {
@@ -622,6 +694,47 @@ int pt_dk(const float* dy, const float* x, float* dk, int B, int H, int L, int K
     if (ce != cudaSuccess) return cuda_fail(ce);
   }
   return PT_OK;
+}
+
+int pt_dx_dk_fused(int B, int H, int L, int K) {
+  if (B < 1 || H < 1 || L < 1 || K < 1 || L > PT_MAX_L || K > PT_MAX_K) return 0;
+  DeviceInfo* di = nullptr;
+  if (current_device(di) != PT_OK) return 0;
+  Plan p;
+  return plan_fused(B, H, L, K, *di, p) ? 1 : 0;
+}
+
+size_t pt_dx_dk_workspace_bytes(int B, int H, int L, int K) {
+  if (B < 1 || H < 1 || L < 1 || K < 1 || L > PT_MAX_L || K > PT_MAX_K) return 0;
+  DeviceInfo* di = nullptr;
+  if (current_device(di) != PT_OK) return 0;
+  Plan p;
+  if (plan_fused(B, H, L, K, *di, p)) return fused_ws_bytes(p);
+  return pt_dk_workspace_bytes(B, H, L, K);
+}
+
+int pt_dx_dk(const float* dy, const float* x, const float* k, float* dx, float* dk, int B, int H, int L,
+             int K, int mode, void* ws, size_t ws_bytes, void* stream_v) {
+  int rc = check_common(dy, x, k, B, H, L, K);
+  if (rc != PT_OK) return rc;
+  if (!dk || (B > 0 && !dx)) return PT_ERR_ARGS;
+  if (!aligned16(dx) || !aligned16(dk)) return PT_ERR_ALIGN;
+  if (mode != PT_DK_ATOMIC && mode != PT_DK_DETERMINISTIC && mode != PT_DK_DETERMINISTIC_ACCUMULATE)
+    return PT_ERR_ARGS;
+  if (B == 0) return pt_dk(dy, x, dk, B, H, L, K, mode, ws, ws_bytes, stream_v);
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device(di)) != PT_OK) return rc;
+  Plan p;
+  if (plan_fused(B, H, L, K, *di, p)) {
+    const size_t need = fused_ws_bytes(p);
+    if (need > 0) {
+      if (!ws || ws_bytes < need) return PT_ERR_WORKSPACE;
+      if (!aligned16(ws)) return PT_ERR_ALIGN;
+    }
+    return launch_fused(p, dy, x, k, dx, dk, mode, ws, di->err, static_cast<cudaStream_t>(stream_v));
+  }
+  if ((rc = pt_dx(dy, k, dx, B, H, L, K, stream_v)) != PT_OK) return rc;
+  return pt_dk(dy, x, dk, B, H, L, K, mode, ws, ws_bytes, stream_v);
 }
 
 int pt_config(int path, int B, int H, int L, int K, int* out, int n) {

@@ -1,6 +1,7 @@
 // pt_tc.cu -- instantiations of the tensor-core FWD / DX kernels.
 #include "pathtile_b200.h"
 #include "pt_tc.h"
+#include "pt_tc_bwd.cuh"
 #include "pt_tc_dk.cuh"
 #include "pt_tc_kernels.cuh"
 
@@ -62,6 +63,21 @@ __global__ void __launch_bounds__(256) tc_dk_reduce_kernel(const float* __restri
     if (group_of[e] == grp) acc += partial[static_cast<size_t>(e) * hc * K + c * K + j];
   dk[idx] = accumulate ? dk[idx] + acc : acc;
 }
+
+const void* bwd_func(int L, int K) {
+  if (L != BWD_L) return nullptr;
+  switch (K) {
+    case 3: return reinterpret_cast<const void*>(&tc_bwd_kernel<3>);
+    case 8: return reinterpret_cast<const void*>(&tc_bwd_kernel<8>);
+    case 16: return reinterpret_cast<const void*>(&tc_bwd_kernel<16>);
+    case 24: return reinterpret_cast<const void*>(&tc_bwd_kernel<24>);
+    case 32: return reinterpret_cast<const void*>(&tc_bwd_kernel<32>);
+    case 48: return reinterpret_cast<const void*>(&tc_bwd_kernel<48>);
+    default: return nullptr;
+  }
+}
+
+size_t bwd_smem() { return BwdGeo::SMEM; }
 
 void dk_reduce(const float* partial, const int* group_of, int n_slots, int H, int K, int hc, float* dk,
                int accumulate, void* stream) {

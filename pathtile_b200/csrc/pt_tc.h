@@ -51,3 +51,14 @@ void dk_reduce(const float* partial, const int* group_of, int n_slots, int H, in
 
 }  // namespace tc
 }  // namespace pt
+
+namespace pt {
+namespace tc {
+
+// Fused backward (dX on the tensor cores + dK on the CUDA cores) for L = 48 and
+// K in {3, 8, 16, 24, 32, 48}; nullptr otherwise.
+const void* bwd_func(int L, int K);
+size_t bwd_smem();
+
+}  // namespace tc
+}  // namespace pt

@@ -1,0 +1,412 @@
+// pt_tc_bwd.cuh -- fused backward: dX on the tensor cores and dK on the CUDA
+// cores, in one pass over dy and x (L = 48).
+//
+// Separately, dX reads dy and writes dx, and dK reads dy and x: four [B, H, L]
+// streams.  Here one kernel reads dy and x once and writes dx (three streams),
+// and the two halves of the work use different pipes: the dX product runs as
+// in tc_conv_kernel<DX> (3xTF32 split, A in tensor memory, Toeplitz operand
+// resident in shared memory), while the row threads that split dy for it also
+// accumulate the filter gradient of their row with FFMAs.
+//
+// Tiles are 128 batch rows of one channel; CTAs are dealt tiles round-robin
+// and the host uses this kernel only where every CTA keeps a single channel
+// (a grid that is a multiple of H), so each thread's dK accumulators belong to
+// one channel for the whole kernel.  At the end the CTA sums its threads'
+// accumulators in a fixed order and writes one partial per (CTA, tap): with
+// one CTA per channel that partial is the channel's dK.
+//
+// Roles (448 threads, one CTA per SM):
+//   warp 0       TMA producer: ring of 3 stages, each the dy and x tiles
+//   warp 1       allocates 512 TMEM columns; lane 0 issues the dX MMAs
+//   warps 2-9    row workers, two per tile row: split half of the dy row into
+//                TMEM (A of dX), then dK for the even or odd taps over the
+//                whole row, streaming dy from shared memory four columns at a
+//                time against the x row in registers; release the stage
+//   warps 10-13  dX epilogue: TMEM -> staging -> TMA store, as in tc_conv_kernel
+// Every wait is bounded; on expiry the kernel records a bit in the device
+// error word, drains its own copies and MMAs, frees its tensor memory and
+// returns without writing dK.
+#pragma once
+
+#include "pt_tc_kernels.cuh"
+
+namespace pt {
+namespace tc {
+
+constexpr int BWD_STAGES = 3;
+constexpr int BWD_L = 48;
+
+struct BwdGeo {
+  using GG = Geo<3>;                                  // 48-column tiles: 128-B + 64-B boxes
+  static constexpr int N = GG::N;                     // 48
+  static constexpr int TILE = GG::TILE;               // 24 KB
+  static constexpr int STAGE = 2 * TILE;              // dy | x
+  static constexpr int OFF_OUT = BWD_STAGES * STAGE;
+  static constexpr int OFF_B = OFF_OUT + OUT_SLOTS * TILE;
+  static constexpr int OFF_BAR = OFF_B + GG::BMAT;    // one resident Toeplitz operand
+  static constexpr int N_BARS = 2 * BWD_STAGES + 2 * A_SLOTS + 2 * ACC_SLOTS;
+  static constexpr int OFF_TMEM = OFF_BAR + N_BARS * 8;
+  static constexpr int SMEM = OFF_TMEM + 16 + 1024;
+  static_assert(STAGE % 1024 == 0 && OFF_B % 1024 == 0, "swizzled buffers start on 1024-byte boundaries");
+  static_assert(BWD_L * 128 * 4 <= BWD_STAGES * STAGE, "dK reduction scratch (<= 48 rows) fits the idle ring");
+};
+
+// Filter-gradient share of one row worker.  The two workers of a tile row take
+// the even (half 0) and odd (half 1) taps, j = 2 jj + half, over the whole row:
+//   acc[jj] += sum_t dy[t] x[t + 2 jj + half - PAD].
+// With X[m + 1] = x[m + half] (X = [0, x0 .. x47] for half 0 and
+// [x0 .. x47, 0] for half 1) both halves run one instruction stream,
+//   acc[jj] += dy[t] X[t + 2 jj - PAD + 1],   t + 2 jj - PAD in [-1, 48),
+// so the two warps that share an SM sub-partition share its instruction cache
+// (separate nests per half thrashed it).  dy arrives four columns at a time as
+// 16-byte chunks of the swizzled row: one conflict-free LDS.128 per chunk.
+template <int K>
+struct BwdSplit {
+  static constexpr int NJ = (K + 1) / 2;  // accumulators per row worker
+};
+
+template <int K>
+__device__ __forceinline__ void bwd_dk_row(const unsigned char* dyrow128, const unsigned char* dyrow64,
+                                           const uint32_t (&c128)[8], const uint32_t (&c64)[4],
+                                           const float (&X)[BWD_L + 1], float (&acc)[BwdSplit<K>::NJ]) {
+  constexpr int PAD = K / 2;
+  constexpr int NJ = BwdSplit<K>::NJ;
+#pragma unroll
+  for (int c = 0; c < BWD_L / 4; ++c) {
+    bool any = false;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) {
+        const int m = 4 * c + u + 2 * jj - PAD;
+        any = any || (m >= -1 && m < BWD_L);
+      }
+    if (!any) continue;
+    const float4 q = (c < 8) ? *reinterpret_cast<const float4*>(dyrow128 + c128[c & 7])
+                             : *reinterpret_cast<const float4*>(dyrow64 + c64[(c - 8) & 3]);
+    const float d[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) {
+        const int m = 4 * c + u + 2 * jj - PAD;
+        if (m >= -1 && m < BWD_L) acc[jj] = fmaf(d[u], X[m + 1], acc[jj]);
+      }
+  }
+}
+
+// n_tiles = ceil(B / 128) * H; tile tau: channel tau % H, rows [128 * (tau / H), +128).
+// Requires gridDim.x % H == 0 (each CTA keeps channel blockIdx.x % H).
+// dk_out: partial[(g * 2) * K + j] with group_of[2g] = channel, group_of[2g + 1] = -1
+// (the tensor-core dK reduce layout), or, if direct != 0, dk[h * K + j] (=, or += when
+// accumulate != 0) -- valid when each channel has exactly one CTA.
+template <int K>
+__global__ void __launch_bounds__(THREADS, 1)
+    tc_bwd_kernel(const __grid_constant__ CUtensorMap tm_dy128, const __grid_constant__ CUtensorMap tm_dy64,
+                  const __grid_constant__ CUtensorMap tm_x128, const __grid_constant__ CUtensorMap tm_x64,
+                  const __grid_constant__ CUtensorMap tm_dx128, const __grid_constant__ CUtensorMap tm_dx64,
+                  const float* __restrict__ taps, float* __restrict__ dk_out, int* __restrict__ group_of,
+                  int H, int n_tiles, int direct, int accumulate, unsigned* err) {
+  using GG = Geo<3>;
+  using BG = BwdGeo;
+  constexpr int N = GG::N;
+  constexpr int L = BWD_L;
+  constexpr int NJ = BwdSplit<K>::NJ;  // accumulators per row worker
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = aligned_smem(smem_raw);
+  const uint32_t base = smem_u32(sm);
+  const int warp = static_cast<int>(threadIdx.x >> 5);
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const uint32_t bar0 = base + BG::OFF_BAR;
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto sfree = [&](int s) { return bar0 + 8u * (BWD_STAGES + s); };
+  auto aready = [&](int a) { return bar0 + 8u * (2 * BWD_STAGES + a); };
+  auto adone = [&](int a) { return bar0 + 8u * (2 * BWD_STAGES + A_SLOTS + a); };
+  auto mdone = [&](int d) { return bar0 + 8u * (2 * BWD_STAGES + 2 * A_SLOTS + d); };
+  auto accfree = [&](int d) { return bar0 + 8u * (2 * BWD_STAGES + 2 * A_SLOTS + ACC_SLOTS + d); };
+  const int G = static_cast<int>(gridDim.x);
+  const int g = static_cast<int>(blockIdx.x);
+  const int h = g % H;  // the CTA's channel (G % H == 0)
+  const int n_it = (g < n_tiles) ? (n_tiles - 1 - g) / G + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < BWD_STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(sfree(s), CONVERTERS / 32);
+    }
+    for (int a = 0; a < A_SLOTS; ++a) {
+      mbar_init(aready(a), CONVERTERS / 32);
+      mbar_init(adone(a), 1);
+    }
+    for (int d = 0; d < ACC_SLOTS; ++d) {
+      mbar_init(mdone(d), 1);
+      mbar_init(accfree(d), 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(base + BG::OFF_TMEM, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + BG::OFF_TMEM);
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < n_it; ++i) {
+        const int s = i % BWD_STAGES;
+        if (i >= BWD_STAGES &&
+            !mbar_wait_bounded(sfree(s), ((i / BWD_STAGES) - 1) & 1, err, DEVERR_TIMEOUT_DONE))
+          break;
+        const int b0 = ((g + i * G) / H) * M;
+        const uint32_t st = base + static_cast<uint32_t>(s * BG::STAGE);
+        mbar_arrive_expect_tx(full(s), BG::STAGE);
+        tma_load_3d(st, &tm_dy128, 0, h, b0, full(s));
+        tma_load_3d(st + GG::BOX64, &tm_dy64, GG::S64, h, b0, full(s));
+        tma_load_3d(st + BG::TILE, &tm_x128, 0, h, b0, full(s));
+        tma_load_3d(st + BG::TILE + GG::BOX64, &tm_x64, GG::S64, h, b0, full(s));
+        issued = i + 1;
+      }
+      for (int i = issued > BWD_STAGES ? issued - BWD_STAGES : 0; i < issued; ++i)
+        if (!mbar_wait_bounded(full(i % BWD_STAGES), (i / BWD_STAGES) & 1, err, DEVERR_TIMEOUT_DRAIN)) break;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (dX) ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_n2 = idesc_tf32_m128<2 * N>();
+      constexpr uint32_t idesc_n = idesc_tf32_m128<N>();
+      int issued = 0;
+      for (int i = 0; i < n_it; ++i) {
+        const int a = i % A_SLOTS, d = i % ACC_SLOTS;
+        if (!mbar_wait_bounded(aready(a), (i / A_SLOTS) & 1, err, DEVERR_TC_MMA)) break;
+        if (i >= ACC_SLOTS &&
+            !mbar_wait_bounded(accfree(d), ((i / ACC_SLOTS) - 1) & 1, err, DEVERR_TC_MMA))
+          break;
+        tc_fence_after();
+        const uint32_t a_hi = tmem + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS);
+        const uint32_t a_lo = a_hi + LO_COLS;
+        const uint32_t bmat = base + static_cast<uint32_t>(BG::OFF_B);
+        const uint32_t dacc = tmem + static_cast<uint32_t>(D_COL0 + d * D_SLOT_COLS);
+#pragma unroll
+        for (int kk = 0; kk < GG::KSTEPS; ++kk) {
+          const bool in128 = kk < GG::K128;
+          const uint64_t bdesc = kmajor_desc(
+              bmat + (in128 ? 32u * kk : GG::BBOX64 + 32u * (kk - GG::K128)), in128);
+          mma_tf32_ts(dacc, a_hi + 8u * kk, bdesc, idesc_n2, kk > 0);
+          mma_tf32_ts(dacc, a_lo + 8u * kk, bdesc, idesc_n, 1);
+        }
+        mma_commit(adone(a));
+        mma_commit(mdone(d));
+        issued = i + 1;
+      }
+      if (issued > 0)
+        mbar_wait_bounded(mdone((issued - 1) % ACC_SLOTS), ((issued - 1) / ACC_SLOTS) & 1, err,
+                          DEVERR_TC_MMA);
+    }
+    __syncwarp();
+  } else if (warp < EPI0 / 32) {
+    // ---------------- row workers ----------------
+    const int ct = static_cast<int>(threadIdx.x) - 64;  // 0..255
+    const int quad = warp & 3;
+    const int row = 32 * quad + lane;                   // tile row (TMEM lane)
+    const int half = (warp - 2) >> 2;                   // dX: half of the row; dK: half of the taps
+    constexpr int CH = (GG::C128 + GG::C64) / 2;        // 6 chunks per half row
+    const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
+    // Swizzled chunk offsets of this row (128-B box: 8 chunks, 64-B box: 4 chunks).
+    uint32_t c128[8], c64[4];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) c128[c] = sw128_off(row, c) - 128u * row;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) c64[c] = sw64_off(row, c) - 64u * row;
+    // The channel's Toeplitz operand for dX (built once: every tile has channel h).
+    {
+      const int pad = K / 2;  // dX: T[s][t] = k[t - s + K/2]
+      unsigned char* bm = sm + BG::OFF_B;
+      const float* kh = taps + static_cast<size_t>(h) * K;
+      constexpr int CPR = N / 4;
+      for (int task = ct; task < N * CPR; task += CONVERTERS) {
+        const int c4 = task / N;
+        const int tp = task - c4 * N;
+        const int sp = 4 * c4;
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int j = tp - (sp + q) + pad;
+          v[q] = (j >= 0 && j < K) ? __ldg(kh + j) : 0.f;
+        }
+        float4 hi, lo;
+        split4(make_float4(v[0], v[1], v[2], v[3]), hi, lo);
+        if (c4 < GG::C128) {
+          *reinterpret_cast<float4*>(bm + sw128_off(tp, c4)) = hi;
+          *reinterpret_cast<float4*>(bm + GG::BLO128 + sw128_off(tp, c4)) = lo;
+        } else {
+          unsigned char* b64 = bm + GG::BBOX64;
+          *reinterpret_cast<float4*>(b64 + sw64_off(tp, c4 - GG::C128)) = hi;
+          *reinterpret_cast<float4*>(b64 + GG::BLO64 + sw64_off(tp, c4 - GG::C128)) = lo;
+        }
+      }
+      fence_proxy_async_smem();  // the MMAs read the operand through the async proxy
+    }
+    float acc[NJ];
+#pragma unroll
+    for (int jj = 0; jj < NJ; ++jj) acc[jj] = 0.f;
+    for (int i = 0; i < n_it; ++i) {
+      const int s = i % BWD_STAGES, a = i % A_SLOTS;
+      if (i >= A_SLOTS) ok = mbar_wait_bounded(adone(a), ((i / A_SLOTS) - 1) & 1, err, DEVERR_TC_CONVERT);
+      if (ok) ok = mbar_wait_bounded(full(s), (i / BWD_STAGES) & 1, err, DEVERR_TIMEOUT_FULL);
+      if (!__all_sync(0xffffffffu, ok)) {  // each warp arrives as one, so it decides as one
+        ok = false;
+        break;
+      }
+      const unsigned char* st = sm + s * BG::STAGE;
+      const unsigned char* dy128 = st + 128u * row;
+      const unsigned char* dy64 = st + GG::BOX64 + 64u * row;
+      // dX: this thread's half of the dy row -> A_hi / A_lo in tensor memory.
+      {
+        float v[4 * CH];
+#pragma unroll
+        for (int u = 0; u < CH; ++u) {
+          const int c = half * CH + u;
+          const uint32_t off = (c < GG::C128) ? sw128_off(row, c) : GG::BOX64 + sw64_off(row, c - GG::C128);
+          const float4 q = *reinterpret_cast<const float4*>(st + off);
+          v[4 * u] = q.x;
+          v[4 * u + 1] = q.y;
+          v[4 * u + 2] = q.z;
+          v[4 * u + 3] = q.w;
+        }
+        float lo[4 * CH];
+#pragma unroll
+        for (int e = 0; e < 4 * CH; ++e) {
+          const float hi = tf32_round(v[e]);
+          lo[e] = tf32_round(v[e] - hi);
+          v[e] = hi;
+        }
+        const uint32_t acol =
+            tmem + lane_base + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + half * 4 * CH);
+#pragma unroll
+        for (int u = 0; u < CH / 2; ++u) {
+          tmem_st8(acol + 8u * u, v + 8 * u);
+          tmem_st8(acol + LO_COLS + 8u * u, lo + 8 * u);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(aready(a));
+      }
+      // dK: the x row in registers, dy[t] streamed from shared memory.
+      {
+        const unsigned char* x128 = st + BG::TILE + 128u * row;
+        const unsigned char* x64 = st + BG::TILE + GG::BOX64 + 64u * row;
+        float x[L];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 q = *reinterpret_cast<const float4*>(x128 + c128[c]);
+          x[4 * c] = q.x;
+          x[4 * c + 1] = q.y;
+          x[4 * c + 2] = q.z;
+          x[4 * c + 3] = q.w;
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float4 q = *reinterpret_cast<const float4*>(x64 + c64[c]);
+          x[32 + 4 * c] = q.x;
+          x[32 + 4 * c + 1] = q.y;
+          x[32 + 4 * c + 2] = q.z;
+          x[32 + 4 * c + 3] = q.w;
+        }
+        float X[L + 1];  // X[m + 1] = x[m + half]
+#pragma unroll
+        for (int n = L; n >= 0; --n) {
+          const float hi = (n < L) ? x[n] : 0.f;
+          const float lo = (n > 0) ? x[n - 1] : 0.f;
+          X[n] = half ? hi : lo;
+        }
+        bwd_dk_row<K>(dy128, dy64, c128, c64, X, acc);
+      }
+      // The stage is read: order the reads before the next TMA write, release it.
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sfree(s));
+    }
+    // ---------------- dK: sum the CTA's rows in a fixed order ----------------
+    if (!named_barrier_or(2, CONVERTERS, !ok)) {
+      // Wait until the producer's last loads are consumed (every full phase was
+      // waited on above), then reuse the ring as [K][128] scratch.
+      float* red = reinterpret_cast<float*>(sm);
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) {
+        const int j = 2 * jj + half;
+        if (j < K) red[j * M + row] = acc[jj];
+      }
+      named_barrier(2, CONVERTERS);
+      for (int j = ct; j < K; j += CONVERTERS) {
+        float sum = 0.f;
+        for (int r = 0; r < M; ++r) sum += red[j * M + r];
+        if (direct) {
+          float* dst = dk_out + static_cast<size_t>(h) * K + j;
+          *dst = accumulate ? *dst + sum : sum;
+        } else {
+          dk_out[static_cast<size_t>(g) * 2 * K + j] = sum;
+        }
+      }
+      if (!direct && ct == 0) {
+        group_of[2 * g] = h;
+        group_of[2 * g + 1] = -1;
+      }
+    }
+  } else {
+    // ---------------- dX epilogue ----------------
+    const int et = static_cast<int>(threadIdx.x) - EPI0;  // 0..127
+    const int quad = warp & 3;
+    const int r = 32 * quad + lane;
+    for (int j = 0; j < n_it; ++j) {
+      const int d = j % ACC_SLOTS, o = j % OUT_SLOTS;
+      if (et == 0) bulk_wait_read<OUT_SLOTS - 1>();
+      const bool okw = mbar_wait_bounded(mdone(d), (j / ACC_SLOTS) & 1, err, DEVERR_TC_EPILOGUE);
+      if (named_barrier_or(1, 128, !okw)) break;
+      tc_fence_after();
+      float accd[2 * N];
+      const uint32_t ta = tmem + (static_cast<uint32_t>(32 * quad) << 16) +
+                          static_cast<uint32_t>(D_COL0 + d * D_SLOT_COLS);
+#pragma unroll
+      for (int u = 0; u < 2 * N / 16; ++u) tmem_ld16(ta + 16u * u, accd + 16 * u);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(accfree(d));
+      unsigned char* ob = sm + BG::OFF_OUT + o * BG::TILE;
+#pragma unroll
+      for (int c = 0; c < GG::C128 + GG::C64; ++c) {
+        const float4 y = make_float4(accd[4 * c] + accd[N + 4 * c], accd[4 * c + 1] + accd[N + 4 * c + 1],
+                                     accd[4 * c + 2] + accd[N + 4 * c + 2],
+                                     accd[4 * c + 3] + accd[N + 4 * c + 3]);
+        const uint32_t off = (c < GG::C128) ? sw128_off(r, c) : GG::BOX64 + sw64_off(r, c - GG::C128);
+        *reinterpret_cast<float4*>(ob + off) = y;
+      }
+      fence_proxy_async_smem();
+      named_barrier(1, 128);
+      if (et == 0) {
+        const int b0 = ((g + j * G) / H) * M;
+        const uint32_t os = base + static_cast<uint32_t>(BG::OFF_OUT + o * BG::TILE);
+        tma_store_3d(&tm_dx128, os, 0, h, b0);
+        tma_store_3d(&tm_dx64, os + GG::BOX64, GG::S64, h, b0);
+        bulk_commit();
+      }
+    }
+    if (et == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace tc
+}  // namespace pt

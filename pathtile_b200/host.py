@@ -4,8 +4,9 @@ A caller that holds x, k and dy in (pinned) host memory gets y, dX and dK back
 in host memory.  The batch is cut into chunks that flow through a ring of
 device staging buffers on two streams, so that the host-to-device copy of one
 chunk, the kernels of the previous one and the device-to-host copy of the one
-before overlap (PCIe is full duplex).  dK accumulates over chunks on the
-device (deterministic two-pass reduction per chunk, fixed chunk order) and is
+before overlap (PCIe is full duplex).  The backward of a chunk is one
+ops.dx_dk call (the fused dX + dK kernel where it applies); dK accumulates
+over chunks on the device (deterministic per chunk, fixed chunk order) and is
 copied back once.  Every kernel is the native library's; nothing is computed
 on the host.
 """
@@ -79,8 +80,8 @@ class HostPipeline:
                 with torch.cuda.stream(self.compute):
                     xs, dys = self.x[slot][:nb], self.dy[slot][:nb]
                     ops.fwd(xs, self.k, self.y[slot][:nb])
-                    ops.dx(dys, self.k, self.gx[slot][:nb])
-                    ops.dk(dys, xs, self.gk, mode="deterministic", accumulate=(i > 0))
+                    ops.dx_dk(dys, xs, self.k, self.gk, gx=self.gx[slot][:nb], mode="deterministic",
+                              accumulate=(i > 0))
                     self.comp_done[slot].record(self.compute)
                 self.copy_out.wait_event(self.comp_done[slot])
                 with torch.cuda.stream(self.copy_out):
@@ -93,5 +94,9 @@ class HostPipeline:
             cur.wait_stream(self.copy_out)
 
     def launches_per_call(self, B: int) -> int:
-        """Native kernel launches of one call (FWD, dX, dK pass 1 and 2 per chunk)."""
-        return 4 * ((B + self.chunk_b - 1) // self.chunk_b)
+        """Native kernel launches of one call: per chunk, FWD and the backward's."""
+        n = 0
+        for b0 in range(0, B, self.chunk_b):
+            nb = min(self.chunk_b, B - b0)
+            n += 1 + ops.dx_dk_launches(nb, self.H, self.L, self.K)
+        return n

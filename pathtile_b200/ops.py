@@ -203,6 +203,80 @@ def dk(
     return gk
 
 
+def dx_dk(
+    dy: torch.Tensor,
+    x: torch.Tensor,
+    k: torch.Tensor,
+    gk: torch.Tensor,
+    gx: torch.Tensor | None = None,
+    mode: str = "deterministic",
+    accumulate: bool = False,
+    workspace: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Both backward products in one call: returns gx = dX(dy, k) and writes the
+    filter gradient into gk with dk()'s modes.  For L = 48 and K in {3, 8, 16,
+    24, 32, 48} on grids that give each CTA one channel this is one fused kernel
+    (dy and x read once); other shapes run dx() then dk().  The reference's
+    backward launches the two separately (kernels/warp_tiled_ampere.py:882-898).
+    """
+    _ensure_cuda_f32(dy, "gy")
+    _ensure_cuda_f32(x, "x")
+    _ensure_cuda_f32(k, "k")
+    _ensure_cuda_f32(gk, "gk")
+    if tuple(dy.shape) != tuple(x.shape):
+        raise ValueError("gy and x must have the same [B,H,L] shape")
+    B, H, L, K = check_shapes(x, k)
+    if tuple(gk.shape) != (H, K):
+        raise ValueError(f"gk must have shape {(H, K)}")
+    if gx is None:
+        gx = torch.empty_like(dy, memory_format=torch.contiguous_format)
+    _ensure_cuda_f32(gx, "gx")
+    if tuple(gx.shape) != tuple(dy.shape):
+        raise ValueError("gx must have the shape of gy")
+    if not (dy.device == x.device == k.device == gk.device == gx.device):
+        raise ValueError("gy, x, k, gk and gx must be on one device")
+    if mode not in DK_MODES:
+        raise ValueError(f"mode must be one of {sorted(DK_MODES)}")
+    for t, n in ((dy, "gy"), (x, "x"), (k, "k"), (gk, "gk"), (gx, "gx")):
+        _ensure_raw(t, n)
+    code = DK_MODES[mode]
+    if code == PT_DK_DETERMINISTIC and accumulate:
+        code = PT_DK_DETERMINISTIC_ACCUMULATE
+    lib = _lib.load()
+    dev = x.device
+    with torch.cuda.device(dev):
+        ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
+        need = int(lib.pt_dx_dk_workspace_bytes(B, H, L, K)) if B > 0 else 0
+        if need > 0:
+            ws = workspace if workspace is not None else WORKSPACES.get(dev, need)
+            if ws.device != dev or ws.numel() * ws.element_size() < need:
+                raise ValueError(f"workspace must be on {dev} and hold {need} bytes")
+            ws.record_stream(torch.cuda.current_stream(dev))
+            ws_ptr = _ptr(ws)
+            ws_bytes = ws.numel() * ws.element_size()
+        st = lib.pt_dx_dk(_ptr(dy), _ptr(x), _ptr(k), _ptr(gx), _ptr(gk), B, H, L, K, code, ws_ptr, ws_bytes,
+                          _stream(dev))
+    _lib.check(st, "pt_dx_dk")
+    return gx
+
+
+def fused_backward(B: int, H: int, L: int, K: int) -> bool:
+    """True when dx_dk() runs the single fused kernel at this shape on the current device."""
+    return bool(_lib.load().pt_dx_dk_fused(B, H, L, K))
+
+
+def dx_dk_launches(B: int, H: int, L: int, K: int) -> int:
+    """Kernel launches of one deterministic dx_dk() at this shape: the fused kernel
+    (plus the partial reduce when a channel spans several CTAs), or dX + the
+    two-pass dK."""
+    if B <= 0:
+        return 0
+    lib = _lib.load()
+    if lib.pt_dx_dk_fused(B, H, L, K):
+        return 1 if int(lib.pt_dx_dk_workspace_bytes(B, H, L, K)) == 0 else 2
+    return 3
+
+
 def config(path: str, B: int, H: int, L: int, K: int) -> dict[str, int]:
     """Frozen launch choice of one path at one shape (C ABI pt_config)."""
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]

@@ -269,6 +269,11 @@ class B200WarpRuntime:
     ``dk_mode`` selects the dK reduction: "deterministic" (two-pass, default)
     or "atomic".  Both accumulate into ``gk`` in ``launch_bwd_weight`` so the
     reference contract -- the caller zero-fills gk -- holds for either.
+    ``fuse_backward`` (B200 addition, default on): when autograd needs both
+    gradients at a shape the fused kernel covers, backward is one
+    ``launch_bwd_fused`` (phase "bwd_fused") instead of the reference's two
+    launches; the explicit ``launch_bwd_input`` / ``launch_bwd_weight`` calls
+    are unchanged.
     """
 
     def __init__(
@@ -282,6 +287,7 @@ class B200WarpRuntime:
         threads_per_row: int = 1,
         dk_mode: str = "deterministic",
         device: int | None = None,
+        fuse_backward: bool = True,
     ) -> None:
         if warps_per_block is not None and warps_per_block not in {1, 2, 4, 8}:
             raise ValueError("warps_per_block must be one of 1,2,4,8 (32..256 rows per tile)")
@@ -307,6 +313,7 @@ class B200WarpRuntime:
             raise ValueError("threads_per_row must be 1 or 2")
         self.threads_per_row = threads_per_row
         self.dk_mode = dk_mode
+        self.fuse_backward = bool(fuse_backward)
         self.fast_math = False
         self._closed = False
         self._apply_overrides()
@@ -362,6 +369,18 @@ class B200WarpRuntime:
             "bwd_weight", lambda: ops.dk(gy, x, gk, mode=mode, accumulate=True),
             {"B": B, "H": H, "L": L, "K": K})
 
+    def launch_bwd_fused(self, gy: torch.Tensor, x: torch.Tensor, k: torch.Tensor, gx: torch.Tensor,
+                         gk: torch.Tensor, collector: KernelEventCollector | None = None) -> None:
+        """gx = dX and gk += dK in one call (ops.dx_dk; one fused kernel where it
+        applies, else the two kernels); gk zero-filled by the caller, as for
+        launch_bwd_weight."""
+        self._check_open()
+        B, H, L, K = self._check_shapes(x, k)
+        mode = self.dk_mode
+        (collector or KERNEL_EVENTS).launch(
+            "bwd_fused", lambda: ops.dx_dk(gy, x, k, gk, gx=gx, mode=mode, accumulate=True),
+            {"B": B, "H": H, "L": L, "K": K})
+
     def resource_report(self, B: int = DEFAULT_B, H: int = DEFAULT_H, L: int = DEFAULT_L,
                         K: int = DEFAULT_K) -> list[dict[str, Any]]:
         """Registers, shared memory and occupancy of the three kernels at one shape."""
@@ -411,7 +430,9 @@ def default_runtime() -> B200WarpRuntime:
 
 class DepthConvB200(torch.autograd.Function):
     """Autograd op: forward launches FWD; backward launches dX and dK for the
-    inputs that need gradients (kernels/warp_tiled_ampere.py:863-894)."""
+    inputs that need gradients (kernels/warp_tiled_ampere.py:863-894), as one
+    fused launch when both are needed, the runtime's fuse_backward is on and
+    the shape is one the fused kernel covers."""
 
     @staticmethod
     def forward(ctx: Any, x: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
@@ -434,6 +455,17 @@ class DepthConvB200(torch.autograd.Function):
         if tuple(gy_c.shape) != (B, H, L):
             raise ValueError("Unexpected gradient shape")
         gx = gk = None
+        if (ctx.needs_input_grad[0] and ctx.needs_input_grad[1] and runtime.fuse_backward
+                and ops.fused_backward(B, H, L, K)):
+            gx = torch.empty_like(x_c)
+            if runtime.dk_mode == "atomic":
+                gk = torch.zeros_like(k_c)
+                runtime.launch_bwd_fused(gy_c, x_c, k_c, gx, gk)
+            else:
+                gk = torch.empty_like(k_c)
+                KERNEL_EVENTS.launch("bwd_fused", lambda: ops.dx_dk(gy_c, x_c, k_c, gk, gx=gx),
+                                     {"B": B, "H": H, "L": L, "K": K})
+            return gx, gk
         if ctx.needs_input_grad[0]:
             gx = torch.empty_like(x_c)
             runtime.launch_bwd_input(gy_c, k_c, gx)

@@ -1,0 +1,193 @@
+"""GPU parity of the fused backward (one kernel: dX on the tensor cores, dK on
+the CUDA cores) reached through ops.dx_dk / pt_dx_dk.
+
+Bars as for the separate kernels: dX within rtol = atol = 1e-5 of the FP64 C
+oracle, dK within 1e-4 relative of the FP64 dK.  Covered: every fused
+instantiation (L = 48, K in {3, 8, 16, 24, 32, 48}), both dK regimes of the
+fused kernel (one CTA per channel writes dK directly; several CTAs per channel
+write partials summed by the reduce kernel), the three dK modes, ragged batch
+tiles, grids smaller than the SM count, and shapes that fall back to pt_dx +
+pt_dk.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import c_oracle, reference_torch
+from pathtile_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+FWD_TOL = dict(rtol=1e-5, atol=1e-5)
+DK_RTOL = 1e-4
+FUSED_K = (3, 8, 16, 24, 32, 48)
+
+
+def assert_dk_close(got: np.ndarray, ref64: np.ndarray) -> None:
+    scale = float(np.abs(ref64).max()) if ref64.size else 0.0
+    np.testing.assert_allclose(got, ref64, rtol=DK_RTOL, atol=DK_RTOL * max(scale, 1e-30))
+
+
+def _inputs(B, H, L, K, seed, device):
+    x, k, dy = reference_torch.make_inputs(B, H, L, K, seed)
+    return x.to(device), k.to(device), dy.to(device), (x, k, dy)
+
+
+def _sm_count(dev) -> int:
+    return torch.cuda.get_device_properties(dev).multi_processor_count
+
+
+def _expect_fused(B, H, L, K, sm) -> bool:
+    """The host rule: L = 48, a fused K, and a grid of whole channels (a
+    multiple of H) that keeps at least 3/4 of min(tiles, SMs) busy."""
+    if L != 48 or K not in FUSED_K:
+        return False
+    gmax = min(-(-B // 128) * H, sm)
+    G = (gmax // H) * H
+    return G >= 1 and 4 * G >= 3 * gmax
+
+
+def _run(dy, x, k, mode="deterministic", accumulate=False, gk=None):
+    if gk is None:
+        gk = torch.zeros_like(k) if mode == "atomic" else torch.full_like(k, float("nan"))
+    gx = ops.dx_dk(dy, x, k, gk, mode=mode, accumulate=accumulate)
+    torch.cuda.synchronize()
+    assert ops.device_error(clear=True) == 0, "a kernel wait expired"
+    return gx, gk
+
+
+SHAPES = [
+    (1000, 128, 48, 48),  # one CTA per channel: direct dK; ragged last tile
+    (1000, 128, 48, 3),
+    (700, 128, 48, 8),
+    (513, 128, 48, 16),
+    (300, 128, 48, 24),
+    (129, 128, 48, 32),
+    (1000, 64, 48, 48),   # two CTAs per channel: partials + reduce
+    (20000, 3, 48, 24),   # 49 CTAs per channel
+    (900, 37, 48, 16),    # 4 CTAs per channel
+    (100, 128, 48, 48),   # one tile per CTA
+    (1, 4, 48, 48),       # one row, four CTAs
+    (5000, 74, 48, 32),   # 2 CTAs per channel
+    (64, 1, 48, 3),
+]
+
+
+@pytest.mark.parametrize("mode", ["deterministic", "atomic"])
+@pytest.mark.parametrize("B,H,L,K", SHAPES)
+def test_fused_backward_against_fp64_oracle(cuda_device, B, H, L, K, mode):
+    dev = cuda_device
+    if _sm_count(dev) >= 128:
+        assert ops.fused_backward(B, H, L, K) == _expect_fused(B, H, L, K, _sm_count(dev))
+    x, k, dy, cpu = _inputs(B, H, L, K, 1717, dev)
+    gx, gk = _run(dy, x, k, mode=mode)
+    np.testing.assert_allclose(gx.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
+    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+
+
+@pytest.mark.parametrize("B,H,L,K", [(300, 96, 48, 48), (200, 8, 40, 40), (100, 5, 48, 5), (64, 300, 48, 48)])
+def test_unfused_shapes_fall_back_to_separate_kernels(cuda_device, B, H, L, K):
+    dev = cuda_device
+    assert not ops.fused_backward(B, H, L, K) or _sm_count(dev) < 128
+    x, k, dy, cpu = _inputs(B, H, L, K, 99, dev)
+    gx, gk = _run(dy, x, k)
+    np.testing.assert_allclose(gx.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
+    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+
+
+@pytest.mark.parametrize("H", [128, 64])
+def test_fused_backward_accumulate_and_determinism(cuda_device, H):
+    dev = cuda_device
+    B, L, K = 3000, 48, 48
+    x, k, dy, cpu = _inputs(B, H, L, K, 5, dev)
+    outs = [_run(dy, x, k)[1].clone() for _ in range(3)]
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    gk = torch.ones_like(k)
+    gx, gk = _run(dy, x, k, mode="deterministic", accumulate=True, gk=gk)
+    ref = c_oracle.dk(cpu[2], cpu[0], K)
+    assert_dk_close(gk.cpu().numpy() - 1.0, ref)
+    gk = torch.full_like(k, 2.0)
+    _, gk = _run(dy, x, k, mode="atomic", gk=gk)  # atomic adds onto what gk holds
+    assert_dk_close(gk.cpu().numpy() - 2.0, ref)
+
+
+def test_fused_backward_matches_separate_kernels(cuda_device):
+    dev = cuda_device
+    x, k, dy, _ = _inputs(4096, 128, 48, 48, 31, dev)
+    gx_f, gk_f = _run(dy, x, k)
+    gx_s = ops.dx(dy, k)
+    gk_s = torch.empty_like(k)
+    ops.dk(dy, x, gk_s)
+    torch.cuda.synchronize()
+    assert ops.device_error(clear=True) == 0
+    torch.testing.assert_close(gx_f, gx_s, **FWD_TOL)
+    torch.testing.assert_close(gk_f, gk_s, rtol=DK_RTOL, atol=DK_RTOL * float(gk_s.abs().max()))
+
+
+def test_fused_backward_primary_workload(cuda_device):
+    dev = cuda_device
+    B, H, L, K = 16384, 128, 48, 48
+    if _sm_count(dev) >= 128:
+        assert ops.fused_backward(B, H, L, K)
+    x, k, dy, cpu = _inputs(B, H, L, K, 42, dev)
+    gx, gk = _run(dy, x, k)
+    rows = np.random.default_rng(11).choice(B * H, size=4096, replace=False)
+    rows.sort()
+    ridx = torch.from_numpy(rows).to(dev)
+    np.testing.assert_allclose(gx.reshape(B * H, L)[ridx].cpu().numpy(),
+                               c_oracle.dx_rows(cpu[2], cpu[1], rows), **FWD_TOL)
+    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+    # <dK, k> = <dy, FWD(x)> = <dX(dy), x> over the whole tensors.
+    y = ops.fwd(x, k)
+    a = float((gk.double() * k.double()).sum())
+    b = float((y.double() * dy.double()).sum())
+    c = float((gx.double() * x.double()).sum())
+    scale = float(y.double().abs().sum()) + 1.0
+    assert abs(a - b) <= 1e-6 * scale and abs(c - b) <= 1e-6 * scale
+
+
+def test_fused_backward_side_stream(cuda_device):
+    dev = cuda_device
+    x, k, dy, cpu = _inputs(1500, 128, 48, 16, 8, dev)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        gk = torch.empty_like(k)
+        gx = ops.dx_dk(dy, x, k, gk)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    assert ops.device_error(clear=True) == 0
+    np.testing.assert_allclose(gx.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
+    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], 16))
+
+
+@pytest.mark.parametrize("fuse", [True, False])
+def test_autograd_backward_fuses_when_both_gradients_are_needed(cuda_device, fuse):
+    from pathtile_b200 import runtime
+
+    prev = runtime._RUNTIME
+    rt = runtime.B200WarpRuntime(fuse_backward=fuse)
+    runtime.install_runtime(rt)
+    try:
+        B, H, L, K = 1000, 128, 48, 48
+        x, k, dy, cpu = _inputs(B, H, L, K, 77, cuda_device)
+        xr = x.clone().requires_grad_(True)
+        kr = k.clone().requires_grad_(True)
+        runtime.KERNEL_EVENTS.clear()
+        runtime.KERNEL_EVENTS.enabled = True
+        y = runtime.depthwise_conv_ampere(xr, kr)
+        y.backward(dy)
+        rows = runtime.KERNEL_EVENTS.resolve_rows()
+        phases = [r["phase"] for r in rows]
+        expect = ["fwd", "bwd_fused"] if fuse and ops.fused_backward(B, H, L, K) else ["fwd", "bwd_input", "bwd_weight"]
+        assert phases == expect
+        assert ops.device_error(clear=True) == 0
+        np.testing.assert_allclose(xr.grad.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
+        assert_dk_close(kr.grad.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+    finally:
+        runtime.KERNEL_EVENTS.enabled = False
+        runtime.KERNEL_EVENTS.clear()
+        rt.close()
+        runtime._RUNTIME = prev
