@@ -44,12 +44,29 @@ struct BwdGeo {
   static constexpr int OFF_OUT = BWD_STAGES * STAGE;
   static constexpr int OFF_B = OFF_OUT + OUT_SLOTS * TILE;
   static constexpr int OFF_BAR = OFF_B + GG::BMAT;    // one resident Toeplitz operand
-  static constexpr int N_BARS = 2 * BWD_STAGES + 2 * A_SLOTS + 2 * ACC_SLOTS;
+  static constexpr int N_BARS = 3 * BWD_STAGES + 2 * A_SLOTS + 2 * ACC_SLOTS;
   static constexpr int OFF_TMEM = OFF_BAR + N_BARS * 8;
   static constexpr int SMEM = OFF_TMEM + 16 + 1024;
   static_assert(STAGE % 1024 == 0 && OFF_B % 1024 == 0, "swizzled buffers start on 1024-byte boundaries");
   static_assert(BWD_L * 128 * 4 <= BWD_STAGES * STAGE, "dK reduction scratch (<= 48 rows) fits the idle ring");
 };
+
+// D (+)= A B with A read from shared memory through a descriptor (tf32 operands).
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// dy - (dy with its low 13 mantissa bits cleared): the part of dy a tf32 MMA,
+// which ignores those bits, does not see.  Exact in fp32.
+__device__ __forceinline__ float bwd_tf32_rest(float v) {
+  return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+}
 
 // Filter-gradient share of one row worker.  The two workers of a tile row take
 // the even (half 0) and odd (half 1) taps, j = 2 jj + half, over the whole row:
@@ -124,6 +141,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto adone = [&](int a) { return bar0 + 8u * (2 * BWD_STAGES + A_SLOTS + a); };
   auto mdone = [&](int d) { return bar0 + 8u * (2 * BWD_STAGES + 2 * A_SLOTS + d); };
   auto accfree = [&](int d) { return bar0 + 8u * (2 * BWD_STAGES + 2 * A_SLOTS + ACC_SLOTS + d); };
+  // The dX MMAs of the tile in stage s have completed (they read its dy half).
+  auto mfree = [&](int s) { return bar0 + 8u * (2 * BWD_STAGES + 2 * A_SLOTS + 2 * ACC_SLOTS + s); };
   const int G = static_cast<int>(gridDim.x);
   const int g = static_cast<int>(blockIdx.x);
   const int h = g % H;  // the CTA's channel (G % H == 0)
@@ -133,6 +152,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < BWD_STAGES; ++s) {
       mbar_init(full(s), 1);
       mbar_init(sfree(s), CONVERTERS / 32);
+      mbar_init(mfree(s), 1);
     }
     for (int a = 0; a < A_SLOTS; ++a) {
       mbar_init(aready(a), CONVERTERS / 32);
@@ -161,7 +181,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int i = 0; i < n_it; ++i) {
         const int s = i % BWD_STAGES;
         if (i >= BWD_STAGES &&
-            !mbar_wait_bounded(sfree(s), ((i / BWD_STAGES) - 1) & 1, err, DEVERR_TIMEOUT_DONE))
+            (!mbar_wait_bounded(sfree(s), ((i / BWD_STAGES) - 1) & 1, err, DEVERR_TIMEOUT_DONE) ||
+             !mbar_wait_bounded(mfree(s), ((i / BWD_STAGES) - 1) & 1, err, DEVERR_TIMEOUT_DONE)))
           break;
         const int b0 = ((g + i * G) / H) * M;
         const uint32_t st = base + static_cast<uint32_t>(s * BG::STAGE);
@@ -182,14 +203,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       constexpr uint32_t idesc_n = idesc_tf32_m128<N>();
       int issued = 0;
       for (int i = 0; i < n_it; ++i) {
-        const int a = i % A_SLOTS, d = i % ACC_SLOTS;
+        const int a = i % A_SLOTS, d = i % ACC_SLOTS, s = i % BWD_STAGES;
+        // The stage's dy tile is the A_hi operand: wait for its load as well.
+        if (!mbar_wait_bounded(full(s), (i / BWD_STAGES) & 1, err, DEVERR_TC_MMA)) break;
         if (!mbar_wait_bounded(aready(a), (i / A_SLOTS) & 1, err, DEVERR_TC_MMA)) break;
         if (i >= ACC_SLOTS &&
             !mbar_wait_bounded(accfree(d), ((i / ACC_SLOTS) - 1) & 1, err, DEVERR_TC_MMA))
           break;
         tc_fence_after();
-        const uint32_t a_hi = tmem + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS);
-        const uint32_t a_lo = a_hi + LO_COLS;
+        const uint32_t a_lo = tmem + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + LO_COLS);
+        const uint32_t dyt = base + static_cast<uint32_t>(s * BG::STAGE);
         const uint32_t bmat = base + static_cast<uint32_t>(BG::OFF_B);
         const uint32_t dacc = tmem + static_cast<uint32_t>(D_COL0 + d * D_SLOT_COLS);
 #pragma unroll
@@ -197,10 +220,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           const bool in128 = kk < GG::K128;
           const uint64_t bdesc = kmajor_desc(
               bmat + (in128 ? 32u * kk : GG::BBOX64 + 32u * (kk - GG::K128)), in128);
-          mma_tf32_ts(dacc, a_hi + 8u * kk, bdesc, idesc_n2, kk > 0);
-          mma_tf32_ts(dacc, a_lo + 8u * kk, bdesc, idesc_n, 1);
+          const uint64_t adesc = kmajor_desc(
+              dyt + (in128 ? 32u * kk : GG::BOX64 + 32u * (kk - GG::K128)), in128);
+          mma_tf32_ss(dacc, adesc, bdesc, idesc_n2, kk > 0);    // dy (tf32 part) [T_hi; T_lo]
+          mma_tf32_ts(dacc, a_lo + 8u * kk, bdesc, idesc_n, 1);  // dy rest T_hi
         }
         mma_commit(adone(a));
+        mma_commit(mfree(s));
         mma_commit(mdone(d));
         issued = i + 1;
       }
@@ -266,33 +292,26 @@ __global__ void __launch_bounds__(THREADS, 1)
       const unsigned char* st = sm + s * BG::STAGE;
       const unsigned char* dy128 = st + 128u * row;
       const unsigned char* dy64 = st + GG::BOX64 + 64u * row;
-      // dX: this thread's half of the dy row -> A_hi / A_lo in tensor memory.
+      const unsigned char* x128 = st + BG::TILE + 128u * row;
+      const unsigned char* x64 = st + BG::TILE + GG::BOX64 + 64u * row;
+      // dX: the MMA reads dy's tf32 part straight from the stage; this thread
+      // writes the rest of its half of the dy row (A_lo) into tensor memory.
       {
-        float v[4 * CH];
+        float lo[4 * CH];
 #pragma unroll
         for (int u = 0; u < CH; ++u) {
           const int c = half * CH + u;
           const uint32_t off = (c < GG::C128) ? sw128_off(row, c) : GG::BOX64 + sw64_off(row, c - GG::C128);
           const float4 q = *reinterpret_cast<const float4*>(st + off);
-          v[4 * u] = q.x;
-          v[4 * u + 1] = q.y;
-          v[4 * u + 2] = q.z;
-          v[4 * u + 3] = q.w;
-        }
-        float lo[4 * CH];
-#pragma unroll
-        for (int e = 0; e < 4 * CH; ++e) {
-          const float hi = tf32_round(v[e]);
-          lo[e] = tf32_round(v[e] - hi);
-          v[e] = hi;
+          lo[4 * u] = bwd_tf32_rest(q.x);
+          lo[4 * u + 1] = bwd_tf32_rest(q.y);
+          lo[4 * u + 2] = bwd_tf32_rest(q.z);
+          lo[4 * u + 3] = bwd_tf32_rest(q.w);
         }
         const uint32_t acol =
-            tmem + lane_base + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + half * 4 * CH);
+            tmem + lane_base + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + LO_COLS + half * 4 * CH);
 #pragma unroll
-        for (int u = 0; u < CH / 2; ++u) {
-          tmem_st8(acol + 8u * u, v + 8 * u);
-          tmem_st8(acol + LO_COLS + 8u * u, lo + 8 * u);
-        }
+        for (int u = 0; u < CH / 2; ++u) tmem_st8(acol + 8u * u, lo + 8 * u);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -300,8 +319,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // dK: the x row in registers, dy[t] streamed from shared memory.
       {
-        const unsigned char* x128 = st + BG::TILE + 128u * row;
-        const unsigned char* x64 = st + BG::TILE + GG::BOX64 + 64u * row;
         float x[L];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -334,6 +351,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(sfree(s));
     }
     // ---------------- dK: sum the CTA's rows in a fixed order ----------------
+    // The scratch below overwrites stage 0, which the last tiles' MMAs may still
+    // read: wait for the last MMA group (groups complete in issue order).
+    if (ok && n_it > 0)
+      ok = mbar_wait_bounded(mfree((n_it - 1) % BWD_STAGES), ((n_it - 1) / BWD_STAGES) & 1, err,
+                             DEVERR_TC_CONVERT);
     if (!named_barrier_or(2, CONVERTERS, !ok)) {
       // Wait until the producer's last loads are consumed (every full phase was
       // waited on above), then reuse the ring as [K][128] scratch.
