@@ -79,35 +79,72 @@ __device__ __forceinline__ float bwd_tf32_rest(float v) {
 // 16-byte chunks of the swizzled row: one conflict-free LDS.128 per chunk.
 template <int K>
 struct BwdSplit {
-  static constexpr int NJ = (K + 1) / 2;  // accumulators per row worker
+  static constexpr int NJ = (K + 1) / 2;  // taps per row worker
+};
+
+// Packed FP32 pairs: fma.rn.f32x2 does two FMAs in one issue slot (same FMA
+// pipe throughput as two FFMAs, half the instructions).
+__device__ __forceinline__ uint64_t bwd_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float bwd_pair_sum(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+__device__ __forceinline__ uint64_t bwd_ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// The same sum with even and odd t accumulated apart, two taps-by-column
+// products per instruction:
+//   (accE, accO)[jj] += (dy[t], dy[t+1]) * (X[k], X[k+1]),  t even,
+//   k = t + 2 jj - PAD + 1,
+// whose parity is fixed by K, so the X pairs are packed once per tile (XP) and
+// the dy pairs are the halves of each 16-byte chunk.  X outside [0, 49) is 0.
+template <int K>
+struct BwdPairs {
+  static constexpr int PAD = K / 2;
+  static constexpr int NJ = BwdSplit<K>::NJ;
+  static constexpr int KB = ((1 - PAD) % 2 + 2) % 2;  // parity of every k
+  // first k >= max(1 - PAD, -1) with parity KB
+  static constexpr int K0 = ((1 - PAD) >= -1) ? (1 - PAD) : ((-1 - KB) % 2 == 0 ? -1 : 0);
+  static constexpr int KMAX0 = 46 + 2 * (NJ - 1) - PAD + 1;
+  static constexpr int K1 = KMAX0 < 48 ? KMAX0 : (48 - ((48 - KB) % 2 != 0));
+  static constexpr int NQ = (K1 - K0) / 2 + 1;  // packed X pairs
 };
 
 template <int K>
-__device__ __forceinline__ void bwd_dk_row(const unsigned char* dyrow128, const unsigned char* dyrow64,
-                                           const uint32_t (&c128)[8], const uint32_t (&c64)[4],
-                                           const float (&X)[BWD_L + 1], float (&acc)[BwdSplit<K>::NJ]) {
-  constexpr int PAD = K / 2;
-  constexpr int NJ = BwdSplit<K>::NJ;
+__device__ __forceinline__ void bwd_dk_row2(const unsigned char* dyrow128, const unsigned char* dyrow64,
+                                            uint32_t xm128, uint32_t xm64,
+                                            const uint64_t (&XP)[BwdPairs<K>::NQ],
+                                            uint64_t (&acc)[BwdSplit<K>::NJ]) {
+  using P = BwdPairs<K>;
+  constexpr int NJ = P::NJ;
 #pragma unroll
   for (int c = 0; c < BWD_L / 4; ++c) {
     bool any = false;
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < 2; ++u)
 #pragma unroll
       for (int jj = 0; jj < NJ; ++jj) {
-        const int m = 4 * c + u + 2 * jj - PAD;
-        any = any || (m >= -1 && m < BWD_L);
+        const int k = 4 * c + 2 * u + 2 * jj - P::PAD + 1;
+        any = any || (k >= P::K0 && k <= P::K1);
       }
     if (!any) continue;
-    const float4 q = (c < 8) ? *reinterpret_cast<const float4*>(dyrow128 + c128[c & 7])
-                             : *reinterpret_cast<const float4*>(dyrow64 + c64[(c - 8) & 3]);
-    const float d[4] = {q.x, q.y, q.z, q.w};
+    const ulonglong2 q = (c < 8) ? *reinterpret_cast<const ulonglong2*>(dyrow128 + ((16u * c) ^ xm128))
+                                 : *reinterpret_cast<const ulonglong2*>(dyrow64 + ((16u * (c - 8)) ^ xm64));
+    const uint64_t d[2] = {q.x, q.y};
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < 2; ++u)
 #pragma unroll
       for (int jj = 0; jj < NJ; ++jj) {
-        const int m = 4 * c + u + 2 * jj - PAD;
-        if (m >= -1 && m < BWD_L) acc[jj] = fmaf(d[u], X[m + 1], acc[jj]);
+        const int k = 4 * c + 2 * u + 2 * jj - P::PAD + 1;
+        if (k >= P::K0 && k <= P::K1) acc[jj] = bwd_ffma2(d[u], XP[(k - P::K0) / 2], acc[jj]);
       }
   }
 }
@@ -243,12 +280,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int half = (warp - 2) >> 2;                   // dX: half of the row; dK: half of the taps
     constexpr int CH = (GG::C128 + GG::C64) / 2;        // 6 chunks per half row
     const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
-    // Swizzled chunk offsets of this row (128-B box: 8 chunks, 64-B box: 4 chunks).
-    uint32_t c128[8], c64[4];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) c128[c] = sw128_off(row, c) - 128u * row;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) c64[c] = sw64_off(row, c) - 64u * row;
+    // In-row byte offset of 16-byte chunk c of this row: (16 c) ^ xm128 in the
+    // 128-B box (chunks 0-7), (16 c) ^ xm64 in the 64-B box (chunks 0-3).
+    const uint32_t xm128 = static_cast<uint32_t>(row & 7) << 4;
+    const uint32_t xm64 = static_cast<uint32_t>((row >> 1) & 3) << 4;
     // The channel's Toeplitz operand for dX (built once: every tile has channel h).
     {
       const int pad = K / 2;  // dX: T[s][t] = k[t - s + K/2]
@@ -278,9 +313,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       fence_proxy_async_smem();  // the MMAs read the operand through the async proxy
     }
-    float acc[NJ];
+    uint64_t acc[NJ];  // (even t, odd t) partial sums per tap
 #pragma unroll
-    for (int jj = 0; jj < NJ; ++jj) acc[jj] = 0.f;
+    for (int jj = 0; jj < NJ; ++jj) acc[jj] = 0ull;
     for (int i = 0; i < n_it; ++i) {
       const int s = i % BWD_STAGES, a = i % A_SLOTS;
       if (i >= A_SLOTS) ok = mbar_wait_bounded(adone(a), ((i / A_SLOTS) - 1) & 1, err, DEVERR_TC_CONVERT);
@@ -322,7 +357,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         float x[L];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const float4 q = *reinterpret_cast<const float4*>(x128 + c128[c]);
+          const float4 q = *reinterpret_cast<const float4*>(x128 + ((16u * c) ^ xm128));
           x[4 * c] = q.x;
           x[4 * c + 1] = q.y;
           x[4 * c + 2] = q.z;
@@ -330,20 +365,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const float4 q = *reinterpret_cast<const float4*>(x64 + c64[c]);
+          const float4 q = *reinterpret_cast<const float4*>(x64 + ((16u * c) ^ xm64));
           x[32 + 4 * c] = q.x;
           x[32 + 4 * c + 1] = q.y;
           x[32 + 4 * c + 2] = q.z;
           x[32 + 4 * c + 3] = q.w;
         }
-        float X[L + 1];  // X[m + 1] = x[m + half]
+        // XP[q] = (X[k], X[k + 1]), k = K0 + 2q, with X[n] = x[n - 1 + half] on
+        // [0, 49) and 0 elsewhere (half 1's copy of the row is shifted by one).
+        using P = BwdPairs<K>;
+        auto xz = [&](int n) { return (n >= 0 && n < L) ? x[n] : 0.f; };  // compile-time n
+        uint64_t XP[P::NQ];
 #pragma unroll
-        for (int n = L; n >= 0; --n) {
-          const float hi = (n < L) ? x[n] : 0.f;
-          const float lo = (n > 0) ? x[n - 1] : 0.f;
-          X[n] = half ? hi : lo;
+        for (int q = 0; q < P::NQ; ++q) {
+          const int k = P::K0 + 2 * q;
+          const float e0 = (k >= 0 && k <= L) ? (half ? xz(k) : xz(k - 1)) : 0.f;
+          const float e1 = (k + 1 >= 0 && k + 1 <= L) ? (half ? xz(k + 1) : xz(k)) : 0.f;
+          XP[q] = bwd_pack(e0, e1);
         }
-        bwd_dk_row<K>(dy128, dy64, c128, c64, X, acc);
+        bwd_dk_row2<K>(dy128, dy64, xm128, xm64, XP, acc);
       }
       // The stage is read: order the reads before the next TMA write, release it.
       fence_proxy_async_smem();
@@ -363,7 +403,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int jj = 0; jj < NJ; ++jj) {
         const int j = 2 * jj + half;
-        if (j < K) red[j * M + row] = acc[jj];
+        if (j < K) red[j * M + row] = bwd_pair_sum(acc[jj]);
       }
       named_barrier(2, CONVERTERS);
       for (int j = ct; j < K; j += CONVERTERS) {
