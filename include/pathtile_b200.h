@@ -125,6 +125,22 @@ PT_API int pt_dk_noalloc(const float* dy, const float* x, float* dk, int B, int 
 PT_API int pt_dx_dk(const float* dy, const float* x, const float* k, float* dx, float* dk, int B, int H,
                     int L, int K, int mode, void* ws, size_t ws_bytes, void* stream);
 
+/*
+ * Channels-last variants: x, y, dy, dx are [B, L, H] (H contiguous), k and dk
+ * [H, K], same math as pt_fwd / pt_dx / pt_dk.  They replace the S4 block's
+ * transposes to [B, H, L] and back around the convolution
+ * (kernels/warp_tiled_ampere.py:1186, :1190).  CUDA-core kernels, one thread
+ * per (b, h) sequence; pointers need 4-byte alignment (ws: 16).  pt_dk_cl is
+ * deterministic (per-CTA partials in ws, then a fixed-order sum): dk = dK, or
+ * dk += dK when accumulate != 0.
+ */
+PT_API int pt_fwd_cl(const float* x, const float* k, float* y, int B, int L, int H, int K, void* stream);
+PT_API int pt_dx_cl(const float* dy, const float* k, float* dx, int B, int L, int H, int K, void* stream);
+PT_API int pt_dk_cl(const float* dy, const float* x, float* dk, int B, int L, int H, int K, int accumulate,
+                    void* ws, size_t ws_bytes, void* stream);
+/* Workspace bytes pt_dk_cl needs for this shape on the current device (0 if invalid). */
+PT_API size_t pt_dk_cl_workspace_bytes(int B, int L, int H, int K);
+
 /* 1 if pt_dx_dk runs the fused kernel for this shape on the current device, else 0. */
 PT_API int pt_dx_dk_fused(int B, int H, int L, int K);
 

@@ -47,6 +47,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_dx_dk": (_c_int, [_fp, _fp, _fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
     "pt_dx_dk_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
     "pt_dx_dk_fused": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
+    "pt_fwd_cl": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "pt_dx_cl": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "pt_dk_cl": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
+    "pt_dk_cl_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
     "pt_dk_noalloc": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "pt_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int]),
     "pt_set_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int]),

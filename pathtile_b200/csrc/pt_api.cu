@@ -12,6 +12,7 @@
 
 #include "pathtile_b200.h"
 #define PT_KERNELS_IMPL 1
+#include "pt_cl.h"
 #include "pt_frozen_config.h"
 #include "pt_kernels.cuh"
 #include "pt_registry.h"
@@ -735,6 +736,62 @@ int pt_dx_dk(const float* dy, const float* x, const float* k, float* dx, float* 
   }
   if ((rc = pt_dx(dy, k, dx, B, H, L, K, stream_v)) != PT_OK) return rc;
   return pt_dk(dy, x, dk, B, H, L, K, mode, ws, ws_bytes, stream_v);
+}
+
+// ---------------- channels-last [B, L, H] ----------------
+namespace {
+
+int check_cl(const void* a1, const void* a2, const void* hk, int B, int L, int H, int K) {
+  if (B < 0 || H < 1 || L < 1 || K < 1) return PT_ERR_ARGS;
+  if (L > PT_MAX_L || K > PT_MAX_K) return PT_ERR_UNSUPPORTED;
+  if (!hk || (B > 0 && (!a1 || !a2))) return PT_ERR_ARGS;
+  auto al4 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; };
+  if (!al4(a1) || !al4(a2) || !al4(hk)) return PT_ERR_ALIGN;
+  return PT_OK;
+}
+
+int conv_cl(const float* in, const float* k, float* out, int B, int L, int H, int K, bool rev, void* stream) {
+  int rc = check_cl(in, out, k, B, L, H, K);
+  if (rc != PT_OK || B == 0) return rc;
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device(di)) != PT_OK) return rc;
+  cudaError_t ce = pt::cl::launch_conv(in, k, out, B, L, H, K, rev, static_cast<cudaStream_t>(stream));
+  return ce == cudaSuccess ? PT_OK : cuda_fail(ce);
+}
+
+}  // namespace
+
+int pt_fwd_cl(const float* x, const float* k, float* y, int B, int L, int H, int K, void* stream) {
+  return conv_cl(x, k, y, B, L, H, K, false, stream);
+}
+
+int pt_dx_cl(const float* dy, const float* k, float* dx, int B, int L, int H, int K, void* stream) {
+  return conv_cl(dy, k, dx, B, L, H, K, true, stream);
+}
+
+size_t pt_dk_cl_workspace_bytes(int B, int L, int H, int K) {
+  if (B < 1 || H < 1 || L < 1 || K < 1 || L > PT_MAX_L || K > PT_MAX_K) return 0;
+  DeviceInfo* di = nullptr;
+  if (current_device(di) != PT_OK) return 0;
+  return pt::cl::dk_workspace_bytes(B, L, H, K, di->sm_count);
+}
+
+int pt_dk_cl(const float* dy, const float* x, float* dk, int B, int L, int H, int K, int accumulate, void* ws,
+             size_t ws_bytes, void* stream_v) {
+  int rc = check_cl(dy, x, dk, B, L, H, K);
+  if (rc != PT_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (B == 0) {
+    if (accumulate) return PT_OK;
+    cudaError_t ce = cudaMemsetAsync(dk, 0, static_cast<size_t>(H) * K * sizeof(float), stream);
+    return ce == cudaSuccess ? PT_OK : cuda_fail(ce);
+  }
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device(di)) != PT_OK) return rc;
+  if (!ws || ws_bytes < pt::cl::dk_workspace_bytes(B, L, H, K, di->sm_count)) return PT_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(ws) & 15u) != 0) return PT_ERR_ALIGN;
+  cudaError_t ce = pt::cl::launch_dk(dy, x, dk, B, L, H, K, accumulate ? 1 : 0, ws, di->sm_count, stream);
+  return ce == cudaSuccess ? PT_OK : cuda_fail(ce);
 }
 
 int pt_config(int path, int B, int H, int L, int K, int* out, int n) {

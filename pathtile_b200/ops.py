@@ -277,6 +277,78 @@ def dx_dk_launches(B: int, H: int, L: int, K: int) -> int:
     return 3
 
 
+# ---------------- channels-last [B, L, H] ----------------
+def _check_cl(x: torch.Tensor, k: torch.Tensor) -> tuple[int, int, int, int]:
+    """Validate x[B,L,H] (channels last) and k[H,K]; return (B, L, H, K)."""
+    _ensure_cuda_f32(x, "x")
+    _ensure_cuda_f32(k, "k")
+    if x.ndim != 3 or k.ndim != 2:
+        raise ValueError("Expected x[B,L,H] and k[H,K]")
+    B, L, H = map(int, x.shape)
+    Hk, K = map(int, k.shape)
+    if H != Hk:
+        raise ValueError("x and k channel dimensions do not match")
+    if L > PT_MAX_L or K > PT_MAX_K:
+        raise ValueError(f"Specialized kernels require L<={PT_MAX_L}, K<={PT_MAX_K}")
+    if H < 1 or L < 1 or K < 1:
+        raise ValueError("H, L and K must be positive")
+    if x.device != k.device:
+        raise ValueError("x and k must be on the same device")
+    for tt, n in ((x, "x"), (k, "k")):
+        if not tt.is_contiguous():
+            raise ValueError(f"{n} must be contiguous")
+    return B, L, H, K
+
+
+def _conv_cl(fn_name: str, inp: torch.Tensor, k: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+    B, L, H, K = _check_cl(inp, k)
+    if out is None:
+        out = torch.empty_like(inp, memory_format=torch.contiguous_format)
+    _ensure_cuda_f32(out, "out")
+    if tuple(out.shape) != (B, L, H) or out.device != inp.device or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {(B, L, H)} tensor on the input's device")
+    if B == 0:
+        return out
+    with torch.cuda.device(inp.device):
+        st = getattr(_lib.load(), fn_name)(_ptr(inp), _ptr(k), _ptr(out), B, L, H, K, _stream(inp.device))
+    _lib.check(st, fn_name)
+    return out
+
+
+def fwd_cl(x: torch.Tensor, k: torch.Tensor, y: torch.Tensor | None = None) -> torch.Tensor:
+    """Channels-last FWD: y[b,t,h] = sum_j x[b,t+j-K//2,h] k[h,j] for x, y [B,L,H]."""
+    return _conv_cl("pt_fwd_cl", x, k, y)
+
+
+def dx_cl(dy: torch.Tensor, k: torch.Tensor, gx: torch.Tensor | None = None) -> torch.Tensor:
+    """Channels-last input gradient: gx[b,t,h] = sum_j dy[b,t-j+K//2,h] k[h,j]."""
+    return _conv_cl("pt_dx_cl", dy, k, gx)
+
+
+def dk_cl(dy: torch.Tensor, x: torch.Tensor, gk: torch.Tensor, accumulate: bool = False,
+          workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Channels-last filter gradient into gk[H,K] (deterministic: gk = dK, or gk += dK)."""
+    B, L, H, K = _check_cl(x, gk)
+    _ensure_cuda_f32(dy, "gy")
+    if tuple(dy.shape) != (B, L, H) or dy.device != x.device or not dy.is_contiguous():
+        raise ValueError("gy must be a contiguous tensor shaped and placed like x")
+    lib = _lib.load()
+    dev = x.device
+    with torch.cuda.device(dev):
+        ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
+        if B > 0:
+            need = int(lib.pt_dk_cl_workspace_bytes(B, L, H, K))
+            ws = workspace if workspace is not None else WORKSPACES.get(dev, need)
+            if ws.device != dev or ws.numel() * ws.element_size() < need:
+                raise ValueError(f"workspace must be on {dev} and hold {need} bytes")
+            ws.record_stream(torch.cuda.current_stream(dev))
+            ws_ptr, ws_bytes = _ptr(ws), ws.numel() * ws.element_size()
+        st = lib.pt_dk_cl(_ptr(dy), _ptr(x), _ptr(gk), B, L, H, K, 1 if accumulate else 0, ws_ptr, ws_bytes,
+                          _stream(dev))
+    _lib.check(st, "pt_dk_cl")
+    return gk
+
+
 def config(path: str, B: int, H: int, L: int, K: int) -> dict[str, int]:
     """Frozen launch choice of one path at one shape (C ABI pt_config)."""
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]

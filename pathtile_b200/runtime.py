@@ -496,6 +496,39 @@ def depthwise_conv_ampere(x: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
     return DepthConvB200.apply(x, k)
 
 
+class DepthConvCL(torch.autograd.Function):
+    """Channels-last autograd op: x[B,L,H] * k[H,K] -> y[B,L,H] on the [B,L,H]
+    kernels (ops.fwd_cl / dx_cl / dk_cl), for callers such as the S4 block that
+    hold activations channels-last (kernels/warp_tiled_ampere.py:1186-1190)."""
+
+    @staticmethod
+    def forward(ctx: Any, x: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+        x_c = x.contiguous()
+        k_c = k.contiguous()
+        y = ops.fwd_cl(x_c, k_c)
+        ctx.save_for_backward(x_c, k_c)
+        return y
+
+    @staticmethod
+    def backward(ctx: Any, gy: torch.Tensor):
+        x_c, k_c = ctx.saved_tensors
+        gy_c = gy.contiguous()
+        gx = ops.dx_cl(gy_c, k_c) if ctx.needs_input_grad[0] else None
+        gk = None
+        if ctx.needs_input_grad[1]:
+            gk = torch.empty_like(k_c)
+            ops.dk_cl(gy_c, x_c, gk)
+        return gx, gk
+
+
+def depthwise_conv_b200_cl(x: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+    """Differentiable same-length depthwise Conv1D on channels-last x[B,L,H] with k[H,K]."""
+    return DepthConvCL.apply(x, k)
+
+
+depthwise_conv_b200_cl.channels_last = True
+
+
 def roofline_ms(B: int, H: int, L: int, K: int, hbm_gbs: float, fma_tflops: float) -> float:
     """Per-phase roofline time: max(bytes / HBM bandwidth, FLOPs / FP32 FMA peak)."""
     t_mem = minimum_algorithmic_bytes(B, H, L, K) / (hbm_gbs * 1e9)
@@ -509,7 +542,8 @@ def fp32_fma_peak_tflops(sm_count: int = 148, sm_mhz: float = 1965.0) -> float:
 
 
 __all__ = [
-    "B200WarpRuntime", "AmpereWarpRuntime", "DepthConvB200", "DepthConvAmpere",
+    "B200WarpRuntime", "AmpereWarpRuntime", "DepthConvB200", "DepthConvAmpere", "DepthConvCL",
+    "depthwise_conv_b200_cl",
     "depthwise_conv_b200", "depthwise_conv_ampere", "install_runtime", "get_runtime",
     "default_runtime", "KernelEventCollector", "KERNEL_EVENTS", "GPUProfile", "GPU_PROFILES",
     "detect_gpu_profile", "estimate_gpu_occupancy", "minimum_algorithmic_bytes",

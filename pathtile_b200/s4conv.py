@@ -4,16 +4,24 @@ The reference trains a four-block S4 model whose every block runs the short
 depthwise convolution on [B, H, L] with K = L taps generated from the S4
 parameters (kernels/warp_tiled_ampere.py:1122-1215, training loop :1432-1560:
 batch 16384, L = 48, H = 128, SGD lr 1e-3 momentum 0.9, RMSLE loss).  This
-module rebuilds that model on :func:`pathtile_b200.runtime.depthwise_conv_b200`.
+module rebuilds that model on the native depthwise operator.
 
-One B200-side change: the block's skip term ``y + x * skip`` (:1188) is a
-convolution with ``skip`` added to the centre tap (tap K//2 multiplies x[t]),
-so the block convolves with ``k + skip * e_{K//2}`` and the extra elementwise
-pass over [B, H, L] disappears; autograd routes the centre-tap gradient (which
-dK computes anyway) to ``skip``.
+Two B200-side changes, neither of which changes the function computed:
+
+* the block's skip term ``y + x * skip`` (:1188) is a convolution with ``skip``
+  added to the centre tap (tap K//2 multiplies x[t]), so the block convolves
+  with ``k + skip * e_{K//2}`` and the extra elementwise pass disappears;
+  autograd routes the centre-tap gradient (which dK computes anyway) to ``skip``;
+* the block keeps its activations channels-last: the reference transposes
+  [B, L, H] to [B, H, L] for the convolution and back (:1186, :1190); here the
+  convolution runs on [B, L, H] directly (:func:`runtime.depthwise_conv_b200_cl`)
+  and the 1x1 ``Conv1d`` + GLU over channels becomes the same linear map over
+  the last dimension (same parameters).
 
 ``conv`` is injectable so a caller can time the same model on another
-convolution; by default every block uses the native operator.
+convolution; a conv function with a true ``channels_last`` attribute gets
+[B, L, H] tensors, any other gets [B, H, L] (the reference's layout).  By
+default every block uses the native channels-last operator.
 """
 from __future__ import annotations
 
@@ -23,7 +31,9 @@ from typing import Callable
 import torch
 import torch.nn as nn
 
-from .runtime import MAX_L, depthwise_conv_b200
+import torch.nn.functional as F
+
+from .runtime import MAX_L, depthwise_conv_b200_cl
 
 ConvFn = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
 
@@ -31,7 +41,7 @@ ConvFn = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
 class S4ConvKernel(nn.Module):
     """Diagonal S4 kernel generator: k[h, t] = 2 Re(sum_n C'_hn exp(dt_h A_hn t))."""
 
-    def __init__(self, hidden_dim: int, state_dim: int, conv: ConvFn = depthwise_conv_b200) -> None:
+    def __init__(self, hidden_dim: int, state_dim: int, conv: ConvFn = depthwise_conv_b200_cl) -> None:
         super().__init__()
         self.H = hidden_dim
         self.N = state_dim
@@ -53,8 +63,16 @@ class S4ConvKernel(nn.Module):
         C_eff = C * (torch.exp(dtA) - 1.0) / A
         return (2 * torch.einsum("hn,hnk->hk", C_eff, powers).real).contiguous()
 
+    @property
+    def channels_last(self) -> bool:
+        return bool(getattr(self.conv, "channels_last", False))
+
     def forward(self, x: torch.Tensor, skip: torch.Tensor | None = None) -> torch.Tensor:
-        _, H, L = x.shape
+        """x is [B, L, H] for a channels-last conv, else [B, H, L]; the output likewise."""
+        if self.channels_last:
+            _, L, H = x.shape
+        else:
+            _, H, L = x.shape
         if H != self.H:
             raise ValueError(f"Expected H={self.H}, got {H}")
         if L > MAX_L:
@@ -68,7 +86,7 @@ class S4ConvKernel(nn.Module):
 
 
 class S4ConvBlock(nn.Module):
-    def __init__(self, hidden_dim: int, state_dim: int, dropout: float, conv: ConvFn = depthwise_conv_b200) -> None:
+    def __init__(self, hidden_dim: int, state_dim: int, dropout: float, conv: ConvFn = depthwise_conv_b200_cl) -> None:
         super().__init__()
         self.skip = nn.Parameter(torch.randn(hidden_dim))
         self.kernel_layer = S4ConvKernel(hidden_dim, state_dim, conv)
@@ -77,7 +95,13 @@ class S4ConvBlock(nn.Module):
         self.output_linear = nn.Sequential(nn.Conv1d(hidden_dim, 2 * hidden_dim, kernel_size=1), nn.GLU(dim=1))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        residual = x
+        residual = x  # [B, L, H]
+        if self.kernel_layer.channels_last:
+            y = self.kernel_layer(x.contiguous(), self.skip)
+            y = self.activation(self.dropout(y))
+            conv1x1 = self.output_linear[0]
+            y = F.glu(F.linear(y, conv1x1.weight.squeeze(-1), conv1x1.bias), dim=-1)
+            return y + residual
         x_hl = x.transpose(1, 2).contiguous()
         y = self.kernel_layer(x_hl, self.skip)
         y = self.output_linear(self.activation(self.dropout(y)))
@@ -88,7 +112,7 @@ class Model(nn.Module):
     """Encoder -> S4 blocks -> decoder; input [B, L, input_dim], output [B, output_dim]."""
 
     def __init__(self, state_dim: int = 64, hidden_dim: int = 128, input_dim: int = 4, output_dim: int = 1,
-                 num_blocks: int = 4, dropout: float = 0.01, conv: ConvFn = depthwise_conv_b200) -> None:
+                 num_blocks: int = 4, dropout: float = 0.01, conv: ConvFn = depthwise_conv_b200_cl) -> None:
         super().__init__()
         self.encoder = nn.Linear(input_dim, hidden_dim)
         self.blocks = nn.ModuleList([S4ConvBlock(hidden_dim, state_dim, dropout, conv) for _ in range(num_blocks)])
