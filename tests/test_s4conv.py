@@ -44,6 +44,28 @@ def test_model_shapes_on_cpu():
     assert s4conv.rmsle(m(x), t).ndim == 0
 
 
+def test_channels_last_block_matches_channels_first_block_on_cpu():
+    """The block's [B, L, H] path (no transposes, 1x1 conv as a linear map over
+    the last dimension) computes what its [B, H, L] path computes."""
+    def conv_cl(x, k):  # the reference conv, applied to channels-last tensors
+        return reference_torch.depthwise_same(x.transpose(1, 2), k).transpose(1, 2).contiguous()
+    conv_cl.channels_last = True
+    torch.manual_seed(1)
+    m_cl = s4conv.Model(hidden_dim=16, state_dim=8, num_blocks=2, dropout=0.0, conv=conv_cl)
+    m_cf = copy.deepcopy(m_cl)
+    for blk in m_cf.blocks:
+        blk.kernel_layer.conv = reference_torch.depthwise_same
+    assert m_cl.blocks[0].kernel_layer.channels_last and not m_cf.blocks[0].kernel_layer.channels_last
+    x, target = s4conv.synthetic_batch(6, device="cpu", seed=3)
+    l_cl = s4conv.rmsle(m_cl(x), target)
+    l_cf = s4conv.rmsle(m_cf(x), target)
+    torch.testing.assert_close(l_cl, l_cf, rtol=1e-5, atol=1e-6)
+    l_cl.backward()
+    l_cf.backward()
+    for (name, a), b in zip(m_cl.named_parameters(), m_cf.parameters()):
+        torch.testing.assert_close(a.grad, b.grad, rtol=1e-4, atol=1e-6, msg=name)
+
+
 @pytest.mark.gpu
 def test_native_model_matches_reference_conv_model_through_a_training_step():
     if not torch.cuda.is_available():
