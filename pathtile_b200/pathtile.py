@@ -35,6 +35,7 @@ from __future__ import annotations
 import argparse
 import csv
 import json
+import math
 import statistics
 import time
 import zlib
@@ -267,6 +268,84 @@ def regret_table(summary: list[dict], policy: dict[str, dict[str, tuple[int, int
     return rows
 
 
+# ---------------------------------------------------------------------------
+# Selector baselines (the reference's scripts/evaluate_selector_baselines.py):
+# static policies scored against the per-shape oracle on a shape set.
+# ---------------------------------------------------------------------------
+# The reference runtime's defaults (WARPS_PER_BLOCK = 4 -> 128 rows, BWDK_BLOCK,
+# kernels/warp_tiled_ampere.py:668-672) on this library's candidate axes.
+DEFAULT_POLICY = {"fwd": (128, 3, 2, 1), "bwd_input": (128, 3, 2, 1), "bwd_weight": (128, 2, 2, 1)}
+
+
+def majority_winner_policy(summary: list[dict]) -> dict[str, tuple[int, int, int, int]]:
+    """Per path, the candidate that is fastest on the most shapes (per-shape ties
+    to the smaller candidate, then most wins, ties to the smaller candidate)."""
+    policy = {}
+    for path in PATHS:
+        best: dict[str, tuple[float, tuple]] = {}
+        for r in summary:
+            if r["phase"] != path:
+                continue
+            key = (float(r["mean_ms"]), _cand(r))
+            if r["config_id"] not in best or key < best[r["config_id"]]:
+                best[r["config_id"]] = key
+        if not best:
+            raise ValueError(f"No rows for {path}")
+        wins: dict[tuple, int] = {}
+        for _, cand in best.values():
+            wins[cand] = wins.get(cand, 0) + 1
+        policy[path] = min(wins, key=lambda c: (-wins[c], c))
+    return policy
+
+
+def evaluate_baselines(train: list[dict], evalset: list[dict]) -> tuple[list[dict], dict]:
+    """Per shape of `evalset`: total FWD + dX + dK latency of each static policy
+    chosen on `train` -- default, global (the frozen PathTile rule), majority
+    winner -- and of a uniformly random static candidate (expected latency: the
+    mean over candidates, per path), against the per-shape oracle."""
+    global_pol = select_policy(train)
+    policies = {
+        "default": DEFAULT_POLICY,
+        "global": {p: global_pol[p]["medium"] for p in PATHS},
+        "majority_winner": majority_winner_policy(train),
+    }
+    lookup: dict[tuple, float] = {}
+    per_path: dict[tuple, list[float]] = {}
+    for r in evalset:
+        lookup[(r["config_id"], r["phase"], *_cand(r))] = float(r["mean_ms"])
+        per_path.setdefault((r["config_id"], r["phase"]), []).append(float(r["mean_ms"]))
+    best = oracle_totals(evalset)
+    rows = []
+    for cid in sorted(best):
+        if any(p not in best[cid] for p in PATHS):
+            continue
+        oracle = sum(best[cid][p] for p in PATHS)
+        row = {"config_id": cid, "oracle_total_ms": oracle}
+        for name, pol in policies.items():
+            keys = [(cid, p, *pol[p]) for p in PATHS]
+            total = sum(lookup[k] for k in keys) if all(k in lookup for k in keys) else float("nan")
+            row[f"{name}_total_ms"] = total
+            row[f"{name}_regret_pct"] = 100.0 * (total / oracle - 1.0)
+        rnd = sum(statistics.mean(per_path[(cid, p)]) for p in PATHS)
+        row["random_fixed_total_ms"] = rnd
+        row["random_fixed_regret_pct"] = 100.0 * (rnd / oracle - 1.0)
+        rows.append(row)
+    summary = {"shapes": len(rows),
+               "policies": {name: {p: list(c) for p, c in pol.items()} for name, pol in policies.items()}}
+    for name in (*policies, "random_fixed"):
+        vals = [r[f"{name}_regret_pct"] for r in rows if r[f"{name}_regret_pct"] == r[f"{name}_regret_pct"]]
+        if not vals:
+            continue
+        summary[name] = {
+            "mean_regret_pct": statistics.mean(vals),
+            "geomean_regret_pct": 100.0 * (math.exp(statistics.mean(math.log1p(v / 100.0) for v in vals)) - 1.0),
+            "max_regret_pct": max(vals),
+            "within_2pct": sum(v <= 2.0 for v in vals),
+            "shapes": len(vals),
+        }
+    return rows, summary
+
+
 def select_engines(rows: list[dict]) -> dict[str, dict[str, str]]:
     """Engine per path and intensity class from engine-sweep rows (config_id,
     phase, engine, L, K, mean_ms): "tensor" where its summed latency over the
@@ -402,6 +481,10 @@ def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: 
     torch.backends.cuda.matmul.allow_tf32 = False
     dev = torch.device("cuda", torch.cuda.current_device())
     out.mkdir(parents=True, exist_ok=True)
+    # The candidates are launch configurations of the CUDA-core kernels: keep
+    # every path on them for the sweep (the tensor engine ignores these knobs).
+    for p in PATHS:
+        ops.set_engine(p, "ffma")
     order = cases if trial % 2 else list(reversed(cases))
     cands = candidates() if trial % 2 else list(reversed(candidates()))
     raw_rows, summ = [], []
@@ -477,6 +560,7 @@ def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: 
         torch.cuda.empty_cache()
     for p in PATHS:
         ops.set_config(p, 0)
+        ops.set_engine(p, None)
     _write_csv(out / "raw.csv", raw_rows)
     _write_csv(out / "summary.csv", summ)
     (out / "metadata.json").write_text(json.dumps({
@@ -489,7 +573,8 @@ def run_sweep(cases: list[ShapeCase], warmup: int, runs: int, trial: int, seed: 
                                  "candidate_order": "round-robin, direction alternating per visit; "
                                                     "reversed on even trials",
                                  "shape_order": "listed on odd trials; reversed on even trials",
-                                 "figure": "median over visits of the per-visit mean"}},
+                                 "figure": "median over visits of the per-visit mean",
+                                 "engine": "ffma on every path (the candidates are its launch knobs)"}},
         indent=1))
 
 
@@ -599,7 +684,7 @@ def aggregate_trials(root: Path) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--mode", choices=("run", "aggregate", "regret", "engines"), required=True)
+    ap.add_argument("--mode", choices=("run", "aggregate", "regret", "engines", "baselines"), required=True)
     ap.add_argument("--preset", default="pathtile-train", choices=sorted(PRESETS))
     ap.add_argument("--out", type=Path, required=True, help="results directory of this preset")
     ap.add_argument("--trial", type=int, default=1)
@@ -612,7 +697,19 @@ def main() -> None:
     ap.add_argument("--per-class", action="store_true", help="aggregate: select per intensity class")
     ap.add_argument("--policy", type=Path, help="regret: frozen_config.json to score")
     ap.add_argument("--engines", type=Path, help="aggregate: engine_policy.json to include in the header")
+    ap.add_argument("--train-csv", type=Path, help="baselines: candidate summary of the tuning shapes")
+    ap.add_argument("--eval-csv", type=Path, help="baselines: candidate summary of the shapes to score "
+                    "(default: aggregate the trials under --out)")
     args = ap.parse_args()
+    if args.mode == "baselines":
+        train = _read_csv(args.train_csv)
+        evalset = _read_csv(args.eval_csv) if args.eval_csv else aggregate_trials(args.out)
+        rows, summary = evaluate_baselines(train, evalset)
+        args.out.mkdir(parents=True, exist_ok=True)
+        _write_csv(args.out / "selector_baselines_per_shape.csv", rows)
+        (args.out / "selector_baselines_summary.json").write_text(json.dumps(summary, indent=1))
+        print(json.dumps(summary, indent=1))
+        return
     if args.mode == "engines":
         rows = run_engine_sweep(cases_for_preset(args.preset), args.warmup, args.runs, args.seed, args.out,
                                 reps=args.reps)

@@ -184,3 +184,34 @@ def test_apply_engines_rewrites_only_the_engine_table():
 
 def test_tensor_applicable_means_full_tiles():
     assert [L for L in range(1, 49) if pt.tensor_applicable(L)] == [4, 8, 12, 16, 24, 48]
+
+
+def _cand_rows(cid, phase, times):
+    """Summary rows of one (shape, phase): {candidate tuple: mean_ms}."""
+    return [{"config_id": cid, "phase": phase, "rows": c[0], "stages": c[1], "ctas_per_sm": c[2],
+             "threads_per_row": c[3], "L": 48, "K": 48, "mean_ms": v} for c, v in times.items()]
+
+
+def test_selector_baselines_against_hand_computed_regret():
+    A, B2, C = (128, 3, 2, 1), (128, 2, 2, 1), (256, 3, 1, 1)
+    train = []
+    # Candidate A wins two shapes by a hair, C wins one by a lot: the global
+    # (sum) rule picks C, the majority-winner rule picks A.
+    for cid, ta, tc in (("s1", 1.0, 1.01), ("s2", 1.0, 1.01), ("s3", 3.0, 1.0)):
+        for ph in pt.PATHS:
+            train += _cand_rows(cid, ph, {A: ta, B2: 5.0, C: tc})
+    assert pt.majority_winner_policy(train) == {p: A for p in pt.PATHS}
+    evalset = []
+    for ph in pt.PATHS:
+        evalset += _cand_rows("e1", ph, {A: 2.0, B2: 4.0, C: 1.0})
+    rows, summary = pt.evaluate_baselines(train, evalset)
+    assert len(rows) == 1
+    r = rows[0]
+    assert r["oracle_total_ms"] == pytest.approx(3.0)
+    assert r["global_regret_pct"] == pytest.approx(0.0)
+    assert r["majority_winner_regret_pct"] == pytest.approx(100.0)
+    # default policy: FWD/dX A (2.0 each), dK B2 (4.0) -> 8.0 / 3.0
+    assert r["default_regret_pct"] == pytest.approx(100.0 * (8.0 / 3.0 - 1.0))
+    # random fixed: mean over the three candidates per path = 7/3, times three paths
+    assert r["random_fixed_regret_pct"] == pytest.approx(100.0 * (7.0 / 3.0 - 1.0))
+    assert summary["global"]["shapes"] == 1 and summary["global"]["within_2pct"] == 1
