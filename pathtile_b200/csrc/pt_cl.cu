@@ -71,6 +71,83 @@ __global__ void __launch_bounds__(CH * ROWS)
   }
 }
 
+// The same convolution with the input rows staged through shared memory: each
+// warp walks `rows` batch rows (b = b0 + warp, + ROWS, ...) and prefetches the
+// next row with 16-byte cp.async while it computes the current one, so its
+// loads overlap its FMAs (the direct kernel above waits for every row it
+// loads).  Needs H % 4 == 0 (16-byte aligned row segments).
+__device__ __forceinline__ void cl_cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+
+template <int LMAX, int KMAX, bool REV>
+__global__ void __launch_bounds__(CH * ROWS)
+    cl_conv_pipe_kernel(const float* __restrict__ in, const float* __restrict__ k, float* __restrict__ out, int B,
+                        int L, int H, int K, int rows) {
+  __shared__ __align__(16) float buf[2][ROWS][LMAX][CH];
+  const int tx = static_cast<int>(threadIdx.x), ty = static_cast<int>(threadIdx.y);
+  const int h0 = static_cast<int>(blockIdx.x) * CH;
+  const int h = h0 + tx;
+  constexpr int PMAX = REV ? KMAX / 2 - 1 : KMAX / 2;
+  const int pad = REV ? (K - 1 - K / 2) : K / 2;
+  const int s = PMAX - pad;
+  float w[KMAX];
+#pragma unroll
+  for (int jp = 0; jp < KMAX; ++jp) {
+    const int j = jp - s;
+    w[jp] = (h < H && j >= 0 && j < K) ? __ldg(k + static_cast<size_t>(h) * K + (REV ? K - 1 - j : j)) : 0.f;
+  }
+  const int bfirst = static_cast<int>(blockIdx.y) * ROWS * rows + ty;
+  // Lane tx copies 16-byte chunks id = tx + 32 m of the row: t = id / 8, part id % 8.
+  auto prefetch = [&](int b, int st) {
+    if (b < B) {
+#pragma unroll
+      for (int m = 0; m < LMAX * CH / 4 / 32; ++m) {
+        const int id = tx + 32 * m;
+        const int t = id >> 3, part = id & 7;
+        if (t < L && h0 + 4 * part < H)
+          cl_cp_async16(&buf[st][ty][t][4 * part], in + (static_cast<size_t>(b) * L + t) * H + h0 + 4 * part);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  prefetch(bfirst, 0);
+  for (int i = 0; i < rows; ++i) {
+    const int b = bfirst + i * ROWS;
+    if (b >= B) break;
+    prefetch(b + ROWS, (i + 1) & 1);
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncwarp();
+    const int st = i & 1;
+    float v[LMAX];
+#pragma unroll
+    for (int t = 0; t < LMAX; ++t) v[t] = (t < L) ? buf[st][ty][t][tx] : 0.f;
+    __syncwarp();  // the buffer is refilled by the next iteration's prefetch
+    if (h < H) {
+      const size_t base = static_cast<size_t>(b) * L * H + h;
+#pragma unroll
+      for (int t0 = 0; t0 < LMAX; t0 += 4) {
+        if (t0 < L) {
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int jp = 0; jp < KMAX; ++jp)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int ii = t0 + u + jp - PMAX;
+              if (ii >= 0 && ii < LMAX) acc[u] = fmaf(w[jp], v[ii], acc[u]);
+            }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (t0 + u < L) out[base + static_cast<size_t>(t0 + u) * H] = acc[u];
+        }
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 template <int LMAX, int KMAX>
 __global__ void __launch_bounds__(CH * ROWS)
     cl_dk_kernel(const float* __restrict__ dy, const float* __restrict__ x, float* __restrict__ partial, int B,
@@ -134,6 +211,17 @@ namespace {
 int bucket(int n) { return n <= 16 ? 16 : (n <= 32 ? 32 : 48); }
 
 template <bool REV>
+const void* conv_pipe_func(int lmax, int kmax) {
+#define PT_CL_CONV(LM, KM) \
+  if (lmax == LM && kmax == KM) return reinterpret_cast<const void*>(&cl_conv_pipe_kernel<LM, KM, REV>);
+  PT_CL_CONV(16, 16) PT_CL_CONV(16, 32) PT_CL_CONV(16, 48)
+  PT_CL_CONV(32, 16) PT_CL_CONV(32, 32) PT_CL_CONV(32, 48)
+  PT_CL_CONV(48, 16) PT_CL_CONV(48, 32) PT_CL_CONV(48, 48)
+#undef PT_CL_CONV
+  return nullptr;
+}
+
+template <bool REV>
 const void* conv_func(int lmax, int kmax) {
 #define PT_CL_CONV(LM, KM) \
   if (lmax == LM && kmax == KM) return reinterpret_cast<const void*>(&cl_conv_kernel<LM, KM, REV>);
@@ -172,6 +260,20 @@ int dk_slices(int B, int L, int H, int K, int sm_count) {
 
 cudaError_t launch_conv(const float* in, const float* k, float* out, int B, int L, int H, int K, bool rev,
                         cudaStream_t stream) {
+  if (H % 4 == 0) {
+    // Pipelined form: each warp streams kRowsPerWarp batch rows.
+    constexpr int kRowsPerWarp = 8;
+    const void* fp =
+        rev ? conv_pipe_func<true>(bucket(L), bucket(K)) : conv_pipe_func<false>(bucket(L), bucket(K));
+    if (!fp) return cudaErrorInvalidValue;
+    const long long groups = (static_cast<long long>(B) + ROWS * kRowsPerWarp - 1) / (ROWS * kRowsPerWarp);
+    if (groups <= 65535) {
+      int rows = kRowsPerWarp;
+      dim3 grid((H + CH - 1) / CH, static_cast<unsigned>(groups)), block(CH, ROWS);
+      void* args[] = {const_cast<float**>(&in), const_cast<float**>(&k), &out, &B, &L, &H, &K, &rows};
+      return cudaLaunchKernel(fp, grid, block, args, 0, stream);
+    }
+  }
   const void* f = rev ? conv_func<true>(bucket(L), bucket(K)) : conv_func<false>(bucket(L), bucket(K));
   if (!f) return cudaErrorInvalidValue;
   // gridDim.y holds batch rows / ROWS and is limited to 65535: launch in chunks.
