@@ -114,9 +114,10 @@ PT_API int pt_dk_noalloc(const float* dy, const float* x, float* dk, int B, int 
 
 /*
  * Input and filter gradients in one call: dx as pt_dx, dk as pt_dk (same
- * modes and workspace rules; query pt_dx_dk_workspace_bytes).  For L = 48 and
- * K in {3, 8, 16, 24, 32, 48}, where dX runs on the tensor engine and the grid
- * can give every CTA a single channel, one fused kernel reads dy and x once and
+ * modes and workspace rules; query pt_dx_dk_workspace_bytes).  For rows of
+ * 32 < L <= 48 columns with L % 4 == 0 and any K <= 48, unless dX is forced onto
+ * the CUDA cores (pt_set_engine), and where the grid can give every CTA a
+ * single channel, one fused kernel reads dy and x once and
  * writes dx (dX on the tensor cores, dK on the CUDA cores; no workspace when
  * each channel has one CTA); other shapes run pt_dx then pt_dk.  The reference
  * launches the two separately (DepthConvAmpere.backward,

@@ -489,12 +489,14 @@ int launch_tensor_dk(const Plan& p, const float* dy, const float* x, float* dk, 
 }
 
 // Fused backward (dX on the tensor cores, dK on the CUDA cores, one pass over dy
-// and x): L = 48 with a fused instantiation, dX on the tensor engine at this
-// shape, and a grid in which every CTA keeps one channel (a multiple of H that
-// keeps >= 3/4 of the SMs busy).  G == H makes each CTA's partial its channel's dK.
+// and x): rows of 32 < L <= 48 columns with L % 4 == 0 and any K <= 48 (the
+// kernel's 48-column layout), dX not forced onto the CUDA cores, and a grid in
+// which every CTA keeps one channel (a multiple of H that keeps >= 3/4 of the
+// SMs busy).  G == H makes each CTA's partial its channel's dK.
 bool plan_fused(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   const void* func = pt::tc::bwd_func(L, K);
-  if (!func || engine_for(PT_PATH_DX, B, H, L, K, di.sm_count) != PT_ENGINE_TENSOR) return false;
+  if (!func || g_encode == nullptr) return false;
+  if (g_engine_override[PT_PATH_DX] >= 0 && g_engine_override[PT_PATH_DX] != PT_ENGINE_TENSOR) return false;
   if (static_cast<long long>(pt::tc::bwd_smem()) > di.max_smem) return false;
   const long long tiles = tensor_tiles(PT_PATH_DX, B, H);
   const int gmax = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);

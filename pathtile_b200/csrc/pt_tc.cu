@@ -1,7 +1,6 @@
 // pt_tc.cu -- instantiations of the tensor-core FWD / DX kernels.
 #include "pathtile_b200.h"
 #include "pt_tc.h"
-#include "pt_tc_bwd.cuh"
 #include "pt_tc_dk.cuh"
 #include "pt_tc_kernels.cuh"
 
@@ -65,19 +64,14 @@ __global__ void __launch_bounds__(256) tc_dk_reduce_kernel(const float* __restri
 }
 
 const void* bwd_func(int L, int K) {
-  if (L != BWD_L) return nullptr;
-  switch (K) {
-    case 3: return reinterpret_cast<const void*>(&tc_bwd_kernel<3>);
-    case 8: return reinterpret_cast<const void*>(&tc_bwd_kernel<8>);
-    case 16: return reinterpret_cast<const void*>(&tc_bwd_kernel<16>);
-    case 24: return reinterpret_cast<const void*>(&tc_bwd_kernel<24>);
-    case 32: return reinterpret_cast<const void*>(&tc_bwd_kernel<32>);
-    case 48: return reinterpret_cast<const void*>(&tc_bwd_kernel<48>);
-    default: return nullptr;
-  }
+  // One 48-column tile layout (a 128-B and a 64-B box per row): rows shorter
+  // than 48 columns (32 < L < 48, L % 4 == 0) are zero-filled by the loads and
+  // clipped by the stores, which leaves dX and dK exact.
+  if (L % 4 != 0 || L <= 32 || L > 48 || K < 1 || K > 48) return nullptr;
+  return K <= 24 ? bwd_kernel_k1_24(K) : bwd_kernel_k25_48(K);
 }
 
-size_t bwd_smem() { return BwdGeo::SMEM; }
+size_t bwd_smem() { return bwd_smem_bytes(); }
 
 void dk_reduce(const float* partial, const int* group_of, int n_slots, int H, int K, int hc, float* dk,
                int accumulate, void* stream) {

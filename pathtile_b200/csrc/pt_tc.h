@@ -55,9 +55,13 @@ void dk_reduce(const float* partial, const int* group_of, int n_slots, int H, in
 namespace pt {
 namespace tc {
 
-// Fused backward (dX on the tensor cores + dK on the CUDA cores) for L = 48 and
-// K in {3, 8, 16, 24, 32, 48}; nullptr otherwise.
+// Fused backward (dX on the tensor cores + dK on the CUDA cores) for any K <= 48
+// and rows of 32 < L <= 48 columns with L % 4 == 0; nullptr otherwise.
 const void* bwd_func(int L, int K);
+// The fused kernel's instantiations, one per K (pt_tc_bwd_k1.cu, pt_tc_bwd_k2.cu).
+const void* bwd_kernel_k1_24(int K);
+const void* bwd_kernel_k25_48(int K);
+size_t bwd_smem_bytes();
 size_t bwd_smem();
 
 }  // namespace tc

@@ -1,5 +1,5 @@
 // pt_tc_bwd.cuh -- fused backward: dX on the tensor cores and dK on the CUDA
-// cores, in one pass over dy and x (L = 48).
+// cores, in one pass over dy and x (rows of up to 48 columns).
 //
 // Separately, dX reads dy and writes dx, and dK reads dy and x: four [B, H, L]
 // streams.  Here one kernel reads dy and x once and writes dx (three streams),

@@ -214,8 +214,8 @@ def dx_dk(
     workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Both backward products in one call: returns gx = dX(dy, k) and writes the
-    filter gradient into gk with dk()'s modes.  For L = 48 and K in {3, 8, 16,
-    24, 32, 48} on grids that give each CTA one channel this is one fused kernel
+    filter gradient into gk with dk()'s modes.  For 32 < L <= 48 (L % 4 == 0)
+    and any K on grids that give each CTA one channel this is one fused kernel
     (dy and x read once); other shapes run dx() then dk().  The reference's
     backward launches the two separately (kernels/warp_tiled_ampere.py:882-898).
     """

@@ -3,7 +3,8 @@ the CUDA cores) reached through ops.dx_dk / pt_dx_dk.
 
 Bars as for the separate kernels: dX within rtol = atol = 1e-5 of the FP64 C
 oracle, dK within 1e-4 relative of the FP64 dK.  Covered: every fused
-instantiation (L = 48, K in {3, 8, 16, 24, 32, 48}), both dK regimes of the
+instantiation class (every K <= 48; rows of 32 < L <= 48 columns, L % 4 == 0,
+in the kernel's 48-column layout), both dK regimes of the
 fused kernel (one CTA per channel writes dK directly; several CTAs per channel
 write partials summed by the reduce kernel), the three dK modes, ragged batch
 tiles, grids smaller than the SM count, and shapes that fall back to pt_dx +
@@ -22,7 +23,8 @@ pytestmark = pytest.mark.gpu
 
 FWD_TOL = dict(rtol=1e-5, atol=1e-5)
 DK_RTOL = 1e-4
-FUSED_K = (3, 8, 16, 24, 32, 48)
+def _fusable_layout(L, K) -> bool:
+    return 32 < L <= 48 and L % 4 == 0 and 1 <= K <= 48
 
 
 def assert_dk_close(got: np.ndarray, ref64: np.ndarray) -> None:
@@ -40,9 +42,9 @@ def _sm_count(dev) -> int:
 
 
 def _expect_fused(B, H, L, K, sm) -> bool:
-    """The host rule: L = 48, a fused K, and a grid of whole channels (a
-    multiple of H) that keeps at least 3/4 of min(tiles, SMs) busy."""
-    if L != 48 or K not in FUSED_K:
+    """The host rule: 32 < L <= 48 with L % 4 == 0, any K <= 48, and a grid of
+    whole channels (a multiple of H) that keeps at least 3/4 of min(tiles, SMs) busy."""
+    if not _fusable_layout(L, K):
         return False
     gmax = min(-(-B // 128) * H, sm)
     G = (gmax // H) * H
@@ -72,6 +74,14 @@ SHAPES = [
     (1, 4, 48, 48),       # one row, four CTAs
     (5000, 74, 48, 32),   # 2 CTAs per channel
     (64, 1, 48, 3),
+    (700, 128, 48, 5),    # K not among the CUDA-core kernels' specialisations
+    (300, 128, 48, 47),   # odd K, the largest register spill
+    (250, 128, 48, 1),
+    (1000, 128, 44, 44),  # 44-column rows in the 48-column layout
+    (513, 64, 40, 40),
+    (400, 128, 40, 13),
+    (129, 128, 36, 36),
+    (600, 128, 36, 8),
 ]
 
 
@@ -87,7 +97,7 @@ def test_fused_backward_against_fp64_oracle(cuda_device, B, H, L, K, mode):
     assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
 
 
-@pytest.mark.parametrize("B,H,L,K", [(300, 96, 48, 48), (200, 8, 40, 40), (100, 5, 48, 5), (64, 300, 48, 48)])
+@pytest.mark.parametrize("B,H,L,K", [(300, 96, 48, 48), (200, 8, 42, 40), (100, 5, 28, 5), (64, 300, 48, 48)])
 def test_unfused_shapes_fall_back_to_separate_kernels(cuda_device, B, H, L, K):
     dev = cuda_device
     assert not ops.fused_backward(B, H, L, K) or _sm_count(dev) < 128
