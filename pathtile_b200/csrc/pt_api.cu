@@ -188,13 +188,16 @@ long long tensor_tiles(int path, int B, int groups) {
 }
 
 // Engine of a path at a shape: PT_ENGINE_TENSOR (tcgen05, L % 4 == 0 and a TMA
-// encoder) or PT_ENGINE_FFMA (CUDA-core kernels, every shape).  The frozen
+// encoder) or PT_ENGINE_FFMA (CUDA-core kernels, every shape).  Shapes without
+// a specialised CUDA-core kernel take the tensor engine where it applies.  The frozen
 // table's tensor choice applies only to full tiles (48 % L == 0: one
 // 48-column channel or 48 / L packed channels per tile row; partially filled
 // tiles measured faster on the FFMA kernels) and needs a grid in which every
 // CTA visits at most two channel groups; an explicit pt_set_engine override
 // needs neither for FWD/DX (they rebuild the Toeplitz operand per tile
 // otherwise), while dK always needs its accumulators resident.
+const pt::Entry* find_entry(int L, int K);
+
 int engine_for(int path, int B, int H, int L, int K, int sm_count) {
   if (L % 4 != 0 || g_encode == nullptr) return PT_ENGINE_FFMA;
   const int groups = tensor_groups(H, L);
@@ -203,6 +206,13 @@ int engine_for(int path, int B, int H, int L, int K, int sm_count) {
   if (g_engine_override[path] >= 0) {
     if (path == PT_PATH_DK && period == 0) return PT_ENGINE_FFMA;
     return g_engine_override[path];
+  }
+  // The frozen table compares the tensor engine with the specialised CUDA-core
+  // kernels; a shape without one would run the generic kernels (runtime bounds,
+  // many times slower), so it takes the tensor engine wherever that applies.
+  if (find_entry(L, K) == nullptr) {
+    if (path == PT_PATH_DK) return period > 0 ? PT_ENGINE_TENSOR : PT_ENGINE_FFMA;
+    return PT_ENGINE_TENSOR;
   }
   if (48 % L != 0 || pt::kFrozenEngine[path][intensity_class(L, K)] != PT_ENGINE_TENSOR)
     return PT_ENGINE_FFMA;

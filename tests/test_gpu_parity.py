@@ -108,7 +108,7 @@ MID_SHAPES = [
     (130, 20, 40, 40),     # TMA path, several batches per tile, ragged last tile
     (37, 19, 23, 11),      # generic kernels (shape not specialised)
     (40, 63, 37, 13),      # generic kernels (H*L % 4 != 0 for odd L)
-    (5, 7, 48, 47),        # generic kernels, even/odd pad asymmetry
+    (5, 7, 48, 47),        # even/odd pad asymmetry (unspecialised: tensor engine by default)
     (1, 1, 1, 1),
     (3, 2, 1, 48),         # K > L
 ]
@@ -122,6 +122,35 @@ def test_mid_shapes_full_oracle(cuda_device, B, H, L, K, mode):
     np.testing.assert_allclose(y.cpu().numpy(), c_oracle.fwd(cpu[0], cpu[1]), **FWD_TOL)
     np.testing.assert_allclose(gx.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
     assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+
+
+@pytest.mark.parametrize("B,H,L,K", [(5, 7, 48, 47), (64, 24, 44, 44), (100, 16, 20, 7)])
+def test_generic_kernels_with_the_cuda_core_engine_forced(cuda_device, B, H, L, K):
+    """Shapes without a specialised CUDA-core kernel default to the tensor engine
+    where it applies; forced onto the CUDA cores they run the generic kernels."""
+    assert ops.config("fwd", B, H, L, K)["specialised"] == 0
+    paths = ("fwd", "bwd_input", "bwd_weight")
+    try:
+        for p in paths:
+            ops.set_engine(p, "ffma")
+        assert all(ops.config(p, B, H, L, K)["engine"] == "ffma" for p in paths)
+        x, k, dy, cpu = _inputs(B, H, L, K, 77, cuda_device)
+        y, gx, gk = run_path(x, k, dy)
+    finally:
+        for p in paths:
+            ops.set_engine(p, None)
+    np.testing.assert_allclose(y.cpu().numpy(), c_oracle.fwd(cpu[0], cpu[1]), **FWD_TOL)
+    np.testing.assert_allclose(gx.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
+    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+    assert ops.device_error() == 0
+
+
+def test_unspecialised_shapes_take_the_tensor_engine(cuda_device):
+    assert ops.config("fwd", 4096, 128, 44, 44)["specialised"] == 0
+    assert ops.config("fwd", 4096, 128, 44, 44)["engine"] == "tensor"
+    assert ops.config("bwd_input", 4096, 128, 44, 44)["engine"] == "tensor"
+    assert ops.config("fwd", 4096, 128, 40, 40)["engine"] == "ffma"  # specialised, partial tile
+    assert ops.config("fwd", 4096, 128, 37, 17)["engine"] == "ffma"  # L % 4 != 0
 
 
 @pytest.mark.parametrize("rows", [32, 64, 128, 256])
