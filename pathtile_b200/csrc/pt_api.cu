@@ -316,6 +316,30 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
   return PT_OK;
 }
 
+// Bucketed generic kernels (compile-time maxima 16 / 32 / 48 for L and K).
+int bucket48(int n) { return n <= 16 ? 16 : (n <= 32 ? 32 : 48); }
+
+template <int OP>
+const void* conv_bucket_func(int L, int K) {
+  const int lm = bucket48(L), km = bucket48(K);
+#define PT_CB(LM, KM) \
+  if (lm == LM && km == KM) return reinterpret_cast<const void*>(&pt::conv_bucket_kernel<LM, KM, OP>);
+  PT_CB(16, 16) PT_CB(16, 32) PT_CB(16, 48) PT_CB(32, 16) PT_CB(32, 32) PT_CB(32, 48)
+  PT_CB(48, 16) PT_CB(48, 32) PT_CB(48, 48)
+#undef PT_CB
+  return nullptr;
+}
+
+const void* dk_bucket_func(int L, int K) {
+  const int lm = bucket48(L), km = bucket48(K);
+#define PT_DB(LM, KM) \
+  if (lm == LM && km == KM) return reinterpret_cast<const void*>(&pt::dk_bucket_kernel<LM, KM>);
+  PT_DB(16, 16) PT_DB(16, 32) PT_DB(16, 48) PT_DB(32, 16) PT_DB(32, 32) PT_DB(32, 48)
+  PT_DB(48, 16) PT_DB(48, 32) PT_DB(48, 48)
+#undef PT_DB
+  return nullptr;
+}
+
 void plan_generic_dk(int B, int H, int L, int K, const DeviceInfo& di, Plan& p) {
   pt::TileGeom& g = p.g;
   g.B = B;
@@ -325,7 +349,12 @@ void plan_generic_dk(int B, int H, int L, int K, const DeviceInfo& di, Plan& p) 
   g.Th = H;
   g.Tb = 1;
   g.nhb = 1;
-  int G = di.sm_count * 4;
+  // One wave of CTAs at the bucketed kernel's occupancy.
+  int per_sm = 0;
+  const void* f = dk_bucket_func(L, K);
+  if (!f || cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, 128, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 2;
+  int G = di.sm_count * per_sm;
   if (G > B) G = B;
   if (G < 1) G = 1;
   g.G = G;
@@ -610,13 +639,11 @@ int launch_rows(int path, const float* in, const float* taps, float* out, int B,
     const long long n_tiles = (S + kGenericRows - 1) / kGenericRows;
     long long grid = static_cast<long long>(di->sm_count) * 8;
     if (grid > n_tiles) grid = n_tiles;
-    if (path == PT_PATH_FWD)
-      pt::conv_generic_kernel<pt::OP_FWD><<<static_cast<unsigned>(grid), kGenericRows, 0, stream>>>(
-          in, taps, out, B, H, L, K, n_tiles);
-    else
-      pt::conv_generic_kernel<pt::OP_DX><<<static_cast<unsigned>(grid), kGenericRows, 0, stream>>>(
-          in, taps, out, B, H, L, K, n_tiles);
-    ce = cudaGetLastError();
+    const void* f = (path == PT_PATH_FWD) ? conv_bucket_func<pt::OP_FWD>(L, K) : conv_bucket_func<pt::OP_DX>(L, K);
+    if (!f) return PT_ERR_UNSUPPORTED;
+    long long nt = n_tiles;
+    void* args[] = {const_cast<float**>(&in), const_cast<float**>(&taps), &out, &B, &H, &L, &K, &nt};
+    ce = cudaLaunchKernel(f, dim3(static_cast<unsigned>(grid)), dim3(kGenericRows), args, 0, stream);
   }
   if (ce != cudaSuccess) return cuda_fail(ce);
   return PT_OK;
@@ -695,8 +722,11 @@ int pt_dk(const float* dy, const float* x, float* dk, int B, int H, int L, int K
                     const_cast<int*>(&atomic_mode), &err};
     ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
   } else {
-    pt::dk_generic_kernel<<<g.G, 128, 0, stream>>>(dy, x, dst, B, H, L, K, g.G, atomic_mode);
-    ce = cudaGetLastError();
+    const void* f = dk_bucket_func(L, K);
+    if (!f) return PT_ERR_UNSUPPORTED;
+    int gG = g.G, am = atomic_mode;
+    void* args[] = {const_cast<float**>(&dy), const_cast<float**>(&x), &dst, &B, &H, &L, &K, &gG, &am};
+    ce = cudaLaunchKernel(f, dim3(g.G), dim3(128), args, 0, stream);
   }
   if (ce != cudaSuccess) return cuda_fail(ce);
   if (!atomic_mode) {
@@ -847,11 +877,11 @@ int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n) {
     threads = (path == PT_PATH_DK) ? 128 : kGenericRows;
     dyn = 0;
     if (path == PT_PATH_FWD)
-      func = reinterpret_cast<const void*>(&pt::conv_generic_kernel<pt::OP_FWD>);
+      func = conv_bucket_func<pt::OP_FWD>(L, K);
     else if (path == PT_PATH_DX)
-      func = reinterpret_cast<const void*>(&pt::conv_generic_kernel<pt::OP_DX>);
+      func = conv_bucket_func<pt::OP_DX>(L, K);
     else
-      func = reinterpret_cast<const void*>(&pt::dk_generic_kernel);
+      func = dk_bucket_func(L, K);
     if (path != PT_PATH_DK) {
       const long long S = static_cast<long long>(B) * H;
       const long long n_tiles = (S + kGenericRows - 1) / kGenericRows;

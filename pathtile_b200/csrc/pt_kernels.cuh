@@ -652,46 +652,142 @@ __global__ void __launch_bounds__(288, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Generic kernels: any L <= 48, K <= 48, any alignment of H*L.  Tiles of
-// `rows` contiguous rows are staged in shared memory by coalesced loads; the
-// tap loops run on runtime bounds.  They carry every shape the specialised
-// table does not, at lower FFMA density.
+// Generic kernels: shapes outside the specialisation table (any L <= 48,
+// K <= 48, any alignment of H*L), with the
+// nests compiled for maxima LMAX, KMAX in {16, 32, 48} and the runtime L, K
+// taken by zero-padding the row past L and shifting the taps by
+// s = PMAX - pad (tap register j' multiplies element t + j' - PMAX; PMAX =
+// KMAX/2 for FWD / dK, KMAX/2 - 1 for dX, which keeps s >= 0 and s + K <= KMAX
+// for every K <= KMAX).  Rows and taps live in registers, so the FMAs are
+// compile-time; the staging is the generic kernels' coalesced one.
 // ---------------------------------------------------------------------------
-template <int OP>
+template <int LMAX, int KMAX, int OP>
 __global__ void __launch_bounds__(128)
-    conv_generic_kernel(const float* __restrict__ in, const float* __restrict__ taps_hk,
-                        float* __restrict__ out, int B, int H, int L, int K, long long n_tiles) {
+    conv_bucket_kernel(const float* __restrict__ in, const float* __restrict__ taps_hk, float* __restrict__ out,
+                       int B, int H, int L, int K, long long n_tiles) {
   static_assert(OP == OP_FWD || OP == OP_DX, "FWD or DX");
   constexpr int ROWS = 128;
-  __shared__ float s_in[ROWS * 48];
-  __shared__ float s_out[ROWS * 48];
+  constexpr int PMAX = (OP == OP_FWD) ? KMAX / 2 : KMAX / 2 - 1;
+  __shared__ float s_io[ROWS * 48];
   const int tid = static_cast<int>(threadIdx.x);
   const long long S = static_cast<long long>(B) * H;
   const int pad = (OP == OP_FWD) ? (K / 2) : (K - 1 - K / 2);
+  const int s = PMAX - pad;
   for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
     const long long r0 = tile * ROWS;
     const int nrows = static_cast<int>(min(static_cast<long long>(ROWS), S - r0));
     const int nelem = nrows * L;
     const float* src = in + r0 * L;
-    for (int e = tid; e < nelem; e += ROWS) s_in[e] = src[e];
+    for (int e = tid; e < nelem; e += ROWS) s_io[e] = src[e];
     __syncthreads();
+    float v[LMAX];
+    float w[KMAX];
     if (tid < nrows) {
+#pragma unroll
+      for (int t = 0; t < LMAX; ++t) v[t] = (t < L) ? s_io[tid * L + t] : 0.f;
       const int hh = static_cast<int>((r0 + tid) % H);
       const float* kp = taps_hk + static_cast<long long>(hh) * K;
-      const float* xr = s_in + tid * L;
-      for (int t = 0; t < L; ++t) {
-        float acc = 0.0f;
-        for (int j = 0; j < K; ++j) {
-          const int i = t + j - pad;
-          const float kv = (OP == OP_FWD) ? __ldg(kp + j) : __ldg(kp + (K - 1 - j));
-          if (i >= 0 && i < L) acc = fmaf(xr[i], kv, acc);
+#pragma unroll
+      for (int jp = 0; jp < KMAX; ++jp) {
+        const int j = jp - s;
+        w[jp] = (j >= 0 && j < K) ? __ldg(kp + (OP == OP_FWD ? j : K - 1 - j)) : 0.f;
+      }
+    }
+    __syncthreads();  // the rows are in registers: the tile buffer takes the outputs
+    if (tid < nrows) {
+#pragma unroll
+      for (int t0 = 0; t0 < LMAX; t0 += 4) {
+        if (t0 < L) {
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int jp = 0; jp < KMAX; ++jp)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = t0 + u + jp - PMAX;
+              if (i >= 0 && i < LMAX) acc[u] = fmaf(w[jp], v[i], acc[u]);
+            }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (t0 + u < L) s_io[tid * L + t0 + u] = acc[u];
         }
-        s_out[tid * L + t] = acc;
       }
     }
     __syncthreads();
     float* dstp = out + r0 * L;
-    for (int e = tid; e < nelem; e += ROWS) dstp[e] = s_out[e];
+    for (int e = tid; e < nelem; e += ROWS) dstp[e] = s_io[e];
+    __syncthreads();
+  }
+}
+
+// dK pass 1 for the same shapes: CTA c owns the batches b = c, c + G, ... of
+// every channel (partial layout [G][K][H], reduced by dk_reduce_kernel; or
+// atomic adds into dk).  Per group of 32 channels, each warp takes a share of the CTA's
+// batches: it stages its 32 rows of x and dy (contiguous in [B, H, L]) through
+// shared memory, each lane takes its channel's two rows into registers and
+// accumulates the KMAX shifted taps; the warps' sums meet in a fixed order.
+template <int LMAX, int KMAX>
+__global__ void __launch_bounds__(128)
+    dk_bucket_kernel(const float* __restrict__ dy, const float* __restrict__ x, float* __restrict__ dst, int B,
+                     int H, int L, int K, int G, int atomic_mode) {
+  constexpr int PMAX = KMAX / 2;
+  // Row staging [warp][x|dy][32 rows x L]; after each channel group the same
+  // memory holds the warps' sums [warp][KMAX][33].
+  __shared__ float s_buf[4 * 2 * 32 * 48];
+  static_assert(4 * KMAX * 33 <= 4 * 2 * 32 * 48, "reduction fits the staging buffer");
+  auto s_rows = [&](int ww, int which) { return s_buf + (ww * 2 + which) * (32 * 48); };
+  auto s_red = [&](int ww, int jp) { return s_buf + (ww * KMAX + jp) * 33; };
+  const int lane = static_cast<int>(threadIdx.x) & 31;
+  const int w = static_cast<int>(threadIdx.x) >> 5;
+  const int c = static_cast<int>(blockIdx.x);
+  const int s = PMAX - K / 2;  // acc[j'] is the gradient of tap j' - s
+  for (int h0 = 0; h0 < H; h0 += 32) {
+    const int nch = min(32, H - h0);
+    float acc[KMAX];
+#pragma unroll
+    for (int jp = 0; jp < KMAX; ++jp) acc[jp] = 0.f;
+    for (int b = c + G * w; b < B; b += 4 * G) {
+      const long long row0 = (static_cast<long long>(b) * H + h0) * L;
+      const int nelem = nch * L;
+      float* sx = s_rows(w, 0);
+      float* sd = s_rows(w, 1);
+      for (int e = lane; e < nelem; e += 32) {
+        sx[e] = __ldg(x + row0 + e);
+        sd[e] = __ldg(dy + row0 + e);
+      }
+      __syncwarp();
+      if (lane < nch) {
+        float v[LMAX], d[LMAX];
+#pragma unroll
+        for (int t = 0; t < LMAX; ++t) {
+          v[t] = (t < L) ? sx[lane * L + t] : 0.f;
+          d[t] = (t < L) ? sd[lane * L + t] : 0.f;
+        }
+#pragma unroll
+        for (int t = 0; t < LMAX; ++t)
+#pragma unroll
+          for (int jp = 0; jp < KMAX; ++jp) {
+            const int i = t + jp - PMAX;
+            if (i >= 0 && i < LMAX) acc[jp] = fmaf(d[t], v[i], acc[jp]);
+          }
+      }
+      __syncwarp();  // the staging buffer is refilled for the next batch
+    }
+    __syncthreads();  // every warp is done with its staging rows
+#pragma unroll
+    for (int jp = 0; jp < KMAX; ++jp) s_red(w, jp)[lane] = acc[jp];
+    __syncthreads();
+    for (int idx = static_cast<int>(threadIdx.x); idx < K * 32; idx += 128) {
+      const int j = idx >> 5, ch = idx & 31;
+      if (ch < nch) {
+        const int jp = j + s;
+        const float sum = s_red(0, jp)[ch] + s_red(1, jp)[ch] + s_red(2, jp)[ch] + s_red(3, jp)[ch];
+        const int hh = h0 + ch;
+        if (atomic_mode)
+          atomicAdd(dst + static_cast<long long>(hh) * K + j, sum);
+        else
+          dst[(static_cast<long long>(c) * K + j) * H + hh] = sum;
+      }
+    }
     __syncthreads();
   }
 }
@@ -740,34 +836,6 @@ __global__ void __launch_bounds__(256) dk_reduce_kernel(const float* __restrict_
     for (int k = 0; k < 8; ++k) total += sums[k][lane];
     float* o = dk + static_cast<long long>(h) * g.K + j;
     *o = accumulate ? (*o + total) : total;
-  }
-}
-
-// Generic DK pass 1: CTA c owns the batches b = c, c+G, ... of every channel.
-// Block 128 threads; thread (hh, jj) pairs over a [H x K] grid in strides.
-// Writes partial[c][j][h] (layout [G][K][H], i.e. Th = H, nhb = 1).
-__global__ void __launch_bounds__(128)
-    dk_generic_kernel(const float* __restrict__ dy, const float* __restrict__ x,
-                      float* __restrict__ dst, int B, int H, int L, int K, int G, int atomic_mode) {
-  const int tid = static_cast<int>(threadIdx.x);
-  const int c = static_cast<int>(blockIdx.x);
-  const int pad = K / 2;
-  for (int p = tid; p < H * K; p += 128) {
-    const int hh = p / K;
-    const int j = p - hh * K;
-    float acc = 0.0f;
-    for (int b = c; b < B; b += G) {
-      const float* g1 = dy + (static_cast<long long>(b) * H + hh) * L;
-      const float* x1 = x + (static_cast<long long>(b) * H + hh) * L;
-      for (int t = 0; t < L; ++t) {
-        const int i = t + j - pad;
-        if (i >= 0 && i < L) acc = fmaf(__ldg(g1 + t), __ldg(x1 + i), acc);
-      }
-    }
-    if (atomic_mode)
-      atomicAdd(dst + static_cast<long long>(hh) * K + j, acc);
-    else
-      dst[(static_cast<long long>(c) * K + j) * H + hh] = acc;
   }
 }
 
