@@ -36,11 +36,11 @@ def shard_range(B: int, rank: int, world: int) -> tuple[int, int]:
 
 
 def native_compute(x: torch.Tensor, k: torch.Tensor, dy: torch.Tensor):
-    """FWD, dX and this shard's dK on the GPU through the native library."""
+    """FWD, dX and this shard's dK on the GPU through the native library (the
+    backward as one ops.dx_dk call: the fused kernel where the shape allows)."""
     y = ops.fwd(x, k)
-    gx = ops.dx(dy, k)
     gk = torch.empty_like(k)
-    ops.dk(dy, x, gk, mode="deterministic")
+    gx = ops.dx_dk(dy, x, k, gk, mode="deterministic")
     return y, gx, gk
 
 
