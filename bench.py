@@ -14,7 +14,7 @@ FWD+dX+dK (bytes per phase (2*B*H*L + H*K)*4, the reference's formula) over
 the device-timed step (CUDA events, max over ranks); ``aggregate_ms`` = sum of
 the three phases' separately timed mean latencies (the reference's headline
 protocol); ``roofline`` for the dominant kernel; ``cpu_baseline`` = the
-reference's PyTorch CPU path timed on this host; ``e2e`` = the same pass
+reference's PyTorch CPU path timed on this host (1-GPU runs only); ``e2e`` = the same pass
 through the host-buffer API (pinned host tensors, copies inside the timed
 region); ``clocks`` sampled by NVML during the timed region.
 
@@ -377,7 +377,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "clocks": clocks.summary(),
         "device_error_word": err,
     }
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:  # the CPU baseline belongs to the 1-GPU line
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     return result
 
