@@ -25,6 +25,7 @@ cores, on a bounded sample of the same workload, and prints the same metric.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -197,6 +198,7 @@ def apply_engine(ops, engine: str) -> None:
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     from pathtile_b200 import build, ops, runtime
+    from pathtile_b200 import host as hostmod
     from pathtile_b200.host import HostPipeline
 
     build.build()
@@ -265,6 +267,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                               "device_error_word": err}), flush=True)
         return None
     # End to end through the host-buffer API: pinned host inputs in, host outputs back.
+    # The host buffers are allocated (and the copies driven) from the CPUs local to
+    # this rank's GPU, then the process's own CPU set comes back for the CPU baseline.
+    numa = contextlib.ExitStack()
+    host_cpus = [] if args.no_numa_bind else numa.enter_context(hostmod.near_device(dev))
     pin = dict(device="cpu", pin_memory=True)
     x_h = torch.empty(B, H, L, **pin)
     dy_h = torch.empty(B, H, L, **pin)
@@ -295,6 +301,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         e2e_ms = float(t.item())
     h2d, d2h = pipe.bytes_per_call(B)
     err = ops.device_error()
+    numa.close()
 
     if rank != 0:
         return None
@@ -372,6 +379,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
             "api": "pathtile_b200.host.HostPipeline.run (pinned host tensors)",
+            "host_cpus": len(host_cpus) if host_cpus else None,
         },
         "gpu_launches": args.steps * (1 + (ops.dx_dk_launches(B, H, L, K) if fused else 3)),
         "clocks": clocks.summary(),
@@ -492,6 +500,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=B_PER_GPU,
                     help="batch per GPU (default: the primary workload; smaller only for profiling)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement (profiling)")
+    ap.add_argument("--no-numa-bind", action="store_true",
+                    help="e2e: leave host buffers where the OS puts them (default: near the GPU)")
     ap.add_argument("--backward", choices=("fused", "separate"), default="fused",
                     help="backward of the step: ops.dx_dk (one fused kernel where it applies) or dX then dK")
     ap.add_argument("--engine", choices=("frozen", "ffma", "tensor"), default="frozen",

@@ -12,9 +12,60 @@ on the host.
 """
 from __future__ import annotations
 
+import contextlib
+import os
+from typing import Iterator, Sequence
+
 import torch
 
 from . import ops
+
+
+def cpus_from_mask(words: Sequence[int]) -> list[int]:
+    """CPU ids set in an NVML CPU-affinity mask (bit i of 64-bit word w is CPU 64 w + i)."""
+    return [64 * w + i for w, word in enumerate(words) for i in range(64) if (int(word) >> i) & 1]
+
+
+def device_local_cpus(device: int | torch.device) -> list[int]:
+    """The CPUs NVML reports as local to `device` (its NUMA node), or [] when NVML
+    cannot say.  The GPU is found by PCI bus id, so CUDA_VISIBLE_DEVICES
+    renumbering does not matter."""
+    try:
+        import pynvml
+
+        props = torch.cuda.get_device_properties(device)
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, ((os.cpu_count() or 64) + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:  # no NVML or no such device: leave placement to the OS
+        return []
+    return cpus_from_mask(words)
+
+
+@contextlib.contextmanager
+def near_device(device: int | torch.device) -> Iterator[list[int]]:
+    """Run the block with the calling thread bound to the CPUs local to `device`.
+
+    Pinned host buffers allocated inside land on the GPU's NUMA node (Linux
+    places pages where they are first touched), so their copies do not cross
+    the inter-socket link.  With several GPUs per host each rank's buffers then
+    sit next to its own GPU.  Yields the CPUs used ([] = unchanged: NVML had no
+    answer, or none of its CPUs is allowed to this process); the previous
+    affinity is restored on exit.
+    """
+    before = os.sched_getaffinity(0)
+    cpus = [c for c in device_local_cpus(device) if c in before]
+    if cpus:
+        os.sched_setaffinity(0, cpus)
+    try:
+        yield cpus
+    finally:
+        if cpus:
+            os.sched_setaffinity(0, before)
 
 
 class HostPipeline:

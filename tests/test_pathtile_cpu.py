@@ -215,3 +215,26 @@ def test_selector_baselines_against_hand_computed_regret():
     # random fixed: mean over the three candidates per path = 7/3, times three paths
     assert r["random_fixed_regret_pct"] == pytest.approx(100.0 * (7.0 / 3.0 - 1.0))
     assert summary["global"]["shapes"] == 1 and summary["global"]["within_2pct"] == 1
+
+
+def test_host_cpu_mask_and_numa_binding_restore(monkeypatch):
+    """near_device binds the calling thread to the GPU-local CPUs NVML reports
+    (here a fake answer) and restores the previous affinity afterwards; with no
+    answer it leaves the affinity alone."""
+    import os
+
+    from pathtile_b200 import host
+
+    assert host.cpus_from_mask([0b1011, 1]) == [0, 1, 3, 64]
+    assert host.cpus_from_mask([0]) == []
+    before = os.sched_getaffinity(0)
+    subset = sorted(before)[:1]
+    monkeypatch.setattr(host, "device_local_cpus", lambda dev: subset + [10_000])
+    with host.near_device(0) as cpus:
+        assert cpus == subset
+        assert os.sched_getaffinity(0) == set(subset)
+    assert os.sched_getaffinity(0) == before
+    monkeypatch.setattr(host, "device_local_cpus", lambda dev: [])
+    with host.near_device(0) as cpus:
+        assert cpus == [] and os.sched_getaffinity(0) == before
+    assert os.sched_getaffinity(0) == before
