@@ -9,18 +9,26 @@ batch-sharded x[131072,128,48] configuration; for N>1 each step also
 all-reduces dK[128,48] over NCCL).  Inputs are resident in HBM and each of
 x, dy, y, dX is 402 MB, larger than the 126 MB L2, so no L2 flush is needed.
 
-Printed (rank 0, one JSON line): ``value`` = whole-job algorithmic GB/s of
-FWD+dX+dK (bytes per phase (2*B*H*L + H*K)*4, the reference's formula) over
-the device-timed step (CUDA events, max over ranks); ``aggregate_ms`` = sum of
-the three phases' separately timed mean latencies (the reference's headline
-protocol); ``roofline`` for the dominant kernel; ``cpu_baseline`` = the
-reference's PyTorch CPU path timed on this host (1-GPU runs only); ``e2e`` = the same pass
+Printed (rank 0, one JSON line): ``value`` = whole-job effective GB/s of
+FWD+dX+dK -- the reference's byte formula, (2*B*H*L + H*K)*4 per phase, three
+phases -- over the device-timed step (CUDA events, max over ranks; the step's
+backward is one fused kernel, which moves fewer bytes than the formula
+credits, see ``step_moved_bytes``); ``aggregate_ms`` = the sum of the three
+phases timed separately under the reference's protocol (each phase: 3 trials
+of 50 untimed + 100 timed launches, median of the trial means; outputs and the
+dK workspace allocated before timing); ``roofline`` for the dominant kernel of
+the step; ``cpu_baseline`` = the reference's PyTorch CPU path timed on this
+host under the reference's protocol (1-GPU runs only); ``e2e`` = the same pass
 through the host-buffer API (pinned host tensors, copies inside the timed
-region); ``clocks`` sampled by NVML during the timed region.
+region); ``clocks`` sampled by NVML during the timed region (and per phase).
+For N > 1, ``compute_ms`` and ``allreduce_ms`` split the step (max over ranks).
 
 ``--impl reference`` times the reference's own CPU implementation (its PyTorch
 path F.pad + grouped conv1d with autograd, restated in oracle/) on this host's
-cores, on a bounded sample of the same workload, and prints the same metric.
+cores under the reference's protocol (FWD, dX and dK timed separately, the
+autograd graph built outside the timed region, summed), on a bounded sample of
+the same workload, and prints the same metric; where the reference's own CUDA
+kernels were built for sm_100a (oracle/_ref) it adds their times on this GPU.
 """
 from __future__ import annotations
 
@@ -132,52 +140,114 @@ def time_loop(fn, iters: int, stream) -> float:
     return s.elapsed_time(e) / iters
 
 
-def cpu_baseline(seconds_per_phase: float = 3.0, B_sample: int = 512) -> dict:
-    """The reference's PyTorch CPU path (restated in oracle/reference_torch.py) on
-    this host's cores: FWD, dX, dK timed separately (graph built outside the
-    timed region, as benchmark/benchmark_pytorch.py:97-144 does)."""
+# The reference's GPU timing protocol (artifact/REPRODUCIBILITY.md:79-121,
+# kernels/warp_tiled_ampere.py:1040-1084): 3 trials x (50 warm-up + 100 timed
+# launches) per phase, phases timed separately.
+PHASE_TRIALS, PHASE_WARMUP, PHASE_RUNS = 3, 50, 100
+
+
+def time_phase(fn, stream, device_index: int, pre=None, trials: int = PHASE_TRIALS, warmup: int = PHASE_WARMUP,
+               runs: int = PHASE_RUNS) -> dict:
+    """One phase under the reference protocol: per trial, `warmup` untimed launches
+    then `runs` timed ones (CUDA events on the launching stream); the phase time
+    is the median of the trial means.  With `pre` (e.g. a zero-fill the reference
+    keeps outside the timed region) every launch is bracketed by its own events,
+    with `pre` before the start event."""
+    trial_ms = []
+    with ClockSampler(device_index) as clk:
+        for _ in range(trials):
+            for _ in range(warmup):
+                if pre is not None:
+                    pre()
+                fn()
+            if pre is None:
+                trial_ms.append(time_loop(fn, runs, stream))
+                continue
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
+            torch.cuda.synchronize()
+            for a, b in ev:
+                pre()
+                a.record(stream)
+                fn()
+                b.record(stream)
+            torch.cuda.synchronize()
+            trial_ms.append(statistics.mean(a.elapsed_time(b) for a, b in ev))
+    return {"ms": statistics.median(trial_ms), "trials_ms": trial_ms, "clocks": clk.summary()}
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_protocol(B: int, warmup: int = 5, runs: int = 30, seed: int = 42) -> dict:
+    """The reference's PyTorch path on this host's CPU cores under the reference's
+    own protocol (benchmark/benchmark_pytorch.py:22-24, 80-144): FWD timed around
+    pad + conv; dX and dK timed around torch.autograd.grad only, each run's
+    forward graph built outside the timed region; 5 warm-up + 30 timed runs per
+    phase, perf_counter.  The path is restated in oracle/reference_torch.py (the
+    reference module imports pycuda, which this host lacks)."""
     from oracle import reference_torch as ref
 
     torch.set_num_threads(os.cpu_count() or 1)
-    x, k, dy = ref.make_inputs(B_sample, H, L, K, seed=42)
+    x, k, dy = ref.make_inputs(B, H, L, K, seed=seed)
     xr = x.clone().requires_grad_(True)
     kr = k.clone().requires_grad_(True)
 
-    def run_fwd():
+    def fwd():
         with torch.no_grad():
+            t0 = time.perf_counter()
             ref.depthwise_same(x, k)
+            return time.perf_counter() - t0
 
-    def run_dx():
+    def dx():
         y = ref.depthwise_same(xr, k)
+        t0 = time.perf_counter()
         torch.autograd.grad(y, xr, dy)
+        return time.perf_counter() - t0
 
-    def run_dk():
+    def dk():
         y = ref.depthwise_same(x, kr)
+        t0 = time.perf_counter()
         torch.autograd.grad(y, kr, dy)
+        return time.perf_counter() - t0
 
-    means = {}
-    for name, fn in (("fwd", run_fwd), ("bwd_input", run_dx), ("bwd_weight", run_dk)):
-        for _ in range(3):
+    phases = {}
+    for name, fn in (("fwd", fwd), ("bwd_input", dx), ("bwd_weight", dk)):
+        for _ in range(warmup):
             fn()
-        n, t0 = 0, time.perf_counter()
-        while True:
-            fn()
-            n += 1
-            el = time.perf_counter() - t0
-            if el >= seconds_per_phase and n >= 5:
-                break
-        means[name] = 1e3 * el / n
-    agg = sum(means.values())
+        ts = [1e3 * fn() for _ in range(runs)]
+        phases[name] = {"median_ms": statistics.median(ts), "mean_ms": statistics.mean(ts)}
+    agg = sum(p["mean_ms"] for p in phases.values())
+    return {"B": B, "phase_ms": {n: p["mean_ms"] for n, p in phases.items()},
+            "phase_median_ms": {n: p["median_ms"] for n, p in phases.items()},
+            "aggregate_ms": agg, "GB/s": 3 * phase_bytes(B) / (agg / 1e3) / 1e9}
+
+
+def cpu_baseline(B_sample: int = 1024) -> dict:
+    """The reference's PyTorch CPU path on this host (reported baseline, not the target):
+    the bounded sample of the primary shape, plus BASELINE's CPU configuration (B=64)."""
+    main = cpu_protocol(B_sample)
+    small = cpu_protocol(64)
     return {
-        "value": 3 * phase_bytes(B_sample) / (agg / 1e3) / 1e9,
+        "value": main["GB/s"],
         "unit": "GB/s",
         "cores": torch.get_num_threads(),
         "kind": "port",
-        "aggregate_ms": agg,
-        "phase_ms": means,
-        "sample": (f"B={B_sample} of the primary shape (H=128,L=48,K=48); reference PyTorch CPU path "
-                   f"F.pad + conv1d(groups=H) with autograd for dX/dK, 3 warm-up + >= {seconds_per_phase:.0f} s "
-                   "per phase; restated in oracle/reference_torch.py (the reference module needs pycuda to import)"),
+        "cpu_model": cpu_model(),
+        "aggregate_ms": main["aggregate_ms"],
+        "phase_ms": main["phase_ms"],
+        "phase_median_ms": main["phase_median_ms"],
+        "config0_B64": {k_: small[k_] for k_ in ("phase_ms", "aggregate_ms", "GB/s")},
+        "sample": (f"B={B_sample} of the primary shape (H=128,L=48,K=48), and B=64 (the CPU config); reference "
+                   "PyTorch CPU path F.pad + conv1d(groups=H), FWD / dX / dK timed separately with the autograd "
+                   "graph built outside the timed region, 5 warm-up + 30 timed runs per phase (the reference's "
+                   "benchmark_pytorch.py protocol), mean per phase summed; restated in oracle/reference_torch.py"),
     }
 
 
@@ -220,13 +290,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     fused = args.backward == "fused"
 
-    def step():
+    def compute():
         ops.fwd(x, k, y)
         if fused:
             ops.dx_dk(dy, x, k, gk, gx=gx, mode="deterministic")
         else:
             ops.dx(dy, k, gx)
             ops.dk(dy, x, gk, mode="deterministic")
+
+    def step():
+        compute()
         if dist is not None:
             dist.all_reduce(gk)
 
@@ -235,26 +308,52 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
+    # For N > 1, events around each step's compute and its all-reduce split the
+    # step; they are recorded on the launching stream and add no device work.
+    marks = []
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
-        step_ms = time_loop(step, args.steps, stream)
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record(stream)
+        for _ in range(args.steps):
+            if dist is None:
+                step()
+                continue
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record(stream)
+            compute()
+            ev[1].record(stream)
+            dist.all_reduce(gk)
+            ev[2].record(stream)
+            marks.append(ev)
+        e_ev.record(stream)
+        e_ev.synchronize()
+        step_ms = s_ev.elapsed_time(e_ev) / args.steps
+    split = None
     if dist is not None:
-        t = torch.tensor([step_ms], device=dev, dtype=torch.float64)
+        comp = statistics.mean(a.elapsed_time(b) for a, b, _ in marks)
+        red = statistics.mean(b.elapsed_time(c) for _, b, c in marks)
+        t = torch.tensor([step_ms, comp, red], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_ms = float(t.item())
+        step_ms, comp, red = map(float, t.tolist())
+        split = {"compute_ms": comp, "allreduce_ms": red}
 
-    # Per-phase means, each phase timed separately (reference protocol).
-    iters = max(20, min(200, args.steps))
-    phase_ms = {
-        "fwd": time_loop(lambda: ops.fwd(x, k, y), iters, stream),
-        "bwd_input": time_loop(lambda: ops.dx(dy, k, gx), iters, stream),
-        "bwd_weight": time_loop(lambda: ops.dk(dy, x, gk, mode="deterministic"), iters, stream),
+    # Per-phase times under the reference protocol, each phase timed separately.
+    # Outputs exist already; the dK workspace is allocated by a call outside the
+    # timed trials (time_phase's warm-up launches come first in any case).
+    ops.dk(dy, x, gk, mode="deterministic")
+    torch.cuda.synchronize()
+    phases = {
+        "fwd": time_phase(lambda: ops.fwd(x, k, y), stream, local_rank),
+        "bwd_input": time_phase(lambda: ops.dx(dy, k, gx), stream, local_rank),
+        "bwd_weight": time_phase(lambda: ops.dk(dy, x, gk, mode="deterministic"), stream, local_rank),
     }
     if fused:
-        phase_ms["bwd_fused"] = time_loop(lambda: ops.dx_dk(dy, x, k, gk, gx=gx, mode="deterministic"), iters,
-                                          stream)
+        phases["bwd_fused"] = time_phase(lambda: ops.dx_dk(dy, x, k, gk, gx=gx, mode="deterministic"), stream,
+                                         local_rank)
+    phase_ms = {p: v["ms"] for p, v in phases.items()}
     if dist is not None:
         t = torch.tensor(list(phase_ms.values()), device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -316,6 +415,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     # fused backward reads dy and x, writes dx, reads k and writes dK.
     kernel_bytes = {p: pb for p in ("fwd", "bwd_input", "bwd_weight")}
     kernel_bytes["bwd_fused"] = (3 * B * H * L + 2 * H * K) * 4
+    step_moved = kernel_bytes["fwd"] + (kernel_bytes["bwd_fused"] if fused_on else 2 * pb)
     achieved = kernel_bytes[dominant] / (phase_ms[dominant] / 1e3) / 1e9
     sm_mhz = clocks.summary()["sm_mhz"] or 1965.0
     fma_peak = runtime.fp32_fma_peak_tflops(torch.cuda.get_device_properties(dev).multi_processor_count,
@@ -354,10 +454,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "engines": engines,
             "l2": "inputs larger than L2 (402,653,184 B per activation tensor vs 126 MB L2)",
         },
+        "value_kind": ("effective: the reference's byte formula (3 phases of (2*B*H*L + H*K)*4 B) over the "
+                       "measured step; the step itself moves step_moved_bytes"),
+        "step_moved_bytes": step_moved * world,
         "aggregate_ms": sum(phase_ms[p] for p in ("fwd", "bwd_input", "bwd_weight")),
+        "aggregate_protocol": (f"each phase separately: {PHASE_TRIALS} trials x ({PHASE_WARMUP} untimed + "
+                               f"{PHASE_RUNS} timed launches), median of the trial means (CUDA events)"),
         "phases": {p: {"ms": ms, "GB/s": kernel_bytes[p] / (ms / 1e3) / 1e9,
                        **({"frac_of_roofline": roof_ms / ms} if p != "bwd_fused" else
-                          {"frac_of_hbm": kernel_bytes[p] / (ms / 1e3) / 1e9 / hbm})}
+                          {"frac_of_hbm": kernel_bytes[p] / (ms / 1e3) / 1e9 / hbm}),
+                       "trials_ms": phases[p]["trials_ms"], "sm_mhz": phases[p]["clocks"]["sm_mhz"]}
                    for p, ms in phase_ms.items()},
         "aggregate_frac_of_roofline": 3 * roof_ms / sum(phase_ms[p] for p in ("fwd", "bwd_input", "bwd_weight")),
         "roofline": {
@@ -382,16 +488,64 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "host_cpus": len(host_cpus) if host_cpus else None,
         },
         "gpu_launches": args.steps * (1 + (ops.dx_dk_launches(B, H, L, K) if fused else 3)),
+        **({"step_split": split} if split else {}),
         "clocks": clocks.summary(),
         "device_error_word": err,
     }
     if not args.no_cpu_baseline and world == 1:  # the CPU baseline belongs to the 1-GPU line
-        result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        result["cpu_baseline"] = cpu_baseline(args.cpu_sample_b)
     return result
 
 
+def reference_gpu_kernels() -> dict | None:
+    """The reference's own warp-tiled CUDA kernels (its CUDA_TEMPLATE with the
+    default launch constants, compiled for sm_100a into oracle/_ref by
+    oracle/build_oracle.py) on this GPU at the primary shape, each phase under
+    the reference protocol with the atomic dK's zero-fill outside the timed
+    region -- the GPU-to-GPU comparison point.  None where not built or no GPU."""
+    import ctypes
+
+    lib_path = ROOT / "oracle" / "_ref" / "libref_warptile.so"
+    if not lib_path.exists() or not torch.cuda.is_available():
+        return None
+    lib = ctypes.CDLL(str(lib_path))
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(42)
+    x = torch.randn(B_PER_GPU, H, L, device=dev, generator=g)
+    k = torch.randn(H, K, device=dev, generator=g) / (K ** 0.5)
+    dy = torch.randn(B_PER_GPU, H, L, device=dev, generator=g)
+    y, gx, gk = torch.empty_like(x), torch.empty_like(x), torch.zeros_like(k)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    B = B_PER_GPU
+
+    def launch(fn, *a):
+        if fn(*a) != 0:
+            raise RuntimeError("reference kernel launch failed")
+
+    phases = {
+        "fwd": time_phase(lambda: launch(lib.ref_fwd, p(x), p(k), p(y), B, H, L, K, sp), stream, 0),
+        "bwd_input": time_phase(lambda: launch(lib.ref_dx, p(dy), p(k), p(gx), B, H, L, K, sp), stream, 0),
+        "bwd_weight": time_phase(lambda: launch(lib.ref_dk, p(dy), p(x), p(gk), B, H, L, K, sp), stream, 0,
+                                 pre=gk.zero_),
+    }
+    agg = sum(v["ms"] for v in phases.values())
+    return {
+        "kernels": "dwconv1d_warptile_fwd / _bwd_input / _bwd_weight (kernels/warp_tiled_ampere.py:372-619), "
+                   "WARPS_PER_BLOCK=16, BWDK_BTILE=64, BWDK_BLOCK=128, compiled for sm_100a",
+        "config": {"B": B, "H": H, "L": L, "K": K},
+        "phase_ms": {n: v["ms"] for n, v in phases.items()},
+        "aggregate_ms": agg,
+        "GB/s": 3 * phase_bytes(B) / (agg / 1e3) / 1e9,
+        "protocol": f"{PHASE_TRIALS} trials x ({PHASE_WARMUP} + {PHASE_RUNS}) launches per phase, CUDA events",
+    }
+
+
 def run_reference(args, rank: int) -> dict | None:
-    """The reference's CPU path on this host, same metric and unit."""
+    """The reference's CPU path on this host, same metric and unit: each step
+    times FWD, dX and dK separately under the reference's protocol (the autograd
+    graph built outside the timed region) on a bounded sample and sums them."""
     if rank != 0:
         return None
     from oracle import reference_torch as ref
@@ -399,37 +553,57 @@ def run_reference(args, rank: int) -> dict | None:
     torch.set_num_threads(os.cpu_count() or 1)
     Bs = args.ref_sample_b
     x, k, dy = ref.make_inputs(Bs, H, L, K, seed=42)
+    xr = x.clone().requires_grad_(True)
+    kr = k.clone().requires_grad_(True)
 
-    def step():
-        xr = x.clone().requires_grad_(True)
-        kr = k.clone().requires_grad_(True)
+    def step() -> dict[str, float]:
+        out = {}
         with torch.no_grad():
+            t0 = time.perf_counter()
             ref.depthwise_same(x, k)
-        y = ref.depthwise_same(xr, kr)
-        torch.autograd.grad(y, (xr, kr), dy)
+            out["fwd"] = time.perf_counter() - t0
+        yx = ref.depthwise_same(xr, k)
+        t0 = time.perf_counter()
+        torch.autograd.grad(yx, xr, dy)
+        out["bwd_input"] = time.perf_counter() - t0
+        yk = ref.depthwise_same(x, kr)
+        t0 = time.perf_counter()
+        torch.autograd.grad(yk, kr, dy)
+        out["bwd_weight"] = time.perf_counter() - t0
+        return out
 
     for _ in range(args.warmup):
         step()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        step()
-        times.append(time.perf_counter() - t0)
-    ms = 1e3 * statistics.mean(times)
+    runs = [step() for _ in range(args.steps)]
+    phase_ms = {n: 1e3 * statistics.mean(r[n] for r in runs) for n in ("fwd", "bwd_input", "bwd_weight")}
+    ms = sum(phase_ms.values())
     val = 3 * phase_bytes(Bs) / (ms / 1e3) / 1e9
-    sample = (f"B={Bs} of the primary shape (H=128,L=48,K=48) per step: FWD under no_grad, then one "
-              "forward + autograd for dX and dK; reference PyTorch CPU path restated in oracle/reference_torch.py")
-    return {
+    sample = (f"B={Bs} of the primary shape (H=128,L=48,K=48) per step; FWD, dX and dK timed separately with "
+              "the autograd graph built outside the timed region (the reference's benchmark_pytorch.py "
+              "protocol) and summed; reference PyTorch CPU path restated in oracle/reference_torch.py")
+    small = cpu_protocol(64)
+    res = {
         "metric": METRIC, "impl": "reference", "value": val, "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: x, dy ~ N(0,1), k ~ N(0,1)/sqrt(K), seeded",
         "config": {"workload": "primary: B=16384 per GPU, H=128, L=48, K=48 (bounded CPU sample per step)",
                    "B_sample": Bs, "H": H, "L": L, "K": K, "parallelism": "cpu"},
+        "aggregate_ms": ms,
+        "phase_ms": phase_ms,
         "cpu_baseline": {"value": val, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": sample},
+                         "cpu_model": cpu_model(), "phase_ms": phase_ms, "sample": sample,
+                         "config0_B64": {k_: small[k_] for k_ in ("phase_ms", "aggregate_ms", "GB/s")}},
         "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_ref_gpu:
+        try:
+            ref_gpu = reference_gpu_kernels()
+        except Exception as exc:  # the CPU line stands on its own
+            ref_gpu = {"error": repr(exc)}
+        if ref_gpu is not None:
+            res["reference_gpu_kernels"] = ref_gpu
+    return res
 
 
 def run_s4_train(args) -> dict:
@@ -494,9 +668,11 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--e2e-chunk", type=int, default=1024)
-    ap.add_argument("--cpu-seconds", type=float, default=3.0)
+    ap.add_argument("--cpu-sample-b", type=int, default=1024, help="batch of the bounded CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ref-sample-b", type=int, default=256)
+    ap.add_argument("--ref-sample-b", type=int, default=1024)
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="--impl reference: skip timing the reference's CUDA kernels on the GPU")
     ap.add_argument("--batch", type=int, default=B_PER_GPU,
                     help="batch per GPU (default: the primary workload; smaller only for profiling)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement (profiling)")

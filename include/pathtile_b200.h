@@ -58,6 +58,7 @@ extern "C" {
 #define PT_PATH_FWD 0
 #define PT_PATH_DX 1
 #define PT_PATH_DK 2
+#define PT_PATH_BWD_FUSED 3  /* pt_kernel_info only: the fused dX + dK kernel of pt_dx_dk */
 
 /* Engines (pt_set_engine, pt_config out[6]). */
 #define PT_ENGINE_FFMA 0    /* CUDA-core FP32 FMA kernels: every path and shape */
@@ -193,11 +194,50 @@ PT_API int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_s
 PT_API int pt_set_engine(int path, int engine);
 
 /*
+ * Per-call launch options, for callers that must not change the process-wide
+ * choice (two runtimes in one process, a tuner beside a training job).  One
+ * entry per path, indexed by PT_PATH_FWD / PT_PATH_DX / PT_PATH_DK:
+ * rows_per_tile 0 takes the frozen PathTile table for that path (the other
+ * three fields are then ignored), else the same ranges as pt_set_config;
+ * engine -1 takes the frozen engine, else PT_ENGINE_*.  The *_ex entry points
+ * below behave exactly like their plain counterparts, with `opts` in place of
+ * the process-wide overrides for the duration of the call (NULL: the
+ * process-wide state).  Invalid options give PT_ERR_ARGS (0 for the size
+ * queries).  The reference's counterpart is one runtime compiled per
+ * configuration (AmpereWarpRuntime(warps_per_block, bwdk_block),
+ * kernels/warp_tiled_ampere.py:636-691).
+ */
+typedef struct pt_launch_opts {
+  int rows_per_tile[3];
+  int stages[3];
+  int ctas_per_sm[3];
+  int threads_per_row[3];
+  int engine[3];
+} pt_launch_opts;
+
+PT_API int pt_fwd_ex(const float* x, const float* k, float* y, int B, int H, int L, int K,
+                     const pt_launch_opts* opts, void* stream);
+PT_API int pt_dx_ex(const float* dy, const float* k, float* dx, int B, int H, int L, int K,
+                    const pt_launch_opts* opts, void* stream);
+PT_API int pt_dk_ex(const float* dy, const float* x, float* dk, int B, int H, int L, int K, int mode,
+                    void* ws, size_t ws_bytes, const pt_launch_opts* opts, void* stream);
+PT_API int pt_dx_dk_ex(const float* dy, const float* x, const float* k, float* dx, float* dk, int B, int H,
+                       int L, int K, int mode, void* ws, size_t ws_bytes, const pt_launch_opts* opts,
+                       void* stream);
+PT_API size_t pt_dk_workspace_bytes_ex(int B, int H, int L, int K, const pt_launch_opts* opts);
+PT_API size_t pt_dx_dk_workspace_bytes_ex(int B, int H, int L, int K, const pt_launch_opts* opts);
+PT_API int pt_dx_dk_fused_ex(int B, int H, int L, int K, const pt_launch_opts* opts);
+PT_API int pt_config_ex(int path, int B, int H, int L, int K, int* out, int n, const pt_launch_opts* opts);
+PT_API int pt_kernel_info_ex(int path, int B, int H, int L, int K, int* out, int n,
+                             const pt_launch_opts* opts);
+
+/*
  * Resources of the kernel `path` would launch for this shape: out[0] registers
  * per thread, out[1] static shared bytes, out[2] local (spill) bytes per
  * thread, out[3] threads per CTA, out[4] dynamic shared bytes, out[5] resident
  * CTAs per SM (occupancy API), out[6] grid size, out[7] 1 if specialised.
- * `n` >= 8.  Counterpart of AmpereWarpRuntime.resource_report, which reads the
+ * `n` >= 8.  `path` PT_PATH_BWD_FUSED reports the fused backward kernel of
+ * pt_dx_dk (PT_ERR_UNSUPPORTED where pt_dx_dk_fused is 0).  Counterpart of AmpereWarpRuntime.resource_report, which reads the
  * compiled function's num_regs / shared_size_bytes / local_size_bytes
  * (kernels/warp_tiled_ampere.py:814-833).
  */
@@ -215,6 +255,18 @@ PT_API int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n)
  * silently on L > 48, kernels/warp_tiled_ampere.py:390).
  */
 PT_API int pt_device_error(unsigned int* out, int clear);
+
+/*
+ * Self-test of the device-side wait limit (test use): launches one warp that
+ * waits on an mbarrier nothing ever arrives on, through the same bounded-wait
+ * routine as every pipeline kernel, but limited to `limit_ns` (1 ns .. 1 s)
+ * instead of 2 s.  The wait runs out, bit 0 of the device error word is set
+ * (as when a consumer's tile never arrives) and the kernel returns; nothing
+ * is left in flight and the context stays usable.  `out` is a 16-byte
+ * aligned device buffer of two unsigned 64-bit words: the wait's duration in
+ * ns and 1 if it reported success (0 expected).  No reference counterpart.
+ */
+PT_API int pt_selftest_wait_timeout(unsigned long long limit_ns, void* out, void* stream);
 
 /* Human-readable text for a status code. */
 PT_API const char* pt_status_string(int status);

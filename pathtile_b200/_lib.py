@@ -30,12 +30,36 @@ PT_DK_DETERMINISTIC_ACCUMULATE = 2
 PT_PATH_FWD = 0
 PT_PATH_DX = 1
 PT_PATH_DK = 2
+PT_PATH_BWD_FUSED = 3  # pt_kernel_info only
 
 PT_ENGINE_FFMA = 0
 PT_ENGINE_TENSOR = 1
 
 PT_MAX_L = 48
 PT_MAX_K = 48
+
+
+class LaunchOpts(ctypes.Structure):
+    """``pt_launch_opts``: per-call launch options, one entry per path (FWD, DX, DK).
+
+    rows_per_tile 0 keeps the frozen PathTile table for that path; engine -1
+    keeps the frozen engine."""
+
+    _fields_ = [
+        ("rows_per_tile", ctypes.c_int * 3),
+        ("stages", ctypes.c_int * 3),
+        ("ctas_per_sm", ctypes.c_int * 3),
+        ("threads_per_row", ctypes.c_int * 3),
+        ("engine", ctypes.c_int * 3),
+    ]
+
+    @classmethod
+    def frozen(cls) -> "LaunchOpts":
+        o = cls()
+        for p in range(3):
+            o.engine[p] = -1
+        return o
+
 
 # Every symbol include/pathtile_b200.h declares, with (restype, argtypes).
 _c_int, _c_size, _vp, _fp = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p
@@ -60,6 +84,18 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_status_string": (ctypes.c_char_p, [_c_int]),
     "pt_last_cuda_error": (_c_int, []),
     "pt_version": (_c_int, []),
+    "pt_fwd_ex": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
+    "pt_dx_ex": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
+    "pt_dk_ex": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp, _vp]),
+    "pt_dx_dk_ex": (_c_int, [_fp, _fp, _fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp,
+                             _vp]),
+    "pt_dk_workspace_bytes_ex": (_c_size, [_c_int, _c_int, _c_int, _c_int, _vp]),
+    "pt_dx_dk_workspace_bytes_ex": (_c_size, [_c_int, _c_int, _c_int, _c_int, _vp]),
+    "pt_dx_dk_fused_ex": (_c_int, [_c_int, _c_int, _c_int, _c_int, _vp]),
+    "pt_config_ex": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int, _vp]),
+    "pt_kernel_info_ex": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int,
+                                   _vp]),
+    "pt_selftest_wait_timeout": (_c_int, [ctypes.c_ulonglong, _vp, _vp]),
 }
 
 _lock = threading.Lock()

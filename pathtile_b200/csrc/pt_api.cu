@@ -51,9 +51,29 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 // Rows are padded to a bank-conflict-free pitch by a TMA box wider than the
 // row; if the driver ever rejects such a box, rows fall back to pitch L.
 bool g_padded_box_ok = true;
-pt::LaunchCfg g_override[3];
-bool g_has_override[3] = {false, false, false};
-int g_engine_override[3] = {-1, -1, -1};  // -1: the frozen table decides
+// Launch options: a configuration and an engine per path, each either set or
+// left to the frozen table.  g_opts holds the process-wide overrides
+// (pt_set_config / pt_set_engine); the *_ex entry points make their caller's
+// options current on this host thread for the duration of the call, so two
+// callers with different options never see each other's choices.
+struct Opts {
+  pt::LaunchCfg cfg[3] = {};
+  bool has_cfg[3] = {false, false, false};
+  int engine[3] = {-1, -1, -1};  // -1: the frozen table decides
+};
+Opts g_opts;
+thread_local const Opts* t_opts = nullptr;
+
+const Opts& opts() { return t_opts ? *t_opts : g_opts; }
+
+// Makes `o` the current options of this host thread until the scope ends.
+struct OptsScope {
+  const Opts* saved;
+  explicit OptsScope(const Opts* o) : saved(t_opts) {
+    if (o) t_opts = o;
+  }
+  ~OptsScope() { t_opts = saved; }
+};
 
 int cuda_fail(cudaError_t e) {
   t_last_cuda_error = static_cast<int>(e);
@@ -142,7 +162,8 @@ int intensity_class(int L, int K) {
 }
 
 pt::LaunchCfg cfg_for(int path, int L, int K) {
-  return g_has_override[path] ? g_override[path] : pt::kFrozenCfg[path][intensity_class(L, K)];
+  const Opts& o = opts();
+  return o.has_cfg[path] ? o.cfg[path] : pt::kFrozenCfg[path][intensity_class(L, K)];
 }
 
 int gcd_int(int a, int b) {
@@ -203,9 +224,10 @@ int engine_for(int path, int B, int H, int L, int K, int sm_count) {
   const int groups = tensor_groups(H, L);
   int G = 0, period = 0;
   tensor_grid(groups, tensor_tiles(path, B, groups), sm_count > 0 ? sm_count : 148, G, period);
-  if (g_engine_override[path] >= 0) {
+  const int forced = opts().engine[path];
+  if (forced >= 0) {
     if (path == PT_PATH_DK && period == 0) return PT_ENGINE_FFMA;
-    return g_engine_override[path];
+    return forced;
   }
   // The frozen table compares the tensor engine with the specialised CUDA-core
   // kernels; a shape without one would run the generic kernels (runtime bounds,
@@ -535,7 +557,8 @@ int launch_tensor_dk(const Plan& p, const float* dy, const float* x, float* dk, 
 bool plan_fused(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   const void* func = pt::tc::bwd_func(L, K);
   if (!func || g_encode == nullptr) return false;
-  if (g_engine_override[PT_PATH_DX] >= 0 && g_engine_override[PT_PATH_DX] != PT_ENGINE_TENSOR) return false;
+  const int dx_engine = opts().engine[PT_PATH_DX];
+  if (dx_engine >= 0 && dx_engine != PT_ENGINE_TENSOR) return false;
   if (static_cast<long long>(pt::tc::bwd_smem()) > di.max_smem) return false;
   const long long tiles = tensor_tiles(PT_PATH_DX, B, H);
   const int gmax = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);
@@ -647,6 +670,47 @@ int launch_rows(int path, const float* in, const float* taps, float* out, int B,
   }
   if (ce != cudaSuccess) return cuda_fail(ce);
   return PT_OK;
+}
+
+bool cfg_valid(int rows_per_tile, int stages, int ctas_per_sm, int threads_per_row) {
+  if (rows_per_tile < 32 || rows_per_tile > 256 || rows_per_tile % 32 != 0) return false;
+  if (stages < 2 || stages > 4 || ctas_per_sm < 1 || ctas_per_sm > 4) return false;
+  return threads_per_row == 1 || threads_per_row == 2;
+}
+
+// Validated copy of a caller's per-call options (null: nothing to copy).
+bool to_opts(const pt_launch_opts* o, Opts& out) {
+  if (!o) return true;
+  for (int p = 0; p < 3; ++p) {
+    if (o->engine[p] != -1 && o->engine[p] != PT_ENGINE_FFMA && o->engine[p] != PT_ENGINE_TENSOR) return false;
+    out.engine[p] = o->engine[p];
+    if (o->rows_per_tile[p] == 0) continue;
+    if (!cfg_valid(o->rows_per_tile[p], o->stages[p], o->ctas_per_sm[p], o->threads_per_row[p])) return false;
+    out.cfg[p] = pt::LaunchCfg{o->rows_per_tile[p], o->stages[p], o->ctas_per_sm[p], o->threads_per_row[p]};
+    out.has_cfg[p] = true;
+  }
+  return true;
+}
+
+// Self-test of the wait limit: warp 0 waits on an mbarrier that nothing arrives
+// on, through the same bounded wait as every pipeline kernel but with a short
+// limit; the wait runs out, sets DEVERR_TIMEOUT_FULL and the kernel returns.
+// Lane 0 records how long the wait lasted and whether it reported success.
+__global__ void wait_selftest_kernel(unsigned long long limit_ns, unsigned long long* out, unsigned* err) {
+  __shared__ __align__(8) unsigned long long bar;
+  const uint32_t b = pt::smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    pt::mbar_init(b, 1);
+    pt::fence_mbar_init();
+  }
+  __syncthreads();
+  const unsigned long long t0 = pt::globaltimer_ns();
+  const bool ok = pt::mbar_wait_bounded_for(b, 0, err, pt::DEVERR_TIMEOUT_FULL, limit_ns);
+  const unsigned long long t1 = pt::globaltimer_ns();
+  if (threadIdx.x == 0) {
+    out[0] = t1 - t0;
+    out[1] = ok ? 1ull : 0ull;
+  }
 }
 
 size_t dk_ws_bytes(const Plan& p) {
@@ -861,14 +925,18 @@ int pt_config(int path, int B, int H, int L, int K, int* out, int n) {
 }
 
 int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n) {
-  if (path < 0 || path > 2 || !out || n < 8) return PT_ERR_ARGS;
+  if (path < 0 || path > PT_PATH_BWD_FUSED || !out || n < 8) return PT_ERR_ARGS;
   if (B < 1 || H < 1 || L < 1 || K < 1) return PT_ERR_ARGS;
   if (L > PT_MAX_L || K > PT_MAX_K) return PT_ERR_UNSUPPORTED;
   DeviceInfo* di = nullptr;
   int rc = current_device(di);
   if (rc != PT_OK) return rc;
   Plan p;
-  if ((rc = plan(path, B, H, L, K, *di, p)) != PT_OK) return rc;
+  if (path == PT_PATH_BWD_FUSED) {
+    if (!plan_fused(B, H, L, K, *di, p)) return PT_ERR_UNSUPPORTED;
+  } else if ((rc = plan(path, B, H, L, K, *di, p)) != PT_OK) {
+    return rc;
+  }
   const void* func = p.func;
   int threads = p.threads;
   size_t dyn = p.smem;
@@ -909,22 +977,100 @@ int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n) {
 int pt_set_config(int path, int rows_per_tile, int stages, int ctas_per_sm, int threads_per_row) {
   if (path < 0 || path > 2) return PT_ERR_ARGS;
   if (rows_per_tile == 0) {
-    g_has_override[path] = false;
+    g_opts.has_cfg[path] = false;
     return PT_OK;
   }
-  if (rows_per_tile < 32 || rows_per_tile > 256 || rows_per_tile % 32 != 0) return PT_ERR_ARGS;
-  if (stages < 2 || stages > 4 || ctas_per_sm < 1 || ctas_per_sm > 4) return PT_ERR_ARGS;
-  if (threads_per_row != 1 && threads_per_row != 2) return PT_ERR_ARGS;
-  g_override[path] = pt::LaunchCfg{rows_per_tile, stages, ctas_per_sm, threads_per_row};
-  g_has_override[path] = true;
+  if (!cfg_valid(rows_per_tile, stages, ctas_per_sm, threads_per_row)) return PT_ERR_ARGS;
+  g_opts.cfg[path] = pt::LaunchCfg{rows_per_tile, stages, ctas_per_sm, threads_per_row};
+  g_opts.has_cfg[path] = true;
   return PT_OK;
 }
 
 int pt_set_engine(int path, int engine) {
   if (path < 0 || path > 2) return PT_ERR_ARGS;
   if (engine != -1 && engine != PT_ENGINE_FFMA && engine != PT_ENGINE_TENSOR) return PT_ERR_ARGS;
-  g_engine_override[path] = engine;
+  g_opts.engine[path] = engine;
   return PT_OK;
+}
+
+// ---------------- per-call launch options ----------------
+int pt_fwd_ex(const float* x, const float* k, float* y, int B, int H, int L, int K, const pt_launch_opts* o,
+              void* stream) {
+  Opts op;
+  if (!to_opts(o, op)) return PT_ERR_ARGS;
+  OptsScope scope(o ? &op : nullptr);
+  return pt_fwd(x, k, y, B, H, L, K, stream);
+}
+
+int pt_dx_ex(const float* dy, const float* k, float* dx, int B, int H, int L, int K, const pt_launch_opts* o,
+             void* stream) {
+  Opts op;
+  if (!to_opts(o, op)) return PT_ERR_ARGS;
+  OptsScope scope(o ? &op : nullptr);
+  return pt_dx(dy, k, dx, B, H, L, K, stream);
+}
+
+int pt_dk_ex(const float* dy, const float* x, float* dk, int B, int H, int L, int K, int mode, void* ws,
+             size_t ws_bytes, const pt_launch_opts* o, void* stream) {
+  Opts op;
+  if (!to_opts(o, op)) return PT_ERR_ARGS;
+  OptsScope scope(o ? &op : nullptr);
+  return pt_dk(dy, x, dk, B, H, L, K, mode, ws, ws_bytes, stream);
+}
+
+int pt_dx_dk_ex(const float* dy, const float* x, const float* k, float* dx, float* dk, int B, int H, int L,
+                int K, int mode, void* ws, size_t ws_bytes, const pt_launch_opts* o, void* stream) {
+  Opts op;
+  if (!to_opts(o, op)) return PT_ERR_ARGS;
+  OptsScope scope(o ? &op : nullptr);
+  return pt_dx_dk(dy, x, k, dx, dk, B, H, L, K, mode, ws, ws_bytes, stream);
+}
+
+size_t pt_dk_workspace_bytes_ex(int B, int H, int L, int K, const pt_launch_opts* o) {
+  Opts op;
+  if (!to_opts(o, op)) return 0;
+  OptsScope scope(o ? &op : nullptr);
+  return pt_dk_workspace_bytes(B, H, L, K);
+}
+
+size_t pt_dx_dk_workspace_bytes_ex(int B, int H, int L, int K, const pt_launch_opts* o) {
+  Opts op;
+  if (!to_opts(o, op)) return 0;
+  OptsScope scope(o ? &op : nullptr);
+  return pt_dx_dk_workspace_bytes(B, H, L, K);
+}
+
+int pt_dx_dk_fused_ex(int B, int H, int L, int K, const pt_launch_opts* o) {
+  Opts op;
+  if (!to_opts(o, op)) return 0;
+  OptsScope scope(o ? &op : nullptr);
+  return pt_dx_dk_fused(B, H, L, K);
+}
+
+int pt_config_ex(int path, int B, int H, int L, int K, int* out, int n, const pt_launch_opts* o) {
+  Opts op;
+  if (!to_opts(o, op)) return PT_ERR_ARGS;
+  OptsScope scope(o ? &op : nullptr);
+  return pt_config(path, B, H, L, K, out, n);
+}
+
+int pt_kernel_info_ex(int path, int B, int H, int L, int K, int* out, int n, const pt_launch_opts* o) {
+  Opts op;
+  if (!to_opts(o, op)) return PT_ERR_ARGS;
+  OptsScope scope(o ? &op : nullptr);
+  return pt_kernel_info(path, B, H, L, K, out, n);
+}
+
+int pt_selftest_wait_timeout(unsigned long long limit_ns, void* out, void* stream) {
+  if (!out || limit_ns == 0 || limit_ns > 1000000000ull) return PT_ERR_ARGS;
+  if (!aligned16(out)) return PT_ERR_ALIGN;
+  DeviceInfo* di = nullptr;
+  int rc = current_device(di);
+  if (rc != PT_OK) return rc;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      limit_ns, static_cast<unsigned long long*>(out), di->err);
+  const cudaError_t ce = cudaGetLastError();
+  return ce == cudaSuccess ? PT_OK : cuda_fail(ce);
 }
 
 int pt_device_error(unsigned int* out, int clear) {

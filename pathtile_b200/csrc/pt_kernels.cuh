@@ -93,18 +93,25 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   return t;
 }
 
-// Bounded wait for phase `parity` of `bar`; false (and an error bit) on expiry.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned* err,
-                                                  unsigned errbit) {
+// Wait for phase `parity` of `bar` for at most `limit_ns`; false (and `errbit`
+// set in the error word) on expiry.
+__device__ __forceinline__ bool mbar_wait_bounded_for(uint32_t bar, uint32_t parity, unsigned* err,
+                                                      unsigned errbit, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (static_cast<long long>(globaltimer_ns() - t0) > static_cast<long long>(WAIT_LIMIT_NS)) {
+    if (static_cast<long long>(globaltimer_ns() - t0) > static_cast<long long>(limit_ns)) {
       atomicOr(err, errbit);
       return false;
     }
   }
+}
+
+// The wait every kernel uses: bounded by WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned* err,
+                                                  unsigned errbit) {
+  return mbar_wait_bounded_for(bar, parity, err, errbit, WAIT_LIMIT_NS);
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {

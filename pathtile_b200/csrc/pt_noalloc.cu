@@ -17,7 +17,11 @@
 // capture.  All calls share the one array: calls whose executions overlap on
 // the GPU (different streams, or different host threads on one device) race on
 // it and must be serialised by the caller.  Nothing in the array needs to start
-// at zero: pass 1 writes every partial that pass 2 reads.
+// at zero: pass 1 writes every partial that pass 2 reads, and the tensor-core
+// dK marks each CTA's partial slots unused before it waits on anything, so a
+// CTA that gives up after a timed-out wait never lets pass 2 read what an
+// earlier call left.  Whenever pt_device_error reports a non-zero word, the
+// dK of the calls since it was last cleared is undefined.
 #include <cuda_runtime.h>
 
 #include <cstdint>

@@ -185,6 +185,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int h = g % H;  // the CTA's channel (G % H == 0)
   const int n_it = (g < n_tiles) ? (n_tiles - 1 - g) / G + 1 : 0;
 
+  // Partials mode: mark this CTA's slots unused before any bounded wait, so a
+  // CTA that gives up after a timed-out wait adds nothing to the reduce (and no
+  // slot id left in the workspace by an earlier launch is read).
+  if (!direct && threadIdx.x == 0) {
+    group_of[2 * g] = -1;
+    group_of[2 * g + 1] = -1;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < BWD_STAGES; ++s) {
       mbar_init(full(s), 1);

@@ -137,6 +137,11 @@ __global__ void __launch_bounds__(DK_THREADS, 1)
   const int n_it = (g < n_tiles) ? (n_tiles - 1 - g) / G + 1 : 0;
   const int Wp = Hc * L;  // packed super-row width (PACKED only)
 
+  // Mark this CTA's partial slots unused before any bounded wait: a CTA that
+  // gives up after a timed-out wait then contributes nothing to the reduce,
+  // never a slot id left behind by an earlier launch in the same workspace.
+  if (!atomic && threadIdx.x == 0)
+    for (int slot = 0; slot < DK_MAX_GROUPS; ++slot) group_of[g * DK_MAX_GROUPS + slot] = -1;
   if (threadIdx.x == 0) {
     for (int s = 0; s < DK_STAGES; ++s) {
       mbar_init(full(s), 1);

@@ -10,6 +10,7 @@ No computation happens on the host and there is no fallback path.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import threading
 
@@ -76,7 +77,12 @@ def _stream(device: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
-def _launch_rows(path: int, inp: torch.Tensor, k: torch.Tensor, out: torch.Tensor, what: str) -> None:
+def _opts_ptr(opts: "_lib.LaunchOpts | None") -> ctypes.c_void_p | None:
+    return None if opts is None else ctypes.cast(ctypes.pointer(opts), ctypes.c_void_p)
+
+
+def _launch_rows(path: int, inp: torch.Tensor, k: torch.Tensor, out: torch.Tensor, what: str,
+                 opts: "_lib.LaunchOpts | None" = None) -> None:
     B, H, L, K = check_shapes(inp, k)
     _ensure_cuda_f32(out, "out")
     if tuple(out.shape) != (B, H, L):
@@ -88,61 +94,91 @@ def _launch_rows(path: int, inp: torch.Tensor, k: torch.Tensor, out: torch.Tenso
     if B == 0:
         return
     lib = _lib.load()
-    fn = lib.pt_fwd if path == PT_PATH_FWD else lib.pt_dx
     with torch.cuda.device(inp.device):
-        st = fn(_ptr(inp), _ptr(k), _ptr(out), B, H, L, K, _stream(inp.device))
+        if opts is None:
+            fn = lib.pt_fwd if path == PT_PATH_FWD else lib.pt_dx
+            st = fn(_ptr(inp), _ptr(k), _ptr(out), B, H, L, K, _stream(inp.device))
+        else:
+            fn = lib.pt_fwd_ex if path == PT_PATH_FWD else lib.pt_dx_ex
+            st = fn(_ptr(inp), _ptr(k), _ptr(out), B, H, L, K, _opts_ptr(opts), _stream(inp.device))
     _lib.check(st, what)
 
 
-def fwd(x: torch.Tensor, k: torch.Tensor, y: torch.Tensor | None = None) -> torch.Tensor:
-    """y[b,h,t] = sum_j x[b,h,t+j-K//2] k[h,j] (same length L)."""
+def fwd(x: torch.Tensor, k: torch.Tensor, y: torch.Tensor | None = None,
+        opts: "_lib.LaunchOpts | None" = None) -> torch.Tensor:
+    """y[b,h,t] = sum_j x[b,h,t+j-K//2] k[h,j] (same length L).  ``opts``: per-call
+    launch options (None: the process-wide choice, by default the frozen table)."""
     if y is None:
         check_shapes(x, k)
         y = torch.empty_like(x, memory_format=torch.contiguous_format)
-    _launch_rows(PT_PATH_FWD, x, k, y, "pt_fwd")
+    _launch_rows(PT_PATH_FWD, x, k, y, "pt_fwd", opts)
     return y
 
 
-def dx(dy: torch.Tensor, k: torch.Tensor, gx: torch.Tensor | None = None) -> torch.Tensor:
+def dx(dy: torch.Tensor, k: torch.Tensor, gx: torch.Tensor | None = None,
+       opts: "_lib.LaunchOpts | None" = None) -> torch.Tensor:
     """gx[b,h,t] = sum_j dy[b,h,t-j+K//2] k[h,j]."""
     if gx is None:
         check_shapes(dy, k)
         gx = torch.empty_like(dy, memory_format=torch.contiguous_format)
-    _launch_rows(PT_PATH_DX, dy, k, gx, "pt_dx")
+    _launch_rows(PT_PATH_DX, dy, k, gx, "pt_dx", opts)
     return gx
 
 
 class _WorkspaceCache:
-    """One reusable deterministic-dK workspace per device (the reference caches
-    its [H,K,num_btiles] partials the same way,
-    kernels/warp_tiled_noatomic_optimized.py:1448-1471).  The buffer is
-    recorded on the launch stream so the caching allocator never hands it out
-    while a launch still reads it."""
+    """One reusable deterministic-dK workspace per (device, stream) (the reference
+    caches its [H,K,num_btiles] partials per runtime,
+    kernels/warp_tiled_noatomic_optimized.py:1448-1471).
+
+    Launches on one stream run in order, so they can share a buffer; launches on
+    two streams of one device may run at the same time, so each stream gets its
+    own buffer (a shared one would let one launch reduce the other's partials).
+    Allocation happens on the launch stream (the caching allocator ties the block
+    to it), so the allocator never hands the memory to other work while a
+    launch still reads it."""
 
     def __init__(self) -> None:
         self._lock = threading.Lock()
-        self._bufs: dict[int, torch.Tensor] = {}
+        self._bufs: dict[tuple[int, int], torch.Tensor] = {}
 
     def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
         idx = device.index if device.index is not None else torch.cuda.current_device()
+        stream = torch.cuda.current_stream(idx)
+        key = (idx, int(stream.cuda_stream))
         with self._lock:
-            buf = self._bufs.get(idx)
+            buf = self._bufs.get(key)
             if buf is None or buf.numel() < nbytes:
                 n = max(nbytes, 1 << 20)
-                buf = torch.empty(n, dtype=torch.uint8, device=torch.device("cuda", idx))
-                self._bufs[idx] = buf
+                with torch.cuda.stream(stream):
+                    buf = torch.empty(n, dtype=torch.uint8, device=torch.device("cuda", idx))
+                self._bufs[key] = buf
             return buf
+
+    def clear(self) -> None:
+        """Release every cached workspace (after the streams that used them are done)."""
+        with self._lock:
+            self._bufs.clear()
 
 
 WORKSPACES = _WorkspaceCache()
 
 
-def dk_workspace_bytes(B: int, H: int, L: int, K: int, device: torch.device | None = None) -> int:
+def dk_workspace_bytes(B: int, H: int, L: int, K: int, device: torch.device | None = None,
+                       opts: "_lib.LaunchOpts | None" = None) -> int:
     lib = _lib.load()
-    if device is None:
-        return int(lib.pt_dk_workspace_bytes(B, H, L, K))
-    with torch.cuda.device(device):
-        return int(lib.pt_dk_workspace_bytes(B, H, L, K))
+    with torch.cuda.device(device) if device is not None else _nullctx():
+        return int(lib.pt_dk_workspace_bytes_ex(B, H, L, K, _opts_ptr(opts)))
+
+
+def dx_dk_workspace_bytes(B: int, H: int, L: int, K: int, device: torch.device | None = None,
+                          opts: "_lib.LaunchOpts | None" = None) -> int:
+    lib = _lib.load()
+    with torch.cuda.device(device) if device is not None else _nullctx():
+        return int(lib.pt_dx_dk_workspace_bytes_ex(B, H, L, K, _opts_ptr(opts)))
+
+
+def _nullctx() -> contextlib.AbstractContextManager:
+    return contextlib.nullcontext()
 
 
 def dk(
@@ -152,6 +188,7 @@ def dk(
     mode: str = "deterministic",
     accumulate: bool = False,
     workspace: torch.Tensor | None = None,
+    opts: "_lib.LaunchOpts | None" = None,
 ) -> torch.Tensor:
     """Filter gradient dk[h,j] = sum_{b,t} dy[b,h,t] x[b,h,t+j-K//2] into gk[H,K].
 
@@ -159,6 +196,10 @@ def dk(
     plain gradient; the reference's contract, kernels/warp_tiled_ampere.py:890-893).
     mode "deterministic": two passes through a workspace; gk = dK, or gk += dK
     with accumulate=True; bit-reproducible for a fixed launch configuration.
+    Without ``workspace`` the cached buffer of the current stream is used:
+    calls on one stream run in order, calls on different streams get
+    different buffers.  A caller-provided ``workspace`` must not be in use by a
+    launch on another stream at the same time.
     """
     _ensure_cuda_f32(dy, "gy")
     _ensure_cuda_f32(x, "x")
@@ -189,7 +230,7 @@ def dk(
     with torch.cuda.device(dev):
         ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
         if code != PT_DK_ATOMIC and B > 0:
-            ws_bytes = int(lib.pt_dk_workspace_bytes(B, H, L, K))
+            ws_bytes = int(lib.pt_dk_workspace_bytes_ex(B, H, L, K, _opts_ptr(opts)))
             if ws_bytes == 0:
                 raise _lib.PathTileError(_lib.PT_ERR_WORKSPACE, "pt_dk_workspace_bytes")
             ws = workspace if workspace is not None else WORKSPACES.get(dev, ws_bytes)
@@ -198,7 +239,8 @@ def dk(
             ws.record_stream(torch.cuda.current_stream(dev))
             ws_ptr = _ptr(ws)
             ws_bytes = ws.numel() * ws.element_size()
-        st = lib.pt_dk(_ptr(dy), _ptr(x), _ptr(gk), B, H, L, K, code, ws_ptr, ws_bytes, _stream(dev))
+        st = lib.pt_dk_ex(_ptr(dy), _ptr(x), _ptr(gk), B, H, L, K, code, ws_ptr, ws_bytes, _opts_ptr(opts),
+                          _stream(dev))
     _lib.check(st, "pt_dk")
     return gk
 
@@ -212,9 +254,10 @@ def dx_dk(
     mode: str = "deterministic",
     accumulate: bool = False,
     workspace: torch.Tensor | None = None,
+    opts: "_lib.LaunchOpts | None" = None,
 ) -> torch.Tensor:
     """Both backward products in one call: returns gx = dX(dy, k) and writes the
-    filter gradient into gk with dk()'s modes.  For 32 < L <= 48 (L % 4 == 0)
+    filter gradient into gk with dk()'s modes (and its workspace rules).  For 32 < L <= 48 (L % 4 == 0)
     and any K on grids that give each CTA one channel this is one fused kernel
     (dy and x read once); other shapes run dx() then dk().  The reference's
     backward launches the two separately (kernels/warp_tiled_ampere.py:882-898).
@@ -246,7 +289,7 @@ def dx_dk(
     dev = x.device
     with torch.cuda.device(dev):
         ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
-        need = int(lib.pt_dx_dk_workspace_bytes(B, H, L, K)) if B > 0 else 0
+        need = int(lib.pt_dx_dk_workspace_bytes_ex(B, H, L, K, _opts_ptr(opts))) if B > 0 else 0
         if need > 0:
             ws = workspace if workspace is not None else WORKSPACES.get(dev, need)
             if ws.device != dev or ws.numel() * ws.element_size() < need:
@@ -254,26 +297,26 @@ def dx_dk(
             ws.record_stream(torch.cuda.current_stream(dev))
             ws_ptr = _ptr(ws)
             ws_bytes = ws.numel() * ws.element_size()
-        st = lib.pt_dx_dk(_ptr(dy), _ptr(x), _ptr(k), _ptr(gx), _ptr(gk), B, H, L, K, code, ws_ptr, ws_bytes,
-                          _stream(dev))
+        st = lib.pt_dx_dk_ex(_ptr(dy), _ptr(x), _ptr(k), _ptr(gx), _ptr(gk), B, H, L, K, code, ws_ptr, ws_bytes,
+                             _opts_ptr(opts), _stream(dev))
     _lib.check(st, "pt_dx_dk")
     return gx
 
 
-def fused_backward(B: int, H: int, L: int, K: int) -> bool:
+def fused_backward(B: int, H: int, L: int, K: int, opts: "_lib.LaunchOpts | None" = None) -> bool:
     """True when dx_dk() runs the single fused kernel at this shape on the current device."""
-    return bool(_lib.load().pt_dx_dk_fused(B, H, L, K))
+    return bool(_lib.load().pt_dx_dk_fused_ex(B, H, L, K, _opts_ptr(opts)))
 
 
-def dx_dk_launches(B: int, H: int, L: int, K: int) -> int:
+def dx_dk_launches(B: int, H: int, L: int, K: int, opts: "_lib.LaunchOpts | None" = None) -> int:
     """Kernel launches of one deterministic dx_dk() at this shape: the fused kernel
     (plus the partial reduce when a channel spans several CTAs), or dX + the
     two-pass dK."""
     if B <= 0:
         return 0
     lib = _lib.load()
-    if lib.pt_dx_dk_fused(B, H, L, K):
-        return 1 if int(lib.pt_dx_dk_workspace_bytes(B, H, L, K)) == 0 else 2
+    if lib.pt_dx_dk_fused_ex(B, H, L, K, _opts_ptr(opts)):
+        return 1 if int(lib.pt_dx_dk_workspace_bytes_ex(B, H, L, K, _opts_ptr(opts))) == 0 else 2
     return 3
 
 
@@ -349,26 +392,31 @@ def dk_cl(dy: torch.Tensor, x: torch.Tensor, gk: torch.Tensor, accumulate: bool 
     return gk
 
 
-def config(path: str, B: int, H: int, L: int, K: int) -> dict[str, int]:
-    """Frozen launch choice of one path at one shape (C ABI pt_config)."""
+def config(path: str, B: int, H: int, L: int, K: int, opts: "_lib.LaunchOpts | None" = None) -> dict[str, int]:
+    """Launch choice of one path at one shape (C ABI pt_config): the frozen table,
+    or ``opts`` / the process-wide overrides where they are set."""
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
     out = (ctypes.c_int * 7)()
-    _lib.check(_lib.load().pt_config(code, B, H, L, K, out, 7), "pt_config")
+    _lib.check(_lib.load().pt_config_ex(code, B, H, L, K, out, 7, _opts_ptr(opts)), "pt_config")
     return {"rows_per_tile": out[0], "stages": out[1], "ctas_per_sm": out[2], "specialised": out[3],
             "intensity_class": ("light", "medium", "heavy")[out[4]], "threads_per_row": out[5],
             "engine": ENGINES[out[6]]}
 
 
-def kernel_info(path: str, B: int, H: int, L: int, K: int, device: torch.device | int | None = None) -> dict[str, int]:
-    """Registers, shared memory, occupancy and grid of the kernel a path launches (C ABI pt_kernel_info)."""
-    code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
+KERNEL_PATHS = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK,
+                "bwd_fused": _lib.PT_PATH_BWD_FUSED}
+
+
+def kernel_info(path: str, B: int, H: int, L: int, K: int, device: torch.device | int | None = None,
+                opts: "_lib.LaunchOpts | None" = None) -> dict[str, int]:
+    """Registers, shared memory, occupancy and grid of the kernel a path launches (C ABI
+    pt_kernel_info); path "bwd_fused" is the fused dX + dK kernel (PathTileError with
+    status PT_ERR_UNSUPPORTED where dx_dk() does not fuse)."""
+    code = KERNEL_PATHS[path]
     out = (ctypes.c_int * 8)()
     lib = _lib.load()
-    if device is None:
-        st = lib.pt_kernel_info(code, B, H, L, K, out, 8)
-    else:
-        with torch.cuda.device(device):
-            st = lib.pt_kernel_info(code, B, H, L, K, out, 8)
+    with torch.cuda.device(device) if device is not None else _nullctx():
+        st = lib.pt_kernel_info_ex(code, B, H, L, K, out, 8, _opts_ptr(opts))
     _lib.check(st, "pt_kernel_info")
     keys = ("regs_per_thread", "static_smem_bytes", "local_memory_bytes", "threads_per_block",
             "dynamic_smem_bytes", "resident_blocks_per_sm", "grid", "specialised")

@@ -264,8 +264,11 @@ class B200WarpRuntime:
     ``warps_per_block`` (FWD/dX rows per tile / 32), ``bwdk_block`` (dK rows
     per tile), ``stages`` and ``ctas_per_sm`` override the frozen PathTile
     table of the native library for every shape; leave them None to use the
-    frozen choice.  The override is process-wide (the native library holds one
-    configuration), as is the reference's one installed runtime.
+    frozen choice.  The overrides belong to this runtime object: they travel
+    with each of its launches as per-call options (``pt_*_ex``), so two
+    runtimes in one process, a tuner beside a training job for instance, never
+    see each other's choices (the reference compiles one kernel module per
+    runtime, kernels/warp_tiled_ampere.py:636-691).
     ``dk_mode`` selects the dK reduction: "deterministic" (two-pass, default)
     or "atomic".  Both accumulate into ``gk`` in ``launch_bwd_weight`` so the
     reference contract -- the caller zero-fills gk -- holds for either.
@@ -295,6 +298,10 @@ class B200WarpRuntime:
             raise ValueError("This paper-confirmed version fixes BWDK_BTILE=64")
         if bwdk_block is not None and (bwdk_block < 32 or bwdk_block > 256 or bwdk_block % 32):
             raise ValueError("bwdk_block must be a multiple of 32 in [32, 256]")
+        if stages is not None and stages not in (2, 3, 4):
+            raise ValueError("stages must be 2, 3 or 4")
+        if ctas_per_sm is not None and ctas_per_sm not in (1, 2, 3, 4):
+            raise ValueError("ctas_per_sm must be 1, 2, 3 or 4")
         if fast_math:
             warnings.warn("fast_math is ignored: the B200 kernels are always strict FP32", stacklevel=2)
         if dk_mode not in ops.DK_MODES:
@@ -316,16 +323,7 @@ class B200WarpRuntime:
         self.fuse_backward = bool(fuse_backward)
         self.fast_math = False
         self._closed = False
-        self._apply_overrides()
-
-    def _apply_overrides(self) -> None:
-        if self.warps_per_block is not None or self.stages is not None or self.ctas_per_sm is not None:
-            rows = 32 * (self.warps_per_block or 4)
-            for path in ("fwd", "bwd_input"):
-                ops.set_config(path, rows, self.stages or 3, self.ctas_per_sm or 2, self.threads_per_row)
-        if self.bwdk_block is not None or self.stages is not None or self.ctas_per_sm is not None:
-            ops.set_config("bwd_weight", self.bwdk_block or 128, self.stages or 2, self.ctas_per_sm or 2,
-                           self.threads_per_row)
+        self.opts = launch_options(warps_per_block, bwdk_block, stages, ctas_per_sm, threads_per_row)
 
     @staticmethod
     def _check_shapes(x: torch.Tensor, k: torch.Tensor) -> tuple[int, int, int, int]:
@@ -339,13 +337,14 @@ class B200WarpRuntime:
                    collector: KernelEventCollector | None = None) -> None:
         self._check_open()
         B, H, L, K = self._check_shapes(x, k)
-        (collector or KERNEL_EVENTS).launch("fwd", lambda: ops.fwd(x, k, y), {"B": B, "H": H, "L": L, "K": K})
+        (collector or KERNEL_EVENTS).launch("fwd", lambda: ops.fwd(x, k, y, opts=self.opts),
+                                            {"B": B, "H": H, "L": L, "K": K})
 
     def launch_bwd_input(self, gy: torch.Tensor, k: torch.Tensor, gx: torch.Tensor,
                          collector: KernelEventCollector | None = None) -> None:
         self._check_open()
         B, H, L, K = self._check_shapes(gy, k)
-        (collector or KERNEL_EVENTS).launch("bwd_input", lambda: ops.dx(gy, k, gx),
+        (collector or KERNEL_EVENTS).launch("bwd_input", lambda: ops.dx(gy, k, gx, opts=self.opts),
                                             {"B": B, "H": H, "L": L, "K": K})
 
     def launch_bwd_weight(self, gy: torch.Tensor, x: torch.Tensor, gk: torch.Tensor, K: int,
@@ -366,7 +365,7 @@ class B200WarpRuntime:
             raise ValueError(f"Specialized kernels require L<={MAX_L}, K<={MAX_K}")
         mode = self.dk_mode
         (collector or KERNEL_EVENTS).launch(
-            "bwd_weight", lambda: ops.dk(gy, x, gk, mode=mode, accumulate=True),
+            "bwd_weight", lambda: ops.dk(gy, x, gk, mode=mode, accumulate=True, opts=self.opts),
             {"B": B, "H": H, "L": L, "K": K})
 
     def launch_bwd_fused(self, gy: torch.Tensor, x: torch.Tensor, k: torch.Tensor, gx: torch.Tensor,
@@ -378,27 +377,56 @@ class B200WarpRuntime:
         B, H, L, K = self._check_shapes(x, k)
         mode = self.dk_mode
         (collector or KERNEL_EVENTS).launch(
-            "bwd_fused", lambda: ops.dx_dk(gy, x, k, gk, gx=gx, mode=mode, accumulate=True),
+            "bwd_fused", lambda: ops.dx_dk(gy, x, k, gk, gx=gx, mode=mode, accumulate=True, opts=self.opts),
             {"B": B, "H": H, "L": L, "K": K})
 
     def resource_report(self, B: int = DEFAULT_B, H: int = DEFAULT_H, L: int = DEFAULT_L,
                         K: int = DEFAULT_K) -> list[dict[str, Any]]:
-        """Registers, shared memory and occupancy of the three kernels at one shape."""
+        """Registers, shared memory, spills and occupancy of the kernels this runtime
+        launches at one shape: FWD, dX and dK, plus the fused backward where
+        autograd would use it."""
         rows = []
-        for name in ("fwd", "bwd_input", "bwd_weight"):
-            info = ops.kernel_info(name, B, H, L, K, device=self.device_id)
+        names = ["fwd", "bwd_input", "bwd_weight"]
+        if self.fuse_backward and ops.fused_backward(B, H, L, K, opts=self.opts):
+            names.append("bwd_fused")
+        for name in names:
+            info = ops.kernel_info(name, B, H, L, K, device=self.device_id, opts=self.opts)
             est = estimate_gpu_occupancy(info["threads_per_block"], info["regs_per_thread"],
                                          info["static_smem_bytes"] + info["dynamic_smem_bytes"], self.profile)
             rows.append({"kernel": name, **est, **info})
         return rows
 
     def close(self) -> None:
+        """Synchronise the device; later launches through this runtime raise."""
         if self._closed:
             return
         torch.cuda.synchronize(self.device_id)
-        for path in ("fwd", "bwd_input", "bwd_weight"):
-            ops.set_config(path, 0)
         self._closed = True
+
+
+def launch_options(warps_per_block: int | None = None, bwdk_block: int | None = None, stages: int | None = None,
+                   ctas_per_sm: int | None = None, threads_per_row: int = 1):
+    """Per-call launch options (``pt_launch_opts``) for the reference's runtime
+    arguments: FWD/dX take ``warps_per_block`` 32-row warps per tile, dK
+    ``bwdk_block`` rows per tile; unset values keep the frozen table for that
+    path, unless another argument is set (it then fills in the defaults of the
+    reference runtime's launch: 4 warps, 3 stages, 2 CTAs per SM for FWD/dX;
+    128 rows, 2 stages, 2 CTAs per SM for dK)."""
+    from ._lib import LaunchOpts
+
+    o = LaunchOpts.frozen()
+    if warps_per_block is not None or stages is not None or ctas_per_sm is not None:
+        for p in (0, 1):
+            o.rows_per_tile[p] = 32 * (warps_per_block or 4)
+            o.stages[p] = stages or 3
+            o.ctas_per_sm[p] = ctas_per_sm or 2
+            o.threads_per_row[p] = threads_per_row
+    if bwdk_block is not None or stages is not None or ctas_per_sm is not None:
+        o.rows_per_tile[2] = bwdk_block or 128
+        o.stages[2] = stages or 2
+        o.ctas_per_sm[2] = ctas_per_sm or 2
+        o.threads_per_row[2] = threads_per_row
+    return o
 
 
 AmpereWarpRuntime = B200WarpRuntime

@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol(native_lib):
 
 def test_version_and_status_strings(native_lib):
     assert native_lib.pt_version() >= 100
-    for st in (0, -2, -3, -4, -5, -6, -7):
+    for st in (0, -2, -3, -4, -5, -6, -7, -8):
         assert _lib.status_string(st)
     assert "L <= 48" in _lib.status_string(_lib.PT_ERR_UNSUPPORTED)
 
@@ -82,6 +82,44 @@ def test_set_config_validation(native_lib):
     cfg = ops.config("fwd", 16384, 128, 48, 48)
     assert cfg["rows_per_tile"] == 64 and cfg["stages"] == 2 and cfg["threads_per_row"] == 2
     assert native_lib.pt_set_config(0, 0, 0, 0, 0) == _lib.PT_OK
+
+
+def test_per_call_options_validation_and_effect(native_lib):
+    o = _lib.LaunchOpts.frozen()
+    o.rows_per_tile[0], o.stages[0], o.ctas_per_sm[0], o.threads_per_row[0] = 64, 2, 1, 2
+    po = ctypes.cast(ctypes.pointer(o), ctypes.c_void_p)
+    # Per-call options change that call's plan only; the process-wide choice stays frozen.
+    assert ops.config("fwd", 16384, 128, 48, 48, opts=o)["rows_per_tile"] == 64
+    assert ops.config("fwd", 16384, 128, 48, 48)["rows_per_tile"] == 128
+    assert native_lib.pt_fwd_ex(FAKE, FAKE, FAKE, 0, 4, 16, 8, po, NULL) == _lib.PT_OK
+    bad = _lib.LaunchOpts.frozen()
+    bad.rows_per_tile[2], bad.stages[2], bad.ctas_per_sm[2], bad.threads_per_row[2] = 100, 3, 2, 1
+    pb = ctypes.cast(ctypes.pointer(bad), ctypes.c_void_p)
+    assert native_lib.pt_fwd_ex(FAKE, FAKE, FAKE, 2, 4, 16, 8, pb, NULL) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_dk_ex(FAKE, FAKE, FAKE, 2, 4, 16, 8, 1, NULL, 0, pb, NULL) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_dk_workspace_bytes_ex(2, 4, 16, 8, pb) == 0
+    eng = _lib.LaunchOpts.frozen()
+    eng.engine[1] = 7
+    pe = ctypes.cast(ctypes.pointer(eng), ctypes.c_void_p)
+    assert native_lib.pt_dx_ex(FAKE, FAKE, FAKE, 2, 4, 16, 8, pe, NULL) == _lib.PT_ERR_ARGS
+    out = (ctypes.c_int * 7)()
+    assert native_lib.pt_config_ex(0, 16, 4, 16, 8, out, 7, pe) == _lib.PT_ERR_ARGS
+
+
+def test_runtime_launch_options_map_reference_arguments():
+    o = runtime.launch_options(warps_per_block=2, bwdk_block=256, stages=4, ctas_per_sm=1)
+    assert list(o.rows_per_tile) == [64, 64, 256]
+    assert list(o.stages) == [4, 4, 4] and list(o.ctas_per_sm) == [1, 1, 1]
+    assert list(o.engine) == [-1, -1, -1]
+    f = runtime.launch_options()
+    assert list(f.rows_per_tile) == [0, 0, 0]  # all frozen
+
+
+def test_wait_selftest_argument_checks(native_lib):
+    assert native_lib.pt_selftest_wait_timeout(0, FAKE, NULL) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_selftest_wait_timeout(2_000_000_000, FAKE, NULL) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_selftest_wait_timeout(1000, NULL, NULL) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_selftest_wait_timeout(1000, MISALIGNED, NULL) == _lib.PT_ERR_ALIGN
 
 
 def test_frozen_config_and_specialisation_flags(native_lib):

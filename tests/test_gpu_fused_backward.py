@@ -136,28 +136,6 @@ def test_fused_backward_matches_separate_kernels(cuda_device):
     torch.testing.assert_close(gk_f, gk_s, rtol=DK_RTOL, atol=DK_RTOL * float(gk_s.abs().max()))
 
 
-def test_fused_backward_primary_workload(cuda_device):
-    dev = cuda_device
-    B, H, L, K = 16384, 128, 48, 48
-    if _sm_count(dev) >= 128:
-        assert ops.fused_backward(B, H, L, K)
-    x, k, dy, cpu = _inputs(B, H, L, K, 42, dev)
-    gx, gk = _run(dy, x, k)
-    rows = np.random.default_rng(11).choice(B * H, size=4096, replace=False)
-    rows.sort()
-    ridx = torch.from_numpy(rows).to(dev)
-    np.testing.assert_allclose(gx.reshape(B * H, L)[ridx].cpu().numpy(),
-                               c_oracle.dx_rows(cpu[2], cpu[1], rows), **FWD_TOL)
-    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
-    # <dK, k> = <dy, FWD(x)> = <dX(dy), x> over the whole tensors.
-    y = ops.fwd(x, k)
-    a = float((gk.double() * k.double()).sum())
-    b = float((y.double() * dy.double()).sum())
-    c = float((gx.double() * x.double()).sum())
-    scale = float(y.double().abs().sum()) + 1.0
-    assert abs(a - b) <= 1e-6 * scale and abs(c - b) <= 1e-6 * scale
-
-
 def test_fused_backward_side_stream(cuda_device):
     dev = cuda_device
     x, k, dy, cpu = _inputs(1500, 128, 48, 16, 8, dev)

@@ -52,23 +52,17 @@ def test_golden_vectors(cuda_device, case, mode):
     np.testing.assert_allclose(y.cpu().numpy(), g["y64"], **FWD_TOL)
     np.testing.assert_allclose(gx.cpu().numpy(), g["gx64"], **FWD_TOL)
     assert_dk_close(gk.cpu().numpy(), g["gk64"])
+    # Accuracy margin against the FP64 reference (1.0 = at the 1e-5 bar): the
+    # 3xTF32 tensor-core path and the FFMA path both stay at or below half the bar.
+    for got, ref in ((y, g["y64"]), (gx, g["gx64"])):
+        err = np.abs(got.cpu().numpy().astype(np.float64) - ref)
+        margin = float((err / (FWD_TOL["atol"] + FWD_TOL["rtol"] * np.abs(ref))).max()) if ref.size else 0.0
+        assert margin <= 0.5, margin
 
 
 def _inputs(B, H, L, K, seed, device):
     x, k, dy = reference_torch.make_inputs(B, H, L, K, seed)
     return x.to(device), k.to(device), dy.to(device), (x, k, dy)
-
-
-def _check_rows(y, gx, cpu, n_rows=2048, seed=0):
-    x, k, dy = cpu
-    B, H, L = x.shape
-    rows = np.random.default_rng(seed).choice(B * H, size=min(n_rows, B * H), replace=False)
-    rows.sort()
-    y_ref = c_oracle.fwd_rows(x, k, rows)
-    gx_ref = c_oracle.dx_rows(dy, k, rows)
-    ridx = torch.from_numpy(rows).to(y.device)
-    np.testing.assert_allclose(y.reshape(B * H, L)[ridx].cpu().numpy(), y_ref, **FWD_TOL)
-    np.testing.assert_allclose(gx.reshape(B * H, L)[ridx].cpu().numpy(), gx_ref, **FWD_TOL)
 
 
 def _adjoint_checks(x, k, dy, y, gx, gk):
@@ -88,14 +82,14 @@ FULL_SHAPES = [
     (16384, 128, 48, 3),
     (2048, 512, 33, 33),
 ]
+# Every element of FWD, dX and dK at these shapes, on every engine, is compared
+# with the FP64 oracle in tests/test_gpu_full_size.py.
 
 
 @pytest.mark.parametrize("B,H,L,K", FULL_SHAPES)
-def test_full_size_against_fp64_oracle(cuda_device, B, H, L, K):
+def test_full_size_adjoint_identities(cuda_device, B, H, L, K):
     x, k, dy, cpu = _inputs(B, H, L, K, 42, cuda_device)
     y, gx, gk = run_path(x, k, dy)
-    _check_rows(y, gx, cpu)
-    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
     _adjoint_checks(x, k, dy, y, gx, gk)
     assert ops.device_error() == 0
 
@@ -202,7 +196,7 @@ def test_side_stream(cuda_device):
         ops.dk(dy, x, gk)
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
-    _check_rows(y, ops.dx(dy, k), cpu, n_rows=512)
+    np.testing.assert_allclose(y.cpu().numpy(), c_oracle.fwd(cpu[0], cpu[1]), **FWD_TOL)
     assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], 48))
 
 
@@ -250,11 +244,43 @@ def test_reference_runtime_surface(cuda_device):
     out = runtime.depthwise_conv_ampere(xr, k)
     out.backward(dy)
     np.testing.assert_allclose(xr.grad.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
-    report = rt.resource_report()
-    assert {r["kernel"] for r in report} == {"fwd", "bwd_input", "bwd_weight"}
-    assert all(r["local_memory_bytes"] == 0 for r in report)
+    report = {r["kernel"]: r for r in rt.resource_report()}
+    expect = {"fwd", "bwd_input", "bwd_weight"} | ({"bwd_fused"} if ops.fused_backward(16384, 128, 48, 48) else set())
+    assert set(report) == expect
+    assert all(report[p]["local_memory_bytes"] == 0 for p in ("fwd", "bwd_input", "bwd_weight"))
+    assert all(r["regs_per_thread"] > 0 and r["resident_blocks_per_sm"] >= 1 for r in report.values())
     rt.close()
     runtime._RUNTIME = None
+
+
+def test_two_runtimes_keep_their_own_launch_options(cuda_device):
+    """Each runtime's overrides travel with its own launches; neither changes the
+    process-wide (frozen) choice nor the other runtime's."""
+    B, H, L, K = 700, 128, 48, 48
+    frozen = ops.config("fwd", B, H, L, K)
+    a = runtime.B200WarpRuntime(warps_per_block=2, stages=2, ctas_per_sm=1, bwdk_block=64)
+    b = runtime.B200WarpRuntime()
+    assert ops.config("fwd", B, H, L, K) == frozen
+    assert ops.config("fwd", B, H, L, K, opts=a.opts)["rows_per_tile"] == 64
+    assert ops.config("bwd_weight", B, H, L, K, opts=a.opts)["rows_per_tile"] == 64
+    assert ops.config("fwd", B, H, L, K, opts=b.opts) == frozen
+    x, k, dy, cpu = _inputs(B, H, L, K, 17, cuda_device)
+    outs = {}
+    for name, rt in (("a", a), ("b", b), ("a2", a)):
+        y, gx, gk = torch.empty_like(x), torch.empty_like(x), torch.zeros_like(k)
+        rt.launch_fwd(x, k, y)
+        rt.launch_bwd_input(dy, k, gx)
+        rt.launch_bwd_weight(dy, x, gk, K)
+        torch.cuda.synchronize()
+        outs[name] = (y, gx, gk)
+    assert ops.device_error(clear=True) == 0
+    y64, gx64, gk64 = c_oracle.fwd(cpu[0], cpu[1]), c_oracle.dx(cpu[2], cpu[1]), c_oracle.dk(cpu[2], cpu[0], K)
+    for y, gx, gk in outs.values():
+        np.testing.assert_allclose(y.cpu().numpy(), y64, **FWD_TOL)
+        np.testing.assert_allclose(gx.cpu().numpy(), gx64, **FWD_TOL)
+        assert_dk_close(gk.cpu().numpy(), gk64)
+    a.close()
+    assert ops.config("fwd", B, H, L, K) == frozen
 
 
 def test_legacy_warp_tiled_surface(cuda_device):
