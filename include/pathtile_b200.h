@@ -115,14 +115,18 @@ PT_API int pt_dk_noalloc(const float* dy, const float* x, float* dk, int B, int 
 
 /*
  * Input and filter gradients in one call: dx as pt_dx, dk as pt_dk (same
- * modes and workspace rules; query pt_dx_dk_workspace_bytes).  For rows of
- * 32 < L <= 48 columns with L % 4 == 0 and any K <= 48, unless dX is forced onto
- * the CUDA cores (pt_set_engine), and where the grid can give every CTA a
- * single channel, one fused kernel reads dy and x once and
- * writes dx (dX on the tensor cores, dK on the CUDA cores; no workspace when
- * each channel has one CTA); other shapes run pt_dx then pt_dk.  The reference
- * launches the two separately (DepthConvAmpere.backward,
- * kernels/warp_tiled_ampere.py:882-898); no fused counterpart.
+ * modes and workspace rules; query pt_dx_dk_workspace_bytes).  One kernel
+ * reads dy and x once and writes dx wherever a fused kernel applies:
+ *  - the tensor-core one (dX on tcgen05, dK on the CUDA cores) for rows of
+ *    32 < L <= 48 columns with L % 4 == 0 and any K <= 48, unless dX is forced
+ *    onto the CUDA cores, where the grid can give every CTA a single channel
+ *    (no workspace when each channel has one CTA);
+ *  - otherwise the CUDA-core one for every (L, K) with a specialised CUDA-core
+ *    kernel (and H*L % 4 == 0 when L % 4 != 0), unless dX or dK is forced onto
+ *    the tensor cores;
+ * other shapes run pt_dx then pt_dk.  The reference launches the two
+ * separately (DepthConvAmpere.backward, kernels/warp_tiled_ampere.py:882-898);
+ * no fused counterpart.
  */
 PT_API int pt_dx_dk(const float* dy, const float* x, const float* k, float* dx, float* dk, int B, int H,
                     int L, int K, int mode, void* ws, size_t ws_bytes, void* stream);
@@ -143,7 +147,8 @@ PT_API int pt_dk_cl(const float* dy, const float* x, float* dk, int B, int L, in
 /* Workspace bytes pt_dk_cl needs for this shape on the current device (0 if invalid). */
 PT_API size_t pt_dk_cl_workspace_bytes(int B, int L, int H, int K);
 
-/* 1 if pt_dx_dk runs the fused kernel for this shape on the current device, else 0. */
+/* Kernel pt_dx_dk runs for this shape on the current device: 1 the tensor-core
+ * fused kernel, 2 the CUDA-core fused kernel, 0 pt_dx then pt_dk. */
 PT_API int pt_dx_dk_fused(int B, int H, int L, int K);
 
 /* Workspace bytes pt_dx_dk needs for this shape (0 for invalid shapes or none needed). */

@@ -268,8 +268,14 @@ struct Plan {
 // 8 distinct 16-byte bank groups iff pitch/4 is odd.
 int tma_pitch(int L) { return (!g_padded_box_ok || (L / 4) % 2 == 1) ? L : L + 4; }
 
+// Internal path id of plan_exact: the fused CUDA-core backward (bwd_rows_kernel),
+// planned with the dK path's launch configuration and one thread per row.
+constexpr int kPathBwdRows = 4;
+
 int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::Entry& e, Plan& p) {
-  const pt::LaunchCfg cfg = cfg_for(path, L, K);
+  const bool bwd = (path == kPathBwdRows);
+  const bool two_inputs = bwd || path == PT_PATH_DK;
+  const pt::LaunchCfg cfg = cfg_for(bwd ? PT_PATH_DK : path, L, K);
   pt::TileGeom& g = p.g;
   g.B = B;
   g.H = H;
@@ -298,19 +304,20 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
   const int T = g.Th * g.Tb;
   const long long tile_bytes = static_cast<long long>(g.pitch) * T * 4;
   long long stage = (tile_bytes + 1023) / 1024 * 1024;
-  // Buffers: DK = (dy, x) per stage; FWD/DX = one in-place buffer per stage.
-  auto n_buf = [&](int stages) { return (path == PT_PATH_DK) ? 2 * stages : stages; };
+  // Buffers: DK and the fused backward = (dy, x) per stage; FWD/DX = one in-place buffer per stage.
+  auto n_buf = [&](int stages) { return two_inputs ? 2 * stages : stages; };
+  // mbarriers: full + done per stage (+ the fused backward's stores-done barrier, padded to 16 bytes).
+  auto bars = [&](int stages) { return 2LL * stages * 8 + (bwd ? 16 : 0); };
   // Fewer stages when the buffers would not fit the per-block shared memory.
-  while (g.stages > 2 &&
-         static_cast<long long>(n_buf(g.stages)) * stage + (2LL * g.stages) * 8 + 1024 > di.max_smem)
+  while (g.stages > 2 && static_cast<long long>(n_buf(g.stages)) * stage + bars(g.stages) + 1024 > di.max_smem)
     --g.stages;
-  if (path == PT_PATH_DK) {
+  if (two_inputs) {
     // The idle ring doubles as the [K][T] in-CTA reduction buffer at the end.
     const long long red = static_cast<long long>(K) * T * 4;
     if (n_buf(g.stages) * stage < red)
       stage = ((red + n_buf(g.stages) - 1) / n_buf(g.stages) + 1023) / 1024 * 1024;
   }
-  const long long bar_bytes = 2LL * g.stages * 8;  // full + done per stage
+  const long long bar_bytes = bars(g.stages);
   if (static_cast<long long>(n_buf(g.stages)) * stage + bar_bytes + 1024 > di.max_smem)
     return PT_ERR_UNSUPPORTED;
   g.stage_bytes = static_cast<unsigned>(stage);
@@ -318,9 +325,12 @@ int plan_exact(int path, int B, int H, int L, int K, DeviceInfo& di, const pt::E
   p.smem = static_cast<size_t>(n_buf(g.stages)) * stage + static_cast<size_t>(bar_bytes) + 1024;
   // Two consumer threads per row only while the CTA stays within 288 threads
   // (the kernels' launch bound); larger tiles run one thread per row.
-  const int tpr = (cfg.tpr == 2 && 2 * round_up(T, 32) + 32 <= 288) ? 2 : 1;
+  const int tpr = (!bwd && cfg.tpr == 2 && 2 * round_up(T, 32) + 32 <= 288) ? 2 : 1;
   p.threads = tpr * round_up(T, 32) + 32;  // consumer warps (tpr per row) + one producer warp
-  p.func = (path == PT_PATH_FWD) ? e.fwd[tpr - 1] : (path == PT_PATH_DX) ? e.dx[tpr - 1] : e.dk[tpr - 1];
+  p.func = bwd                    ? e.bwd
+           : (path == PT_PATH_FWD) ? e.fwd[tpr - 1]
+           : (path == PT_PATH_DX)  ? e.dx[tpr - 1]
+                                   : e.dk[tpr - 1];
   p.exact = true;
   int rc = ensure_smem_attr(di, p.func, p.smem);
   if (rc != PT_OK) return rc;
@@ -449,7 +459,12 @@ int encode_pair(int path, int B, int H, int L, int K, DeviceInfo& di, Plan& p, C
   if (rc == PT_OK) rc = encode_rows_tmap(b, pb, p.g);
   if (rc == PT_OK || p.g.pitch == L) return rc;
   g_padded_box_ok = false;
-  if ((rc = plan(path, B, H, L, K, di, p)) != PT_OK) return rc;
+  if (path == kPathBwdRows) {
+    const pt::Entry* e = find_entry(L, K);
+    if (!e || (rc = plan_exact(path, B, H, L, K, di, *e, p)) != PT_OK) return e ? rc : PT_ERR_UNSUPPORTED;
+  } else if ((rc = plan(path, B, H, L, K, di, p)) != PT_OK) {
+    return rc;
+  }
   rc = encode_rows_tmap(a, pa, p.g);
   if (rc == PT_OK) rc = encode_rows_tmap(b, pb, p.g);
   return rc;
@@ -619,6 +634,55 @@ int launch_fused(const Plan& p, const float* dy, const float* x, const float* k,
   if (ce != cudaSuccess) return cuda_fail(ce);
   if (!direct) {
     pt::tc::dk_reduce(out, group_of, static_cast<int>(slots), H, g.K, 1, dk, accumulate, stream);
+    if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_fail(ce);
+  }
+  return PT_OK;
+}
+
+size_t dk_ws_bytes(const Plan& p);
+
+// Fused backward on the CUDA cores (bwd_rows_kernel): shapes with a specialised
+// CUDA-core kernel whose loader applies, where the tensor-core fused kernel
+// does not, and where neither dX nor dK is forced onto the tensor cores.
+bool plan_bwd_rows(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
+  const Opts& o = opts();
+  if (o.engine[PT_PATH_DX] == PT_ENGINE_TENSOR || o.engine[PT_PATH_DK] == PT_ENGINE_TENSOR) return false;
+  const pt::Entry* e = find_entry(L, K);
+  if (!e) return false;
+  if (!((e->loader == pt::LOAD_TMA3D && g_encode != nullptr) ||
+        (e->loader == pt::LOAD_BULK1D && (static_cast<long long>(H) * L) % 4 == 0)))
+    return false;
+  return plan_exact(kPathBwdRows, B, H, L, K, di, *e, p) == PT_OK;
+}
+
+int launch_bwd_rows(Plan& p, DeviceInfo& di, const float* dy, const float* x, const float* k, float* dx,
+                    float* dk, int mode, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  const int B = p.g.B, H = p.g.H, L = p.g.L, K = p.g.K;
+  CUtensorMap tm_dy, tm_x, tm_dx;
+  std::memset(&tm_dy, 0, sizeof(tm_dy));
+  std::memset(&tm_x, 0, sizeof(tm_x));
+  std::memset(&tm_dx, 0, sizeof(tm_dx));
+  int rc = PT_OK;
+  if (p.loader == pt::LOAD_TMA3D) {
+    if ((rc = encode_pair(kPathBwdRows, B, H, L, K, di, p, &tm_dy, dy, &tm_x, x)) != PT_OK) return rc;
+    if ((rc = encode_rows_tmap(&tm_dx, dx, p.g)) != PT_OK) return rc;
+  }
+  const int atomic_mode = (mode == PT_DK_ATOMIC) ? 1 : 0;
+  float* dst = dk;
+  if (!atomic_mode) {
+    if (!ws || ws_bytes < dk_ws_bytes(p)) return PT_ERR_WORKSPACE;
+    if (!aligned16(ws)) return PT_ERR_ALIGN;
+    dst = static_cast<float*>(ws);
+  }
+  pt::TileGeom g = p.g;
+  unsigned* err = di.err;
+  void* args[] = {&tm_dy, &tm_x, &tm_dx, const_cast<float**>(&dy), const_cast<float**>(&x),
+                  const_cast<float**>(&k), &dx, &dst, &g, const_cast<int*>(&atomic_mode), &err};
+  cudaError_t ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  if (!atomic_mode) {
+    const dim3 grid2((H + 31) / 32, K);
+    pt::dk_reduce_kernel<<<grid2, 256, 0, stream>>>(dst, dk, g, mode == PT_DK_DETERMINISTIC_ACCUMULATE ? 1 : 0);
     if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_fail(ce);
   }
   return PT_OK;
@@ -808,7 +872,8 @@ int pt_dx_dk_fused(int B, int H, int L, int K) {
   DeviceInfo* di = nullptr;
   if (current_device(di) != PT_OK) return 0;
   Plan p;
-  return plan_fused(B, H, L, K, *di, p) ? 1 : 0;
+  if (plan_fused(B, H, L, K, *di, p)) return 1;
+  return plan_bwd_rows(B, H, L, K, *di, p) ? 2 : 0;
 }
 
 size_t pt_dx_dk_workspace_bytes(int B, int H, int L, int K) {
@@ -817,6 +882,7 @@ size_t pt_dx_dk_workspace_bytes(int B, int H, int L, int K) {
   if (current_device(di) != PT_OK) return 0;
   Plan p;
   if (plan_fused(B, H, L, K, *di, p)) return fused_ws_bytes(p);
+  if (plan_bwd_rows(B, H, L, K, *di, p)) return dk_ws_bytes(p);
   return pt_dk_workspace_bytes(B, H, L, K);
 }
 
@@ -840,6 +906,8 @@ int pt_dx_dk(const float* dy, const float* x, const float* k, float* dx, float* 
     }
     return launch_fused(p, dy, x, k, dx, dk, mode, ws, di->err, static_cast<cudaStream_t>(stream_v));
   }
+  if (plan_bwd_rows(B, H, L, K, *di, p))
+    return launch_bwd_rows(p, *di, dy, x, k, dx, dk, mode, ws, ws_bytes, static_cast<cudaStream_t>(stream_v));
   if ((rc = pt_dx(dy, k, dx, B, H, L, K, stream_v)) != PT_OK) return rc;
   return pt_dk(dy, x, dk, B, H, L, K, mode, ws, ws_bytes, stream_v);
 }
@@ -933,7 +1001,7 @@ int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n) {
   if (rc != PT_OK) return rc;
   Plan p;
   if (path == PT_PATH_BWD_FUSED) {
-    if (!plan_fused(B, H, L, K, *di, p)) return PT_ERR_UNSUPPORTED;
+    if (!plan_fused(B, H, L, K, *di, p) && !plan_bwd_rows(B, H, L, K, *di, p)) return PT_ERR_UNSUPPORTED;
   } else if ((rc = plan(path, B, H, L, K, *di, p)) != PT_OK) {
     return rc;
   }

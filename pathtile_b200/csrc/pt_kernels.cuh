@@ -290,6 +290,41 @@ __device__ __forceinline__ void conv_row(const float (&in)[L], const float (&tap
   }
 }
 
+// conv_row with each group of four outputs written to the row at `p` as soon
+// as it is complete (the input row is already in registers, so the row may be
+// the input's own shared-memory row): four output registers live, not L.
+template <int L, int K, int PAD, int LOADER>
+__device__ __forceinline__ void conv_row_to_smem(const float (&in)[L], const float (&taps)[K],
+                                                 float* __restrict__ p) {
+  constexpr int G = 4;
+#pragma unroll
+  for (int t0 = 0; t0 < L; t0 += G) {
+    float acc[G];
+#pragma unroll
+    for (int u = 0; u < G; ++u) acc[u] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+#pragma unroll
+      for (int u = 0; u < G; ++u) {
+        const int t = t0 + u;
+        const int i = t + j - PAD;
+        if (t < L && i >= 0 && i < L) acc[u] = fmaf(in[i], taps[j], acc[u]);
+      }
+    }
+    if constexpr (LOADER == LOAD_TMA3D) {
+      *reinterpret_cast<float4*>(p + t0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    } else if constexpr (L % 2 == 0) {
+#pragma unroll
+      for (int u = 0; u < G; u += 2)
+        if (t0 + u < L) *reinterpret_cast<float2*>(p + t0 + u) = make_float2(acc[u], acc[u + 1]);
+    } else {
+#pragma unroll
+      for (int u = 0; u < G; ++u)
+        if (t0 + u < L) p[t0 + u] = acc[u];
+    }
+  }
+}
+
 // Output split for two threads per row: the first thread computes outputs
 // [0, kSplit), the second [kSplit, L).  A multiple of 4 (128-bit stores) near
 // L/2; the in-range FFMA counts of the halves differ by a few percent.
@@ -642,6 +677,156 @@ __global__ void __launch_bounds__(288, 1)
       const int j = part + TPR * m;
       if (j < K) red[j * T + r] = acc[m];
     }
+  }
+  named_barrier(1, nc);
+  const int nh = min(g.Th, g.H - cur.hb * g.Th);
+  for (int idx = tid; idx < K * nh; idx += nc) {
+    const int j = idx / nh;
+    const int hl = idx - j * nh;
+    float sum = 0.0f;
+    for (int bl = 0; bl < g.Tb; ++bl) sum += red[j * T + bl * g.Th + hl];
+    if (atomic_mode) {
+      atomicAdd(dst + static_cast<long long>(cur.hb * g.Th + hl) * g.K + j, sum);
+    } else {
+      dst[(static_cast<long long>(blockIdx.x) * g.K + j) * g.Th + hl] = sum;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fused backward on the CUDA cores: dX and dK from one pass over dy and x.
+// For the shapes the tensor-core fused kernel does not take (rows of L <= 32
+// or L % 4 != 0, or a channel count whose grid cannot keep one channel per
+// CTA).  Separately, dX reads dy and writes dx and dK reads dy and x (four
+// [B, H, L] streams); here three.  Stages hold the (dy, x) tiles as in DK pass
+// 1; each consumer thread takes its dy and x rows into registers, adds the
+// row's filter-gradient terms to its K accumulators, computes its dx row from
+// the dy row and the channel's reversed taps, and writes it over its dy row.
+// The producer stores the dx tile from the dy buffer, waits until the store
+// has read it, then refills the stage.  The filter-gradient epilogue is DK
+// pass 1's (in-CTA fixed-order sum, then an atomic or a partial per (CTA, j, h));
+// it reuses the ring only after the producer reports, on one more mbarrier,
+// that its last stores have read shared memory.
+// ---------------------------------------------------------------------------
+template <int L, int K, int LOADER>
+__global__ void __launch_bounds__(288, 1)
+    bwd_rows_kernel(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_x,
+                    const __grid_constant__ CUtensorMap tm_dx, const float* __restrict__ dy,
+                    const float* __restrict__ x, const float* __restrict__ taps_hk, float* __restrict__ dx,
+                    float* __restrict__ dst, const TileGeom g, const int atomic_mode, unsigned* __restrict__ err) {
+  constexpr int PAD_K = K / 2;          // dK: x[t + j - K/2]
+  constexpr int PAD_X = K - 1 - K / 2;  // dX: dy[t + j' - (K-1-K/2)] k[K-1-j']
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  const int tid = static_cast<int>(threadIdx.x);
+  const int nc = static_cast<int>(blockDim.x) - 32;
+  const TileCursor cur(g);
+  const int S = g.stages;
+  auto buf = [&](int s, int which) -> float* {
+    return reinterpret_cast<float*>(smem + static_cast<size_t>(2 * s + which) * g.stage_bytes);
+  };
+  const PipeBars bars = carve_bars(smem + static_cast<size_t>(2 * S) * g.stage_bytes, S);
+  uint64_t* stored = bars.done + S;  // the producer's last stores have read shared memory
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&bars.full[s]), 1);
+      mbar_init(smem_u32(&bars.done[s]), static_cast<uint32_t>(nc));
+    }
+    mbar_init(smem_u32(stored), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (tid >= nc) {  // ---------------- producer warp ----------------
+    if (tid != nc) return;
+    if constexpr (LOADER == LOAD_TMA3D) {
+      prefetch_tmap(&tm_dy);
+      prefetch_tmap(&tm_x);
+      prefetch_tmap(&tm_dx);
+    }
+    auto load = [&](int t) {
+      const int s = t % S;
+      const int q = cur.q(t);
+      const uint32_t bar = smem_u32(&bars.full[s]);
+      mbar_arrive_expect_tx(bar, 2u * tile_tx_bytes<LOADER>(g, cur.hb, q));
+      issue_tile_load<LOADER>(g, &tm_dy, dy, cur.hb, q, smem_u32(buf(s, 0)), bar);
+      issue_tile_load<LOADER>(g, &tm_x, x, cur.hb, q, smem_u32(buf(s, 1)), bar);
+    };
+    int issued = 0;
+    for (; issued < min(S, cur.n_it); ++issued) load(issued);
+    for (int it = 0; it < cur.n_it; ++it) {
+      const int s = it % S;
+      // Every dx row of tile it is in place over its dy row: store the tile.
+      if (!mbar_wait_bounded(smem_u32(&bars.done[s]), static_cast<uint32_t>(it / S) & 1u, err,
+                             DEVERR_TIMEOUT_DONE))
+        break;
+      const int q = cur.q(it);
+      if constexpr (LOADER == LOAD_TMA3D) {
+        tma_store_3d(&tm_dx, smem_u32(buf(s, 0)), 0, cur.hb * g.Th, q * g.Tb);
+      } else {
+        long long row0;
+        int nrows;
+        tile_rows(g, cur.hb, q, row0, nrows);
+        bulk_store_1d(dx + row0 * g.L, smem_u32(buf(s, 0)), static_cast<uint32_t>(nrows) * g.L * 4u);
+      }
+      bulk_commit();
+      if (it + S < cur.n_it) {
+        bulk_wait_read<0>();  // the store has read stage s: refill it
+        load(it + S);
+        ++issued;
+      }
+    }
+    producer_drain(bars, S, issued, err);  // loads landed, stores complete
+    mbar_arrive(smem_u32(stored));
+    return;
+  }
+
+  // ---------------- consumer threads: one per row ----------------
+  const int r = tid;
+  const int T = g.Th * g.Tb;
+  const int h_local = r % g.Th;
+  const int b_local = r / g.Th;
+  const int h = cur.hb * g.Th + h_local;
+  const bool thread_has_row = (r < T) && (h < g.H);
+  float taps[K];  // reversed: dX is FWD with reversed taps and left pad K-1-K/2
+#pragma unroll
+  for (int j = 0; j < K; ++j)
+    taps[j] = thread_has_row ? __ldg(taps_hk + static_cast<long long>(h) * K + (K - 1 - j)) : 0.0f;
+  float acc[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) acc[j] = 0.0f;
+  bool failed = false;
+  for (int it = 0; it < cur.n_it; ++it) {
+    const int s = it % S;
+    if (!mbar_wait_bounded(smem_u32(&bars.full[s]), static_cast<uint32_t>(it / S) & 1u, err,
+                           DEVERR_TIMEOUT_FULL)) {
+      failed = true;
+      break;
+    }
+    if (thread_has_row && cur.q(it) * g.Tb + b_local < g.B) {
+      float* dyp = buf(s, 0) + static_cast<size_t>(r) * g.pitch;
+      float gyr[L];
+      row_load<L, LOADER>(dyp, gyr);
+      {
+        float xr[L];
+        row_load<L, LOADER>(buf(s, 1) + static_cast<size_t>(r) * g.pitch, xr);
+        xcorr_row<L, K, PAD_K>(gyr, xr, acc);
+      }
+      conv_row_to_smem<L, K, PAD_X, LOADER>(gyr, taps, dyp);
+    }
+    fence_proxy_async_smem();  // the dx row write precedes the async-proxy store
+    mbar_arrive(smem_u32(&bars.done[s]));
+  }
+  if (named_barrier_or(1, nc, failed)) return;
+  // The ring becomes the reduction buffer once the producer's stores have read it.
+  bool ok = mbar_wait_bounded(smem_u32(stored), 0, err, DEVERR_TIMEOUT_DONE);
+  if (named_barrier_or(1, nc, !ok)) return;
+
+  float* red = reinterpret_cast<float*>(smem);  // [K][T]
+  if (r < T) {
+#pragma unroll
+    for (int j = 0; j < K; ++j) red[j * T + r] = acc[j];
   }
   named_barrier(1, nc);
   const int nh = min(g.Th, g.H - cur.hb * g.Th);

@@ -14,6 +14,7 @@ struct Entry {
   const void* fwd[2];  // conv_rows_kernel<L,K,OP_FWD,loader,TPR>, TPR = 1, 2
   const void* dx[2];   // conv_rows_kernel<L,K,OP_DX,loader,TPR>
   const void* dk[2];   // dk_rows_kernel<L,K,loader,TPR>
+  const void* bwd;     // bwd_rows_kernel<L,K,loader>: fused dX + dK on the CUDA cores
 };
 
 template <int L, int K>
@@ -27,7 +28,8 @@ Entry make_entry() {
                {reinterpret_cast<const void*>(&conv_rows_kernel<L, K, OP_DX, LD, 1>),
                 reinterpret_cast<const void*>(&conv_rows_kernel<L, K, OP_DX, LD, 2>)},
                {reinterpret_cast<const void*>(&dk_rows_kernel<L, K, LD, 1>),
-                reinterpret_cast<const void*>(&dk_rows_kernel<L, K, LD, 2>)}};
+                reinterpret_cast<const void*>(&dk_rows_kernel<L, K, LD, 2>)},
+               reinterpret_cast<const void*>(&bwd_rows_kernel<L, K, LD>)};
 }
 
 void register_shard_0(std::vector<Entry>& v);

@@ -257,10 +257,12 @@ def dx_dk(
     opts: "_lib.LaunchOpts | None" = None,
 ) -> torch.Tensor:
     """Both backward products in one call: returns gx = dX(dy, k) and writes the
-    filter gradient into gk with dk()'s modes (and its workspace rules).  For 32 < L <= 48 (L % 4 == 0)
-    and any K on grids that give each CTA one channel this is one fused kernel
-    (dy and x read once); other shapes run dx() then dk().  The reference's
-    backward launches the two separately (kernels/warp_tiled_ampere.py:882-898).
+    filter gradient into gk with dk()'s modes (and its workspace rules).  Where a
+    fused kernel applies (see backward_kind) dy and x are read once: the
+    tensor-core one for 32 < L <= 48 (L % 4 == 0) on grids that give each CTA one
+    channel, else the CUDA-core one for the specialised (L, K) shapes; other
+    shapes run dx() then dk().  The reference's backward launches the two
+    separately (kernels/warp_tiled_ampere.py:882-898).
     """
     _ensure_cuda_f32(dy, "gy")
     _ensure_cuda_f32(x, "x")
@@ -303,21 +305,34 @@ def dx_dk(
     return gx
 
 
+BACKWARD_KINDS = {0: "separate", 1: "tensor_fused", 2: "ffma_fused"}
+
+
+def backward_kind(B: int, H: int, L: int, K: int, opts: "_lib.LaunchOpts | None" = None) -> str:
+    """What dx_dk() runs at this shape on the current device: "tensor_fused" (one
+    kernel, dX on tcgen05, dK on the CUDA cores), "ffma_fused" (one kernel on the
+    CUDA cores) or "separate" (dx() then dk())."""
+    return BACKWARD_KINDS[int(_lib.load().pt_dx_dk_fused_ex(B, H, L, K, _opts_ptr(opts)))]
+
+
 def fused_backward(B: int, H: int, L: int, K: int, opts: "_lib.LaunchOpts | None" = None) -> bool:
-    """True when dx_dk() runs the single fused kernel at this shape on the current device."""
-    return bool(_lib.load().pt_dx_dk_fused_ex(B, H, L, K, _opts_ptr(opts)))
+    """True when dx_dk() reads dy and x once (one fused kernel) at this shape on the current device."""
+    return backward_kind(B, H, L, K, opts) != "separate"
 
 
-def dx_dk_launches(B: int, H: int, L: int, K: int, opts: "_lib.LaunchOpts | None" = None) -> int:
-    """Kernel launches of one deterministic dx_dk() at this shape: the fused kernel
-    (plus the partial reduce when a channel spans several CTAs), or dX + the
-    two-pass dK."""
+def dx_dk_launches(B: int, H: int, L: int, K: int, opts: "_lib.LaunchOpts | None" = None,
+                   mode: str = "deterministic") -> int:
+    """Kernel launches of one dx_dk() at this shape: the fused kernel (plus a partial
+    reduce where the deterministic dK needs one), or dX + the dK kernels."""
     if B <= 0:
         return 0
     lib = _lib.load()
-    if lib.pt_dx_dk_fused_ex(B, H, L, K, _opts_ptr(opts)):
+    kind = int(lib.pt_dx_dk_fused_ex(B, H, L, K, _opts_ptr(opts)))
+    if kind == 1:
         return 1 if int(lib.pt_dx_dk_workspace_bytes_ex(B, H, L, K, _opts_ptr(opts))) == 0 else 2
-    return 3
+    if kind == 2:
+        return 1 if mode == "atomic" else 2
+    return 2 if mode == "atomic" else 3
 
 
 # ---------------- channels-last [B, L, H] ----------------

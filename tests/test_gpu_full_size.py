@@ -103,5 +103,5 @@ def test_every_element_every_engine_against_fp64(cuda_device, B, H, L, K):
     torch.cuda.synchronize()
     assert ops.device_error(clear=True) == 0, "a kernel wait expired"
     m = dict(dx=conv_margin(gx, gx64), dk=dk_margin(gk, gk64))
-    record(test="full_size", **shape, requested="dx_dk", fused=ops.fused_backward(B, H, L, K), margin=m)
+    record(test="full_size", **shape, requested="dx_dk", kind=ops.backward_kind(B, H, L, K), margin=m)
     assert m["dx"] <= 1.0 and m["dk"] <= 1.0, m

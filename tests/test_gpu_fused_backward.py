@@ -1,14 +1,16 @@
-"""GPU parity of the fused backward (one kernel: dX on the tensor cores, dK on
-the CUDA cores) reached through ops.dx_dk / pt_dx_dk.
+"""GPU parity of the fused backward reached through ops.dx_dk / pt_dx_dk: the
+tensor-core kernel (dX on tcgen05, dK on the CUDA cores) and the CUDA-core
+kernel (dX and dK both FFMA, one pass over dy and x).
 
 Bars as for the separate kernels: dX within rtol = atol = 1e-5 of the FP64 C
-oracle, dK within 1e-4 relative of the FP64 dK.  Covered: every fused
-instantiation class (every K <= 48; rows of 32 < L <= 48 columns, L % 4 == 0,
-in the kernel's 48-column layout), both dK regimes of the
-fused kernel (one CTA per channel writes dK directly; several CTAs per channel
-write partials summed by the reduce kernel), the three dK modes, ragged batch
-tiles, grids smaller than the SM count, and shapes that fall back to pt_dx +
-pt_dk.
+oracle, dK within 1e-4 relative of the FP64 dK.  Covered: every tensor-core
+fused instantiation class (every K <= 48; rows of 32 < L <= 48 columns,
+L % 4 == 0, in the kernel's 48-column layout), both dK regimes of that kernel
+(one CTA per channel writes dK directly; several CTAs per channel write
+partials summed by the reduce kernel); for the CUDA-core kernel both loaders
+(TMA tiles at L % 4 == 0, 1-D bulk copies otherwise), channel blocks with a
+ragged last block (H > 256), several batches per tile, ragged batch tiles; the
+three dK modes; and shapes that fall back to pt_dx + pt_dk.
 """
 from __future__ import annotations
 
@@ -41,7 +43,7 @@ def _sm_count(dev) -> int:
     return torch.cuda.get_device_properties(dev).multi_processor_count
 
 
-def _expect_fused(B, H, L, K, sm) -> bool:
+def _expect_tensor_fused(B, H, L, K, sm) -> bool:
     """The host rule: 32 < L <= 48 with L % 4 == 0, any K <= 48, and a grid of
     whole channels (a multiple of H) that keeps at least 3/4 of min(tiles, SMs) busy."""
     if not _fusable_layout(L, K):
@@ -49,6 +51,14 @@ def _expect_fused(B, H, L, K, sm) -> bool:
     gmax = min(-(-B // 128) * H, sm)
     G = (gmax // H) * H
     return G >= 1 and 4 * G >= 3 * gmax
+
+
+def _expect_kind(B, H, L, K, sm) -> str:
+    """Tensor-core fused where it applies, else the CUDA-core fused kernel where a
+    specialised CUDA-core kernel exists for (L, K) with its loader, else separate."""
+    if _expect_tensor_fused(B, H, L, K, sm):
+        return "tensor_fused"
+    return "ffma_fused" if ops.config("bwd_weight", B, H, L, K)["specialised"] else "separate"
 
 
 def _run(dy, x, k, mode="deterministic", accumulate=False, gk=None):
@@ -90,21 +100,76 @@ SHAPES = [
 def test_fused_backward_against_fp64_oracle(cuda_device, B, H, L, K, mode):
     dev = cuda_device
     if _sm_count(dev) >= 128:
-        assert ops.fused_backward(B, H, L, K) == _expect_fused(B, H, L, K, _sm_count(dev))
+        assert ops.backward_kind(B, H, L, K) == _expect_kind(B, H, L, K, _sm_count(dev))
     x, k, dy, cpu = _inputs(B, H, L, K, 1717, dev)
     gx, gk = _run(dy, x, k, mode=mode)
     np.testing.assert_allclose(gx.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
     assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
 
 
-@pytest.mark.parametrize("B,H,L,K", [(300, 96, 48, 48), (200, 8, 42, 40), (100, 5, 28, 5), (64, 300, 48, 48)])
+@pytest.mark.parametrize("B,H,L,K", [(200, 8, 42, 40), (100, 5, 28, 5), (40, 63, 37, 13)])
 def test_unfused_shapes_fall_back_to_separate_kernels(cuda_device, B, H, L, K):
+    """No specialised CUDA-core kernel for (L, K), or odd L with H*L % 4 != 0:
+    dX then dK."""
     dev = cuda_device
-    assert not ops.fused_backward(B, H, L, K) or _sm_count(dev) < 128
+    assert ops.backward_kind(B, H, L, K) == "separate"
     x, k, dy, cpu = _inputs(B, H, L, K, 99, dev)
     gx, gk = _run(dy, x, k)
     np.testing.assert_allclose(gx.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
     assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+
+
+FFMA_FUSED_SHAPES = [
+    (300, 96, 48, 48),    # TMA tiles; H = 96 leaves no whole-channel tensor-core grid
+    (64, 300, 48, 48),    # H > 256: channel blocks, ragged last block
+    (513, 64, 37, 13),    # 1-D bulk tiles (odd L), an edge shape's (L, K)
+    (77, 512, 33, 33),    # bulk tiles, channel blocks
+    (1000, 256, 16, 4),   # an edge shape's (L, K): several batches per tile
+    (130, 20, 40, 40),    # TMA tiles, many batches per tile, ragged last tile
+    (257, 64, 31, 16),    # odd L, bulk tiles
+    (999, 128, 24, 24),
+    (700, 40, 32, 32),
+    (5, 4, 16, 8),        # fewer rows than one tile
+]
+
+
+@pytest.mark.parametrize("mode", ["deterministic", "atomic"])
+@pytest.mark.parametrize("B,H,L,K", FFMA_FUSED_SHAPES)
+def test_ffma_fused_backward_against_fp64_oracle(cuda_device, B, H, L, K, mode):
+    dev = cuda_device
+    if _sm_count(dev) >= 128:
+        assert ops.backward_kind(B, H, L, K) == "ffma_fused"
+    x, k, dy, cpu = _inputs(B, H, L, K, 4242, dev)
+    gx, gk = _run(dy, x, k, mode=mode)
+    np.testing.assert_allclose(gx.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
+    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+
+
+def test_ffma_fused_backward_accumulate_determinism_and_separate_agreement(cuda_device):
+    dev = cuda_device
+    B, H, L, K = 2000, 64, 37, 13
+    assert ops.backward_kind(B, H, L, K) == "ffma_fused"
+    x, k, dy, cpu = _inputs(B, H, L, K, 12, dev)
+    outs = [_run(dy, x, k)[1].clone() for _ in range(3)]
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    ref = c_oracle.dk(cpu[2], cpu[0], K)
+    gk = torch.ones_like(k)
+    gx, gk = _run(dy, x, k, mode="deterministic", accumulate=True, gk=gk)
+    assert_dk_close(gk.cpu().numpy() - 1.0, ref)
+    # Same dX arithmetic as the separate CUDA-core kernel (the same in-range FMAs in
+    # the same order): bit-identical.
+    gx_s = ops.dx(dy, k)
+    torch.cuda.synchronize()
+    assert torch.equal(gx, gx_s)
+
+
+def test_forcing_a_tensor_engine_keeps_the_cuda_core_fusion_off(cuda_device):
+    from pathtile_b200 import _lib
+
+    o = _lib.LaunchOpts.frozen()
+    o.engine[2] = _lib.PT_ENGINE_TENSOR
+    assert ops.backward_kind(300, 96, 48, 48, opts=o) == "separate"
+    assert ops.backward_kind(300, 96, 48, 48) == "ffma_fused"
 
 
 @pytest.mark.parametrize("H", [128, 64])
