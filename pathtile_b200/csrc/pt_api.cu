@@ -643,10 +643,18 @@ size_t dk_ws_bytes(const Plan& p);
 
 // Fused backward on the CUDA cores (bwd_rows_kernel): shapes with a specialised
 // CUDA-core kernel whose loader applies, where the tensor-core fused kernel
-// does not, and where neither dX nor dK is forced onto the tensor cores.
+// does not, and where neither dX nor dK is forced onto the tensor cores.  A
+// heavy shape (>= 24 in-range FMAs per output) whose separate dX would run on
+// the tensor cores stays separate: one thread doing both FMA nests of a row is
+// FMA-bound there (measured at B = 16384, H = 96, L = K = 48: 0.348 ms fused on
+// the CUDA cores against 0.253 ms for tensor-core dX + CUDA-core dK), while on
+// light and medium shapes the saved [B, H, L] stream wins (9-31 % on the edge
+// and tuning shapes).
 bool plan_bwd_rows(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   const Opts& o = opts();
   if (o.engine[PT_PATH_DX] == PT_ENGINE_TENSOR || o.engine[PT_PATH_DK] == PT_ENGINE_TENSOR) return false;
+  if (intensity_class(L, K) == 2 && engine_for(PT_PATH_DX, B, H, L, K, di.sm_count) == PT_ENGINE_TENSOR)
+    return false;
   const pt::Entry* e = find_entry(L, K);
   if (!e) return false;
   if (!((e->loader == pt::LOAD_TMA3D && g_encode != nullptr) ||

@@ -58,7 +58,11 @@ def _expect_kind(B, H, L, K, sm) -> str:
     specialised CUDA-core kernel exists for (L, K) with its loader, else separate."""
     if _expect_tensor_fused(B, H, L, K, sm):
         return "tensor_fused"
-    return "ffma_fused" if ops.config("bwd_weight", B, H, L, K)["specialised"] else "separate"
+    if not ops.config("bwd_weight", B, H, L, K)["specialised"]:
+        return "separate"
+    dx = ops.config("bwd_input", B, H, L, K)
+    # Heavy shapes whose separate dX runs on the tensor cores stay separate.
+    return "separate" if dx["engine"] == "tensor" and dx["intensity_class"] == "heavy" else "ffma_fused"
 
 
 def _run(dy, x, k, mode="deterministic", accumulate=False, gk=None):
@@ -107,10 +111,11 @@ def test_fused_backward_against_fp64_oracle(cuda_device, B, H, L, K, mode):
     assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
 
 
-@pytest.mark.parametrize("B,H,L,K", [(200, 8, 42, 40), (100, 5, 28, 5), (40, 63, 37, 13)])
+@pytest.mark.parametrize("B,H,L,K", [(200, 8, 42, 40), (100, 5, 28, 5), (40, 63, 37, 13), (300, 96, 48, 48)])
 def test_unfused_shapes_fall_back_to_separate_kernels(cuda_device, B, H, L, K):
-    """No specialised CUDA-core kernel for (L, K), or odd L with H*L % 4 != 0:
-    dX then dK."""
+    """No specialised CUDA-core kernel for (L, K), odd L with H*L % 4 != 0, or a
+    heavy shape whose dX runs on the tensor cores (no whole-channel grid for the
+    tensor-core fused kernel at H = 96): dX then dK."""
     dev = cuda_device
     assert ops.backward_kind(B, H, L, K) == "separate"
     x, k, dy, cpu = _inputs(B, H, L, K, 99, dev)
@@ -120,12 +125,12 @@ def test_unfused_shapes_fall_back_to_separate_kernels(cuda_device, B, H, L, K):
 
 
 FFMA_FUSED_SHAPES = [
-    (300, 96, 48, 48),    # TMA tiles; H = 96 leaves no whole-channel tensor-core grid
+    (300, 96, 48, 24),    # TMA tiles; H = 96 leaves no whole-channel tensor-core grid
     (64, 300, 48, 48),    # H > 256: channel blocks, ragged last block
     (513, 64, 37, 13),    # 1-D bulk tiles (odd L), an edge shape's (L, K)
     (77, 512, 33, 33),    # bulk tiles, channel blocks
     (1000, 256, 16, 4),   # an edge shape's (L, K): several batches per tile
-    (130, 20, 40, 40),    # TMA tiles, many batches per tile, ragged last tile
+    (130, 20, 32, 32),    # TMA tiles, many batches per tile, ragged last tile
     (257, 64, 31, 16),    # odd L, bulk tiles
     (999, 128, 24, 24),
     (700, 40, 32, 32),
@@ -168,8 +173,8 @@ def test_forcing_a_tensor_engine_keeps_the_cuda_core_fusion_off(cuda_device):
 
     o = _lib.LaunchOpts.frozen()
     o.engine[2] = _lib.PT_ENGINE_TENSOR
-    assert ops.backward_kind(300, 96, 48, 48, opts=o) == "separate"
-    assert ops.backward_kind(300, 96, 48, 48) == "ffma_fused"
+    assert ops.backward_kind(300, 96, 48, 24, opts=o) == "separate"
+    assert ops.backward_kind(300, 96, 48, 24) == "ffma_fused"
 
 
 @pytest.mark.parametrize("H", [128, 64])
