@@ -41,6 +41,7 @@ struct DeviceInfo {
   int max_smem = 0;  // opt-in dynamic shared memory per block
   unsigned* err = nullptr;
   std::unordered_map<const void*, size_t> smem_attr;  // max dynamic smem already granted
+  std::unordered_map<const void*, int> regs;          // registers per thread of a function
 };
 
 std::mutex g_mu;
@@ -580,6 +581,19 @@ bool plan_fused(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   const int G = (gmax / H) * H;
   if (G < 1 || 4LL * G < 3LL * gmax) return false;
   if (ensure_smem_attr(di, func, pt::tc::bwd_smem()) != PT_OK) return false;
+  // The kernel's register split (setmaxnreg) draws on the registers the CTA is
+  // launched with: launch it only with the per-thread count the split assumes.
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = di.regs.find(func);
+    if (it == di.regs.end()) {
+      cudaFuncAttributes fa;
+      const int regs = (cudaFuncGetAttributes(&fa, func) == cudaSuccess) ? fa.numRegs : 0;
+      (void)cudaGetLastError();
+      it = di.regs.emplace(func, regs).first;
+    }
+    if (it->second != pt::tc::kBwdLaunchRegs) return false;
+  }
   pt::TileGeom& g = p.g;
   g.B = B;
   g.H = H;
@@ -592,7 +606,7 @@ bool plan_fused(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   g.nhb = H;
   p.func = func;
   p.smem = pt::tc::bwd_smem();
-  p.threads = pt::tc::kThreads;
+  p.threads = pt::tc::kBwdThreads;
   p.exact = true;
   p.tensor = true;
   p.period = 1;

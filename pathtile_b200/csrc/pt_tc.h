@@ -56,7 +56,11 @@ namespace pt {
 namespace tc {
 
 // Fused backward (dX on the tensor cores + dK on the CUDA cores) for any K <= 48
-// and rows of 32 < L <= 48 columns with L % 4 == 0; nullptr otherwise.
+// and rows of 32 < L <= 48 columns with L % 4 == 0; nullptr otherwise.  It runs
+// 512 threads and rebalances registers between its warpgroups (setmaxnreg),
+// which needs the function to start with kBwdLaunchRegs registers per thread.
+constexpr int kBwdThreads = 512;
+constexpr int kBwdLaunchRegs = 128;
 const void* bwd_func(int L, int K);
 // The fused kernel's instantiations, one per K (pt_tc_bwd_k1.cu, pt_tc_bwd_k2.cu).
 const void* bwd_kernel_k1_24(int K);

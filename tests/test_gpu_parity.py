@@ -300,13 +300,25 @@ def test_legacy_warp_tiled_surface(cuda_device):
         warp_tiled.depthwise_conv_shared(x, k[:64])
 
 
-def test_specialised_kernels_have_no_spills(cuda_device):
+def test_default_path_kernels_have_no_spills(cuda_device):
+    """Every kernel the frozen table launches at the BASELINE shapes -- the
+    tensor-core FWD / dX kernels where they apply, the CUDA-core kernels, and the
+    fused backward of dx_dk -- keeps its working set in registers."""
     for B, H, L, K in FULL_SHAPES:
         for path in ("fwd", "bwd_input", "bwd_weight"):
             info = ops.kernel_info(path, B, H, L, K)
             assert info["specialised"] == 1
-            assert info["local_memory_bytes"] == 0
+            assert info["local_memory_bytes"] == 0, (path, B, H, L, K, info)
             assert info["resident_blocks_per_sm"] >= 1
+        assert ops.fused_backward(B, H, L, K)
+        info = ops.kernel_info("bwd_fused", B, H, L, K)
+        assert info["local_memory_bytes"] == 0, ("bwd_fused", B, H, L, K, info)
+        assert info["resident_blocks_per_sm"] >= 1
+    # Every K of the tensor-core fused kernel (its register split is per K).
+    for K in range(1, 49):
+        info = ops.kernel_info("bwd_fused", 16384, 128, 48, K)
+        assert info["threads_per_block"] == 512 and info["regs_per_thread"] == 128, (K, info)
+        assert info["local_memory_bytes"] == 0, (K, info)
 
 
 def test_reference_kernels_agree_when_built(cuda_device):
