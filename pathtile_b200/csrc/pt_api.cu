@@ -263,6 +263,7 @@ struct Plan {
   pt::TileGeom g{};
   int threads = 0;
   size_t smem = 0;
+  pt::tc::BwdSched sched{};  // fused backward: work schedule
 };
 
 // Row pitch (floats) for TMA3D tiles: 128-bit LDS by 8 consecutive rows hits
@@ -565,24 +566,70 @@ int launch_tensor_dk(const Plan& p, const float* dy, const float* x, float* dk, 
   return PT_OK;
 }
 
+// Work schedule of the tensor-core fused backward on `sms` SMs (pt::tc::BwdSched):
+// kp = floor(min(tiles, sms) / H) primary CTAs per channel; the E = sms - kp*H
+// SMs left over become helpers that take every channel's tail blocks when that
+// shortens the busiest CTA by at least 3 % (a helper's channel switch counted
+// as one tile; P chosen to balance primaries and helpers) and no helper owns
+// more than kMaxHelperChannels channels.  Otherwise the plain grid of kp*H
+// CTAs, which must keep at least 3/4 of min(tiles, SMs) busy.  A channel switch
+// drains the helper's MMA pipeline while the Toeplitz operand is rebuilt (the
+// shared memory holds one), so many switches cost more than the extra SMs
+// give: measured at B = 16384, L = K = 48, helpers made H = 64 (4 channels per
+// helper) 7 % faster and H = 96 (2 per helper; no plain grid) 24 % faster than
+// the separate kernels, but H = 128 (7 per helper) 6 % slower than the plain
+// grid, and 11 % slower at K = 3.
+// Returns the grid size, or 0 where the kernel does not apply.
+constexpr int kMaxHelperChannels = 4;
+
+int fused_schedule(int B, int H, int sms, pt::tc::BwdSched& sc) {
+  const int nblk = (B + pt::tc::kRowsPerTile - 1) / pt::tc::kRowsPerTile;
+  const long long tiles = static_cast<long long>(nblk) * H;
+  const int gmax = static_cast<int>(tiles < sms ? tiles : sms);
+  const int kp = gmax / H;
+  if (kp < 1) return 0;
+  const int plain = (nblk + kp - 1) / kp;  // tiles of the busiest CTA in the plain grid
+  const int E = sms - kp * H;
+  int best_cost = plain, best_p = 0;
+  if (E >= 1 && nblk >= 2 && (H + E - 1) / E <= kMaxHelperChannels) {
+    const int m = (H + E - 1) / E;
+    for (int P = 1; P < nblk; ++P) {
+      const int prim = (P + kp - 1) / kp;
+      const int help = m * (nblk - P) + (m - 1);
+      const int cost = prim > help ? prim : help;
+      if (cost < best_cost) {
+        best_cost = cost;
+        best_p = P;
+      }
+    }
+    if (best_p > 0 && 100LL * best_cost <= 97LL * plain) {
+      sc = pt::tc::BwdSched{H, nblk, kp, best_p, E, m, 0};
+      return sms;
+    }
+  }
+  const int G = kp * H;
+  if (4LL * G < 3LL * gmax) return 0;
+  sc = pt::tc::BwdSched{H, nblk, kp, nblk, 0, 0, kp == 1 ? 1 : 0};
+  return G;
+}
+
 // Fused backward (dX on the tensor cores, dK on the CUDA cores, one pass over dy
 // and x): rows of 32 < L <= 48 columns with L % 4 == 0 and any K <= 48 (the
-// kernel's 48-column layout), dX not forced onto the CUDA cores, and a grid in
-// which every CTA keeps one channel (a multiple of H that keeps >= 3/4 of the
-// SMs busy).  G == H makes each CTA's partial its channel's dK.
+// kernel's 48-column layout), dX not forced onto the CUDA cores, and a schedule
+// from fused_schedule.
 bool plan_fused(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   const void* func = pt::tc::bwd_func(L, K);
   if (!func || g_encode == nullptr) return false;
   const int dx_engine = opts().engine[PT_PATH_DX];
   if (dx_engine >= 0 && dx_engine != PT_ENGINE_TENSOR) return false;
   if (static_cast<long long>(pt::tc::bwd_smem()) > di.max_smem) return false;
-  const long long tiles = tensor_tiles(PT_PATH_DX, B, H);
-  const int gmax = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);
-  const int G = (gmax / H) * H;
-  if (G < 1 || 4LL * G < 3LL * gmax) return false;
+  pt::tc::BwdSched sc{};
+  const int G = fused_schedule(B, H, di.sm_count, sc);
+  if (G < 1) return false;
   if (ensure_smem_attr(di, func, pt::tc::bwd_smem()) != PT_OK) return false;
-  // The kernel's register split (setmaxnreg) draws on the registers the CTA is
-  // launched with: launch it only with the per-thread count the split assumes.
+  // The kernel rebalances registers between its warpgroups (setmaxnreg), which
+  // draws on the registers the CTA is launched with: launch it only with the
+  // per-thread count its split assumes.
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = di.regs.find(func);
@@ -599,29 +646,29 @@ bool plan_fused(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   g.H = H;
   g.L = L;
   g.K = K;
-  g.Q = static_cast<int>(tiles);
+  g.Q = sc.nblk * H;
   g.G = G;
   g.Th = 1;
   g.Tb = pt::tc::kRowsPerTile;
   g.nhb = H;
   p.func = func;
   p.smem = pt::tc::bwd_smem();
-  p.threads = pt::tc::kBwdThreads;
+  p.threads = pt::tc::bwd_threads();
   p.exact = true;
   p.tensor = true;
   p.period = 1;
   p.groups = H;
   p.lay = pt::tc::layout_for(L);
+  p.sched = sc;
   return true;
 }
 
-// Workspace of the fused backward: none when each channel has one CTA, else the
-// tensor-core dK layout (2 slots per CTA, one used, Hc = 1).
+// Workspace of the fused backward: none in direct mode, else [slots][4][K] partials.
 size_t fused_ws_bytes(const Plan& p) {
-  if (p.g.G == p.g.H) return 0;
-  const size_t slots = static_cast<size_t>(p.g.G) * pt::tc::kDkMaxGroups;
-  const size_t part = (slots * p.g.K * sizeof(float) + 255) / 256 * 256;
-  return part + slots * sizeof(int);
+  const pt::tc::BwdSched& sc = p.sched;
+  if (sc.direct) return 0;
+  const size_t slots = static_cast<size_t>(sc.kp) * sc.H + static_cast<size_t>(sc.E) * sc.m;
+  return (slots * 4 * p.g.K * sizeof(float) + 255) / 256 * 256;
 }
 
 int launch_fused(const Plan& p, const float* dy, const float* x, const float* k, float* dx, float* dk,
@@ -635,19 +682,16 @@ int launch_fused(const Plan& p, const float* dy, const float* x, const float* k,
   if ((rc = encode_tc_tmap(&x64, x, g.B, g.H, g.L, 16, false)) != PT_OK) return rc;
   if ((rc = encode_tc_tmap(&dx128, dx, g.B, g.H, g.L, 32, false)) != PT_OK) return rc;
   if ((rc = encode_tc_tmap(&dx64, dx, g.B, g.H, g.L, 16, false)) != PT_OK) return rc;
-  int direct = (g.G == g.H) ? 1 : 0;
+  pt::tc::BwdSched sc = p.sched;
   int accumulate = (mode == PT_DK_DETERMINISTIC) ? 0 : 1;  // atomic and *_ACCUMULATE add to dk
-  float* out = direct ? dk : static_cast<float*>(ws);
-  const size_t slots = static_cast<size_t>(g.G) * pt::tc::kDkMaxGroups;
-  const size_t part_bytes = (slots * g.K * sizeof(float) + 255) / 256 * 256;
-  int* group_of = direct ? nullptr : reinterpret_cast<int*>(static_cast<unsigned char*>(ws) + part_bytes);
-  int H = g.H, n_tiles = g.Q, acc_k = direct ? accumulate : 0;
-  void* args[] = {&dy128, &dy64, &x128, &x64, &dx128, &dx64, const_cast<float**>(&k), &out, &group_of,
-                  &H, &n_tiles, &direct, &acc_k, &err};
+  float* part = sc.direct ? nullptr : static_cast<float*>(ws);
+  int acc_k = sc.direct ? accumulate : 0;
+  void* args[] = {&dy128, &dy64, &x128, &x64, &dx128, &dx64, const_cast<float**>(&k), &part, &dk,
+                  &sc, &acc_k, &err};
   cudaError_t ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
   if (ce != cudaSuccess) return cuda_fail(ce);
-  if (!direct) {
-    pt::tc::dk_reduce(out, group_of, static_cast<int>(slots), H, g.K, 1, dk, accumulate, stream);
+  if (!sc.direct) {
+    pt::tc::bwd_dk_reduce(part, dk, sc, g.K, accumulate, stream);
     if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_fail(ce);
   }
   return PT_OK;

@@ -56,11 +56,26 @@ namespace pt {
 namespace tc {
 
 // Fused backward (dX on the tensor cores + dK on the CUDA cores) for any K <= 48
-// and rows of 32 < L <= 48 columns with L % 4 == 0; nullptr otherwise.  It runs
-// 512 threads and rebalances registers between its warpgroups (setmaxnreg),
-// which needs the function to start with kBwdLaunchRegs registers per thread.
-constexpr int kBwdThreads = 512;
+// and rows of 32 < L <= 48 columns with L % 4 == 0; nullptr otherwise.  The
+// host launches it only where the compiled function starts with
+// kBwdLaunchRegs registers per thread.
 constexpr int kBwdLaunchRegs = 128;
+int bwd_threads();
+
+// Work schedule of the fused backward: nblk = ceil(B / 128) batch blocks per
+// channel; CTAs g < kp*H are primaries (channel g % H, blocks g / H + i*kp
+// below P); the E CTAs after them are helpers (helper e: channels e, e + E, ...,
+// each over the tail blocks [P, nblk)); m = ceil(H / E), the most channels a
+// helper owns; direct = 1 when each channel has exactly one CTA and no helper
+// (the kernel then writes dK itself).  The workspace holds [slots][4][K] floats,
+// slots = kp*H + E*m.
+struct BwdSched {
+  int H, nblk, kp, P, E, m;
+  int direct;
+};
+
+// dk (=, or += when accumulate) the sum of each channel's partials in a fixed order.
+void bwd_dk_reduce(const float* part, float* dk, const BwdSched& sc, int K, int accumulate, void* stream);
 const void* bwd_func(int L, int K);
 // The fused kernel's instantiations, one per K (pt_tc_bwd_k1.cu, pt_tc_bwd_k2.cu).
 const void* bwd_kernel_k1_24(int K);

@@ -5,54 +5,69 @@
 // streams.  Here one kernel reads dy and x once and writes dx (three streams),
 // and the two halves of the work use different pipes: the dX product runs as
 // in tc_conv_kernel<DX> (3xTF32 split, Toeplitz operand resident in shared
-// memory), while row threads split dy for it and accumulate the filter
-// gradient of their rows with packed FFMAs.
+// memory), while the row threads that split dy for it also accumulate the
+// filter gradient of their row with packed FFMAs.
 //
-// Tiles are 128 batch rows of one channel; CTAs are dealt tiles round-robin
-// and the host uses this kernel only where every CTA keeps a single channel
-// (a grid that is a multiple of H), so each thread's dK accumulators belong to
-// one channel for the whole kernel.  At the end the CTA sums its threads'
-// accumulators in a fixed order and writes one partial per (CTA, tap): with
-// one CTA per channel that partial is the channel's dK.
+// Work: tiles of 128 batch rows of one channel.  A CTA keeps the channel's
+// Toeplitz operand and its threads' dK accumulators, so it wants one channel
+// for as long as possible; the SMs, not the channels, set the grid.  The host
+// chooses a schedule (BwdSched):
+//   * primaries: kp CTAs per channel (CTA g < kp*H has channel g % H and
+//     takes batch blocks r, r + kp, r + 2 kp, ... below P, r = g / H);
+//   * helpers: the E = G - kp*H remaining CTAs take the tail blocks [P, nblk)
+//     of every channel: helper e owns channels e, e + E, e + 2E, ... and does
+//     their tail blocks one channel after the other, so at any time the
+//     helpers read one batch block of E adjacent channels (contiguous in HBM)
+//     while the primaries read the blocks below P of all channels.
+// P balances the two (the host counts a channel switch as one tile), so every
+// SM has work: at B = 16384, H = 128 on 148 SMs the longest CTA does 113
+// tiles instead of 128.  Without helpers (E = 0) the schedule is the
+// round-robin one-channel-per-CTA grid.
+//
+// dK: each CTA accumulates per channel "segment" (a primary has one; a helper
+// one per channel it owns) and, at the segment's end, reduces its threads'
+// sums in a fixed order -- a warp shuffle over the 32 rows of each TMEM lane
+// quadrant, one partial per (quadrant, tap) -- and writes them to the
+// workspace; bwd_dk_reduce_kernel then sums each channel's partials in a fixed
+// order (deterministic).  With one CTA per channel and no helpers ("direct"),
+// the CTA sums its four quadrants itself and writes dK.
 //
 // Roles (512 threads = four warpgroups, one CTA per SM):
-//   warpgroup 0  warp 0: TMA producer (dy ring of 4 tiles, x ring of 3);
-//                warp 1: allocates 512 TMEM columns, lane 0 issues the dX MMAs;
-//                warps 2-3: no role after the set-up
-//   warpgroups 1, 2  row workers, one thread per tile row; warpgroup 1 takes
-//                the CTA's even tiles and warpgroup 2 the odd ones, so while
-//                one group writes dy's sub-tf32 remainder (A of dX) into
-//                tensor memory and loads its x rows, the other runs its FMA
-//                nest on the same SM sub-partitions; each thread accumulates
-//                every tap of its rows
-//   warpgroup 3  dX epilogue: TMEM -> staging -> TMA store
-// The row workers need about 170 registers (every tap's accumulator and the
-// x row as packed pairs); the others need few, so after the set-up the CTA's
-// 512 x 128 registers are rebalanced with setmaxnreg (warpgroup 0: 56, row
-// workers: 184, epilogue: 88; none of the three regions spills).  The host
-// launches the kernel only where the compiled function starts with 128
-// registers per thread, the split's budget.
-// Every wait is bounded; on expiry the kernel records a bit in the device
-// error word, drains its own copies and MMAs, frees its tensor memory and
-// returns without writing dK.
+//   warp 0       TMA producer: ring of 3 stages, each the dy and x tiles
+//   warp 1       allocates 512 TMEM columns; lane 0 issues the dX MMAs
+//   warps 2-3    no role after the set-up
+//   warps 4-11   row workers, two per tile row: split half of the dy row into
+//                TMEM (A of dX), then dK for the even or odd taps over the
+//                whole row, streaming dy from shared memory four columns at a
+//                time against the x row in registers; release the stage; at a
+//                channel switch, flush dK and rebuild the Toeplitz operand
+//   warps 12-15  dX epilogue: TMEM -> staging -> TMA store
+// After the set-up the CTA's 512 x 128 registers are rebalanced with
+// setmaxnreg (warpgroup 0: 72, row workers: 168, epilogue: 104; no region
+// spills).  The host launches the kernel only where the compiled function
+// starts with 128 registers per thread, the split's budget.  Every wait is
+// bounded; on expiry the kernel records a bit in the device error word, drains
+// its own copies and MMAs, frees its tensor memory and returns; dK is then
+// undefined.
 #pragma once
 
+#include "pt_tc.h"
 #include "pt_tc_kernels.cuh"
 
 namespace pt {
 namespace tc {
 
+constexpr int BWD_STAGES = 3;
 constexpr int BWD_L = 48;
-constexpr int BWD_DY_SLOTS = 4;   // dy ring: read by the row workers and, as A_hi, by the MMAs
-constexpr int BWD_X_SLOTS = 3;    // x ring: read once per tile by the row workers
 constexpr int BWD_THREADS = 512;
-constexpr int BWD_ROW0 = 128;     // first row-worker thread (warp 4)
-constexpr int BWD_ROWS = 256;     // row workers: two groups of 128
-constexpr int BWD_EPI0 = 384;     // first epilogue thread (warp 12)
+constexpr int BWD_LAUNCH_THREADS = BWD_THREADS;
 constexpr int BWD_LAUNCH_REGS = 128;  // registers per thread at launch (65,536 / 512)
-constexpr int BWD_REG_CTRL = 56;
-constexpr int BWD_REG_ROWS = 184;
-constexpr int BWD_REG_EPI = 88;
+constexpr int BWD_ROW0 = 128;         // first row-worker thread (warp 4)
+constexpr int BWD_ROWS = 256;         // row workers
+constexpr int BWD_EPI0 = 384;         // first epilogue thread (warp 12)
+constexpr int BWD_REG_CTRL = 72;
+constexpr int BWD_REG_ROWS = 168;
+constexpr int BWD_REG_EPI = 104;
 static_assert(128 * BWD_REG_CTRL + BWD_ROWS * BWD_REG_ROWS + 128 * BWD_REG_EPI <= BWD_THREADS * BWD_LAUNCH_REGS,
               "the register split must fit the registers the CTA is launched with");
 
@@ -60,19 +75,46 @@ struct BwdGeo {
   using GG = Geo<3>;                                  // 48-column tiles: 128-B + 64-B boxes
   static constexpr int N = GG::N;                     // 48
   static constexpr int TILE = GG::TILE;               // 24 KB
-  static constexpr int OFF_DY = 0;
-  static constexpr int OFF_X = OFF_DY + BWD_DY_SLOTS * TILE;
-  static constexpr int OFF_OUT = OFF_X + BWD_X_SLOTS * TILE;  // one staging tile for the dx store
-  static constexpr int OFF_B = OFF_OUT + TILE;
+  static constexpr int STAGE = 2 * TILE;              // dy | x
+  static constexpr int OFF_OUT = BWD_STAGES * STAGE;
+  static constexpr int OFF_B = OFF_OUT + OUT_SLOTS * TILE;
   static constexpr int OFF_BAR = OFF_B + GG::BMAT;    // one resident Toeplitz operand
-  // fullD, dfree, mfree per dy slot; fullX, xfree per x slot; aready, adone per A
-  // slot; mdone, accfree per accumulator.
-  static constexpr int N_BARS = 3 * BWD_DY_SLOTS + 2 * BWD_X_SLOTS + 2 * A_SLOTS + 2 * ACC_SLOTS;
-  static constexpr int OFF_TMEM = OFF_BAR + N_BARS * 8;
+  // full, sfree, mfree per stage; aready, adone per A slot; mdone, accfree per
+  // accumulator; tready (the Toeplitz operand of a new channel is built).
+  static constexpr int N_BARS = 3 * BWD_STAGES + 2 * A_SLOTS + 2 * ACC_SLOTS + 1;
+  static constexpr int OFF_RED = OFF_BAR + N_BARS * 8;  // [4 quadrants][48] direct-mode dK sums
+  static constexpr int OFF_TMEM = OFF_RED + 4 * BWD_L * 4;
   static constexpr int SMEM = OFF_TMEM + 16 + 1024;
-  static_assert(TILE % 1024 == 0 && OFF_B % 1024 == 0, "swizzled buffers start on 1024-byte boundaries");
-  static_assert(BWD_L * BWD_ROWS * 4 <= BWD_DY_SLOTS * TILE, "dK reduction scratch fits the idle dy ring");
+  static_assert(STAGE % 1024 == 0 && OFF_B % 1024 == 0, "swizzled buffers start on 1024-byte boundaries");
 };
+
+struct BwdTile {
+  int ch, blk, seg;
+};
+
+__device__ __forceinline__ int bwd_n_tiles(const BwdSched& sc, int g) {
+  if (g < sc.kp * sc.H) {
+    const int r = g / sc.H;
+    return r < sc.P ? (sc.P - r + sc.kp - 1) / sc.kp : 0;
+  }
+  const int e = g - sc.kp * sc.H;
+  const int nch = (sc.H - e + sc.E - 1) / sc.E;
+  return nch * (sc.nblk - sc.P);
+}
+
+__device__ __forceinline__ BwdTile bwd_tile(const BwdSched& sc, int g, int i) {
+  if (g < sc.kp * sc.H) return BwdTile{g % sc.H, g / sc.H + i * sc.kp, 0};
+  const int e = g - sc.kp * sc.H;
+  const int tp = sc.nblk - sc.P;
+  const int seg = i / tp;
+  return BwdTile{e + seg * sc.E, sc.P + (i - seg * tp), seg};
+}
+
+// Workspace slot of (CTA g, segment seg): primaries g, helpers kp*H + e*m + seg;
+// a slot holds [4 quadrants][K] partial sums.
+__device__ __forceinline__ int bwd_slot(const BwdSched& sc, int g, int seg) {
+  return g < sc.kp * sc.H ? g : sc.kp * sc.H + (g - sc.kp * sc.H) * sc.m + seg;
+}
 
 // D (+)= A B with A read from shared memory through a descriptor (tf32 operands).
 __device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
@@ -85,6 +127,93 @@ __device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a, uint64_
       : "memory");
 }
 
+// dy - (dy with its low 13 mantissa bits cleared): the part of dy a tf32 MMA,
+// which ignores those bits, does not see.  Exact in fp32.
+__device__ __forceinline__ float bwd_tf32_rest(float v) {
+  return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+}
+
+// Filter-gradient share of one row worker.  The two workers of a tile row take
+// the even (half 0) and odd (half 1) taps, j = 2 jj + half, over the whole row:
+//   acc[jj] += sum_t dy[t] x[t + 2 jj + half - PAD].
+// With X[m + 1] = x[m + half] (X = [0, x0 .. x47] for half 0 and
+// [x0 .. x47, 0] for half 1) both halves run one instruction stream,
+//   acc[jj] += dy[t] X[t + 2 jj - PAD + 1],   t + 2 jj - PAD in [-1, 48),
+// so the two warps that share an SM sub-partition share its instruction cache
+// (separate nests per half thrashed it).  dy arrives four columns at a time as
+// 16-byte chunks of the swizzled row: one conflict-free LDS.128 per chunk.
+template <int K>
+struct BwdSplit {
+  static constexpr int NJ = (K + 1) / 2;  // taps per row worker
+};
+
+// Packed FP32 pairs: fma.rn.f32x2 does two FMAs in one issue slot (same FMA
+// pipe throughput as two FFMAs, half the instructions).
+__device__ __forceinline__ uint64_t bwd_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float bwd_pair_sum(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+__device__ __forceinline__ uint64_t bwd_ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// The same sum with even and odd t accumulated apart, two taps-by-column
+// products per instruction:
+//   (accE, accO)[jj] += (dy[t], dy[t+1]) * (X[k], X[k+1]),  t even,
+//   k = t + 2 jj - PAD + 1,
+// whose parity is fixed by K, so the X pairs are packed once per tile (XP) and
+// the dy pairs are the halves of each 16-byte chunk.  X outside [0, 49) is 0.
+template <int K>
+struct BwdPairs {
+  static constexpr int PAD = K / 2;
+  static constexpr int NJ = BwdSplit<K>::NJ;
+  static constexpr int KB = ((1 - PAD) % 2 + 2) % 2;  // parity of every k
+  // first k >= max(1 - PAD, -1) with parity KB
+  static constexpr int K0 = ((1 - PAD) >= -1) ? (1 - PAD) : ((-1 - KB) % 2 == 0 ? -1 : 0);
+  static constexpr int KMAX0 = 46 + 2 * (NJ - 1) - PAD + 1;
+  static constexpr int K1 = KMAX0 < 48 ? KMAX0 : (48 - ((48 - KB) % 2 != 0));
+  static constexpr int NQ = (K1 - K0) / 2 + 1;  // packed X pairs
+};
+
+template <int K>
+__device__ __forceinline__ void bwd_dk_row2(const unsigned char* dyrow128, const unsigned char* dyrow64,
+                                            uint32_t xm128, uint32_t xm64,
+                                            const uint64_t (&XP)[BwdPairs<K>::NQ],
+                                            uint64_t (&acc)[BwdSplit<K>::NJ]) {
+  using P = BwdPairs<K>;
+  constexpr int NJ = P::NJ;
+#pragma unroll
+  for (int c = 0; c < BWD_L / 4; ++c) {
+    bool any = false;
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) {
+        const int k = 4 * c + 2 * u + 2 * jj - P::PAD + 1;
+        any = any || (k >= P::K0 && k <= P::K1);
+      }
+    if (!any) continue;
+    const ulonglong2 q = (c < 8) ? *reinterpret_cast<const ulonglong2*>(dyrow128 + ((16u * c) ^ xm128))
+                                 : *reinterpret_cast<const ulonglong2*>(dyrow64 + ((16u * (c - 8)) ^ xm64));
+    const uint64_t d[2] = {q.x, q.y};
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) {
+        const int k = 4 * c + 2 * u + 2 * jj - P::PAD + 1;
+        if (k >= P::K0 && k <= P::K1) acc[jj] = bwd_ffma2(d[u], XP[(k - P::K0) / 2], acc[jj]);
+      }
+  }
+}
+
 template <int N>
 __device__ __forceinline__ void setmaxnreg_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N));
@@ -94,183 +223,92 @@ __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N));
 }
 
-// dy - (dy with its low 13 mantissa bits cleared): the part of dy a tf32 MMA,
-// which ignores those bits, does not see.  Exact in fp32.
-__device__ __forceinline__ float bwd_tf32_rest(float v) {
-  return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
-}
-
-// Packed FP32 pairs: fma.rn.f32x2 does two FMAs in one issue slot (same FMA
-// pipe throughput as two FFMAs, half the instructions).
-__device__ __forceinline__ uint64_t bwd_pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void bwd_unpack(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t bwd_ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-
-// Filter gradient of one row, every tap, taps in pairs:
-//   (acc[2p], acc[2p+1]) += (dy[t], dy[t]) * (x[i], x[i+1]),  i = t + 2p - K/2,
-// with XP[i + 1] = (x[i], x[i + 1]) for i in [-1, 48) (x outside [0, 48) is 0),
-// packed once per tile, and dy[t] broadcast into both halves.  For odd K the
-// last tap (K - 1) has its own scalar accumulator.  dy arrives four columns at
-// a time as 16-byte chunks of the swizzled row (one conflict-free LDS.128).
+// The channel's Toeplitz operand for dX, T[s][t] = k[t - s + K/2], into the
+// operand buffer, by `nthr` threads (thread index `tid`).
 template <int K>
-struct BwdTaps {
-  static constexpr int PAD = K / 2;
-  static constexpr int NP = K / 2;           // full tap pairs
-  static constexpr bool ODD = (K % 2) != 0;  // tap K - 1 on its own
-  static constexpr int NACC = NP > 0 ? NP : 1;
-};
-
-template <int K>
-__device__ __forceinline__ void bwd_dk_row(const unsigned char* dyrow128, const unsigned char* dyrow64,
-                                           uint32_t xm128, uint32_t xm64, const uint64_t (&XP)[BWD_L + 1],
-                                           uint64_t (&acc)[BwdTaps<K>::NACC], float& acc_odd) {
-  using T = BwdTaps<K>;
+__device__ __forceinline__ void bwd_build_toeplitz(unsigned char* bm, const float* __restrict__ taps, int ch,
+                                                   int tid, int nthr) {
+  using GG = Geo<3>;
+  constexpr int N = GG::N;
+  const int pad = K / 2;
+  const float* kh = taps + static_cast<size_t>(ch) * K;
+  constexpr int CPR = N / 4;
+  for (int task = tid; task < N * CPR; task += nthr) {
+    const int c4 = task / N;
+    const int tp = task - c4 * N;
+    const int sp = 4 * c4;
+    float v[4];
 #pragma unroll
-  for (int c = 0; c < BWD_L / 4; ++c) {
-    bool any = false;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-#pragma unroll
-      for (int p = 0; p < T::NP; ++p) {
-        const int i = 4 * c + u + 2 * p - T::PAD;
-        any = any || (i >= -1 && i < BWD_L);
-      }
-      if (T::ODD) {
-        const int i1 = 4 * c + u + (K - 1) - T::PAD;
-        any = any || (i1 >= 0 && i1 < BWD_L);
-      }
+    for (int q = 0; q < 4; ++q) {
+      const int j = tp - (sp + q) + pad;
+      v[q] = (j >= 0 && j < K) ? __ldg(kh + j) : 0.f;
     }
-    if (!any) continue;
-    const float4 q = (c < 8) ? *reinterpret_cast<const float4*>(dyrow128 + ((16u * c) ^ xm128))
-                             : *reinterpret_cast<const float4*>(dyrow64 + ((16u * (c - 8)) ^ xm64));
-    const float d[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = 4 * c + u;
-      const uint64_t d2 = bwd_pack(d[u], d[u]);
-#pragma unroll
-      for (int p = 0; p < T::NP; ++p) {
-        const int i = t + 2 * p - T::PAD;
-        if (i >= -1 && i < BWD_L) acc[p] = bwd_ffma2(d2, XP[i + 1], acc[p]);
-      }
-      if (T::ODD) {
-        const int i1 = t + (K - 1) - T::PAD;
-        if (i1 >= 0 && i1 < BWD_L) {
-          float lo, hi;
-          bwd_unpack(XP[i1 + 1], lo, hi);
-          acc_odd = fmaf(d[u], lo, acc_odd);
-        }
-      }
+    float4 hi, lo;
+    split4(make_float4(v[0], v[1], v[2], v[3]), hi, lo);
+    if (c4 < GG::C128) {
+      *reinterpret_cast<float4*>(bm + sw128_off(tp, c4)) = hi;
+      *reinterpret_cast<float4*>(bm + GG::BLO128 + sw128_off(tp, c4)) = lo;
+    } else {
+      unsigned char* b64 = bm + GG::BBOX64;
+      *reinterpret_cast<float4*>(b64 + sw64_off(tp, c4 - GG::C128)) = hi;
+      *reinterpret_cast<float4*>(b64 + GG::BLO64 + sw64_off(tp, c4 - GG::C128)) = lo;
     }
   }
 }
 
-// n_tiles = ceil(B / 128) * H; tile tau: channel tau % H, rows [128 * (tau / H), +128).
-// Requires gridDim.x % H == 0 (each CTA keeps channel blockIdx.x % H).
-// dk_out: partial[(g * 2) * K + j] with group_of[2g] = channel, group_of[2g + 1] = -1
-// (the tensor-core dK reduce layout), or, if direct != 0, dk[h * K + j] (=, or += when
-// accumulate != 0) -- valid when each channel has exactly one CTA.
+// part: workspace of [slots][4][K] partials (unused when sc.direct); dk: written
+// directly (=, or += when accumulate != 0) when sc.direct.
 template <int K>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tm_dy128, const __grid_constant__ CUtensorMap tm_dy64,
                   const __grid_constant__ CUtensorMap tm_x128, const __grid_constant__ CUtensorMap tm_x64,
                   const __grid_constant__ CUtensorMap tm_dx128, const __grid_constant__ CUtensorMap tm_dx64,
-                  const float* __restrict__ taps, float* __restrict__ dk_out, int* __restrict__ group_of,
-                  int H, int n_tiles, int direct, int accumulate, unsigned* err) {
+                  const float* __restrict__ taps, float* __restrict__ part, float* __restrict__ dk,
+                  const BwdSched sc, int accumulate, unsigned* err) {
   using GG = Geo<3>;
   using BG = BwdGeo;
-  using TP = BwdTaps<K>;
   constexpr int N = GG::N;
   constexpr int L = BWD_L;
+  constexpr int NJ = BwdSplit<K>::NJ;  // accumulators per row worker
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = aligned_smem(smem_raw);
   const uint32_t base = smem_u32(sm);
   const int warp = static_cast<int>(threadIdx.x >> 5);
   const int lane = static_cast<int>(threadIdx.x & 31);
   const uint32_t bar0 = base + BG::OFF_BAR;
-  constexpr int DS = BWD_DY_SLOTS, XS = BWD_X_SLOTS;
-  auto fullD = [&](int s) { return bar0 + 8u * s; };                       // dy tile landed
-  auto dfree = [&](int s) { return bar0 + 8u * (DS + s); };                // row workers done with dy
-  auto mfree = [&](int s) { return bar0 + 8u * (2 * DS + s); };            // dX MMAs done with dy
-  auto fullX = [&](int s) { return bar0 + 8u * (3 * DS + s); };            // x tile landed
-  auto xfree = [&](int s) { return bar0 + 8u * (3 * DS + XS + s); };       // x rows taken
-  constexpr int B2 = 3 * DS + 2 * XS;
-  auto aready = [&](int a) { return bar0 + 8u * (B2 + a); };
-  auto adone = [&](int a) { return bar0 + 8u * (B2 + A_SLOTS + a); };
-  auto mdone = [&](int d) { return bar0 + 8u * (B2 + 2 * A_SLOTS + d); };
-  auto accfree = [&](int d) { return bar0 + 8u * (B2 + 2 * A_SLOTS + ACC_SLOTS + d); };
-  const int G = static_cast<int>(gridDim.x);
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto sfree = [&](int s) { return bar0 + 8u * (BWD_STAGES + s); };
+  auto aready = [&](int a) { return bar0 + 8u * (2 * BWD_STAGES + a); };
+  auto adone = [&](int a) { return bar0 + 8u * (2 * BWD_STAGES + A_SLOTS + a); };
+  auto mdone = [&](int d) { return bar0 + 8u * (2 * BWD_STAGES + 2 * A_SLOTS + d); };
+  auto accfree = [&](int d) { return bar0 + 8u * (2 * BWD_STAGES + 2 * A_SLOTS + ACC_SLOTS + d); };
+  // The dX MMAs of the tile in stage s have completed (they read its dy half).
+  auto mfree = [&](int s) { return bar0 + 8u * (2 * BWD_STAGES + 2 * A_SLOTS + 2 * ACC_SLOTS + s); };
+  const uint32_t tready = bar0 + 8u * (3 * BWD_STAGES + 2 * A_SLOTS + 2 * ACC_SLOTS);
   const int g = static_cast<int>(blockIdx.x);
-  const int h = g % H;  // the CTA's channel (G % H == 0)
-  const int n_it = (g < n_tiles) ? (n_tiles - 1 - g) / G + 1 : 0;
+  const int n_it = bwd_n_tiles(sc, g);
+  const BwdTile first = bwd_tile(sc, g, 0);
 
-  // Partials mode: mark this CTA's slots unused before any bounded wait, so a
-  // CTA that gives up after a timed-out wait adds nothing to the reduce (and no
-  // slot id left in the workspace by an earlier launch is read).
-  if (!direct && threadIdx.x == 0) {
-    group_of[2 * g] = -1;
-    group_of[2 * g + 1] = -1;
-  }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < DS; ++s) {
-      mbar_init(fullD(s), 1);
-      mbar_init(dfree(s), 4);  // the four warps of the group that took the tile
+    for (int s = 0; s < BWD_STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(sfree(s), BWD_ROWS / 32);
       mbar_init(mfree(s), 1);
     }
-    for (int s = 0; s < XS; ++s) {
-      mbar_init(fullX(s), 1);
-      mbar_init(xfree(s), 4);
-    }
     for (int a = 0; a < A_SLOTS; ++a) {
-      mbar_init(aready(a), 4);
+      mbar_init(aready(a), BWD_ROWS / 32);
       mbar_init(adone(a), 1);
     }
     for (int d = 0; d < ACC_SLOTS; ++d) {
       mbar_init(mdone(d), 1);
       mbar_init(accfree(d), 4);
     }
+    mbar_init(tready, 1);
     fence_mbar_init();
   }
-  // The channel's Toeplitz operand for dX, T[s][t] = k[t - s + K/2], built once
-  // by the whole CTA (every tile of this CTA has channel h).
-  {
-    const int pad = K / 2;
-    unsigned char* bm = sm + BG::OFF_B;
-    const float* kh = taps + static_cast<size_t>(h) * K;
-    constexpr int CPR = N / 4;
-    for (int task = static_cast<int>(threadIdx.x); task < N * CPR; task += BWD_THREADS) {
-      const int c4 = task / N;
-      const int tp = task - c4 * N;
-      const int sp = 4 * c4;
-      float v[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int j = tp - (sp + q) + pad;
-        v[q] = (j >= 0 && j < K) ? __ldg(kh + j) : 0.f;
-      }
-      float4 hi, lo;
-      split4(make_float4(v[0], v[1], v[2], v[3]), hi, lo);
-      if (c4 < GG::C128) {
-        *reinterpret_cast<float4*>(bm + sw128_off(tp, c4)) = hi;
-        *reinterpret_cast<float4*>(bm + GG::BLO128 + sw128_off(tp, c4)) = lo;
-      } else {
-        unsigned char* b64 = bm + GG::BBOX64;
-        *reinterpret_cast<float4*>(b64 + sw64_off(tp, c4 - GG::C128)) = hi;
-        *reinterpret_cast<float4*>(b64 + GG::BLO64 + sw64_off(tp, c4 - GG::C128)) = lo;
-      }
-    }
-    fence_proxy_async_smem();  // the MMAs read the operand through the async proxy
-  }
+  // The first channel's Toeplitz operand, by the whole CTA.
+  bwd_build_toeplitz<K>(sm + BG::OFF_B, taps, first.ch, static_cast<int>(threadIdx.x), BWD_THREADS);
+  fence_proxy_async_smem();  // the MMAs read the operand through the async proxy
   if (warp == 1) {
     tmem_alloc(base + BG::OFF_TMEM, TMEM_COLS);
     tmem_relinquish();
@@ -286,42 +324,46 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       // ---------------- TMA producer ----------------
       int issued = 0;
       for (int i = 0; i < n_it; ++i) {
-        const int sd = i % DS, sx = i % XS;
-        if (i >= DS && (!mbar_wait_bounded(dfree(sd), ((i / DS) - 1) & 1, err, DEVERR_TIMEOUT_DONE) ||
-                        !mbar_wait_bounded(mfree(sd), ((i / DS) - 1) & 1, err, DEVERR_TIMEOUT_DONE)))
+        const int s = i % BWD_STAGES;
+        if (i >= BWD_STAGES &&
+            (!mbar_wait_bounded(sfree(s), ((i / BWD_STAGES) - 1) & 1, err, DEVERR_TIMEOUT_DONE) ||
+             !mbar_wait_bounded(mfree(s), ((i / BWD_STAGES) - 1) & 1, err, DEVERR_TIMEOUT_DONE)))
           break;
-        if (i >= XS && !mbar_wait_bounded(xfree(sx), ((i / XS) - 1) & 1, err, DEVERR_TIMEOUT_DONE)) break;
-        const int b0 = ((g + i * G) / H) * M;
-        const uint32_t dst = base + static_cast<uint32_t>(BG::OFF_DY + sd * BG::TILE);
-        const uint32_t xst = base + static_cast<uint32_t>(BG::OFF_X + sx * BG::TILE);
-        mbar_arrive_expect_tx(fullD(sd), BG::TILE);
-        tma_load_3d(dst, &tm_dy128, 0, h, b0, fullD(sd));
-        tma_load_3d(dst + GG::BOX64, &tm_dy64, GG::S64, h, b0, fullD(sd));
-        mbar_arrive_expect_tx(fullX(sx), BG::TILE);
-        tma_load_3d(xst, &tm_x128, 0, h, b0, fullX(sx));
-        tma_load_3d(xst + GG::BOX64, &tm_x64, GG::S64, h, b0, fullX(sx));
+        const BwdTile t = bwd_tile(sc, g, i);
+        const int b0 = t.blk * M;
+        const uint32_t st = base + static_cast<uint32_t>(s * BG::STAGE);
+        mbar_arrive_expect_tx(full(s), BG::STAGE);
+        tma_load_3d(st, &tm_dy128, 0, t.ch, b0, full(s));
+        tma_load_3d(st + GG::BOX64, &tm_dy64, GG::S64, t.ch, b0, full(s));
+        tma_load_3d(st + BG::TILE, &tm_x128, 0, t.ch, b0, full(s));
+        tma_load_3d(st + BG::TILE + GG::BOX64, &tm_x64, GG::S64, t.ch, b0, full(s));
         issued = i + 1;
       }
-      for (int i = issued > DS ? issued - DS : 0; i < issued; ++i)
-        if (!mbar_wait_bounded(fullD(i % DS), (i / DS) & 1, err, DEVERR_TIMEOUT_DRAIN)) break;
-      for (int i = issued > XS ? issued - XS : 0; i < issued; ++i)
-        if (!mbar_wait_bounded(fullX(i % XS), (i / XS) & 1, err, DEVERR_TIMEOUT_DRAIN)) break;
+      for (int i = issued > BWD_STAGES ? issued - BWD_STAGES : 0; i < issued; ++i)
+        if (!mbar_wait_bounded(full(i % BWD_STAGES), (i / BWD_STAGES) & 1, err, DEVERR_TIMEOUT_DRAIN)) break;
     } else if (warp == 1 && lane == 0) {
       // ---------------- MMA issuer (dX) ----------------
       constexpr uint32_t idesc_n2 = idesc_tf32_m128<2 * N>();
       constexpr uint32_t idesc_n = idesc_tf32_m128<N>();
       int issued = 0;
+      int seg = 0;
       for (int i = 0; i < n_it; ++i) {
-        const int a = i % A_SLOTS, d = i % ACC_SLOTS, sd = i % DS;
-        // The dy tile is the A_hi operand: wait for its load as well.
-        if (!mbar_wait_bounded(fullD(sd), (i / DS) & 1, err, DEVERR_TC_MMA)) break;
+        const int a = i % A_SLOTS, d = i % ACC_SLOTS, s = i % BWD_STAGES;
+        const int tseg = bwd_tile(sc, g, i).seg;
+        // A new channel: its Toeplitz operand must be in place.
+        if (tseg != seg) {
+          if (!mbar_wait_bounded(tready, (tseg - 1) & 1, err, DEVERR_TC_MMA)) break;
+          seg = tseg;
+        }
+        // The stage's dy tile is the A_hi operand: wait for its load as well.
+        if (!mbar_wait_bounded(full(s), (i / BWD_STAGES) & 1, err, DEVERR_TC_MMA)) break;
         if (!mbar_wait_bounded(aready(a), (i / A_SLOTS) & 1, err, DEVERR_TC_MMA)) break;
         if (i >= ACC_SLOTS &&
             !mbar_wait_bounded(accfree(d), ((i / ACC_SLOTS) - 1) & 1, err, DEVERR_TC_MMA))
           break;
         tc_fence_after();
         const uint32_t a_lo = tmem + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + LO_COLS);
-        const uint32_t dyt = base + static_cast<uint32_t>(BG::OFF_DY + sd * BG::TILE);
+        const uint32_t dyt = base + static_cast<uint32_t>(s * BG::STAGE);
         const uint32_t bmat = base + static_cast<uint32_t>(BG::OFF_B);
         const uint32_t dacc = tmem + static_cast<uint32_t>(D_COL0 + d * D_SLOT_COLS);
 #pragma unroll
@@ -335,7 +377,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           mma_tf32_ts(dacc, a_lo + 8u * kk, bdesc, idesc_n, 1);  // dy rest T_hi
         }
         mma_commit(adone(a));
-        mma_commit(mfree(sd));
+        mma_commit(mfree(s));
         mma_commit(mdone(d));
         issued = i + 1;
       }
@@ -347,126 +389,153 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   } else if (warp < BWD_EPI0 / 32) {
     setmaxnreg_inc<BWD_REG_ROWS>();
     // ---------------- row workers ----------------
-    bool ok = true;
     const int ct = static_cast<int>(threadIdx.x) - BWD_ROW0;  // 0..255
-    const int grp = ct >> 7;                                   // 0: even tiles, 1: odd tiles
     const int quad = warp & 3;
-    const int row = 32 * quad + lane;                          // tile row (TMEM lane)
+    const int row = 32 * quad + lane;                   // tile row (TMEM lane)
+    const int half = ct >> 7;                           // dX: half of the row; dK: even or odd taps
+    constexpr int CH = (GG::C128 + GG::C64) / 2;        // 6 chunks per half row
     const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
     // In-row byte offset of 16-byte chunk c of this row: (16 c) ^ xm128 in the
     // 128-B box (chunks 0-7), (16 c) ^ xm64 in the 64-B box (chunks 0-3).
     const uint32_t xm128 = static_cast<uint32_t>(row & 7) << 4;
     const uint32_t xm64 = static_cast<uint32_t>((row >> 1) & 3) << 4;
-    uint64_t acc[TP::NACC];
+    uint64_t acc[NJ];  // (even t, odd t) partial sums per tap
 #pragma unroll
-    for (int p = 0; p < TP::NACC; ++p) acc[p] = 0ull;
-    float acc_odd = 0.f;
-    for (int i = grp; i < n_it; i += 2) {
-      const int sd = i % DS, sx = i % XS, a = i % A_SLOTS;  // a == grp
-      if (i >= A_SLOTS) ok = mbar_wait_bounded(adone(a), ((i / A_SLOTS) - 1) & 1, err, DEVERR_TC_CONVERT);
-      if (ok) ok = mbar_wait_bounded(fullD(sd), (i / DS) & 1, err, DEVERR_TIMEOUT_FULL);
-      if (!__all_sync(0xffffffffu, ok)) {  // each warp arrives as one, so it decides as one
-        ok = false;
-        break;
+    for (int jj = 0; jj < NJ; ++jj) acc[jj] = 0ull;
+    // The segment's dK: a warp sum over the quadrant's 32 rows per tap, then
+    // one partial per (quadrant, tap) -- to the workspace, or (direct) to shared
+    // memory for the CTA's own fixed-order sum.
+    auto flush = [&](int seg) {
+      float* red = reinterpret_cast<float*>(sm + BG::OFF_RED);
+      const int slot = bwd_slot(sc, g, seg);
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) {
+        float v = bwd_pair_sum(acc[jj]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        const int j = 2 * jj + half;
+        if (lane == 0 && j < K) {
+          if (sc.direct)
+            red[quad * L + j] = v;
+          else
+            part[(static_cast<size_t>(slot) * 4 + quad) * K + j] = v;
+        }
+        acc[jj] = 0ull;
       }
-      const unsigned char* dy128 = sm + BG::OFF_DY + sd * BG::TILE + 128u * row;
-      const unsigned char* dy64 = sm + BG::OFF_DY + sd * BG::TILE + GG::BOX64 + 64u * row;
-      // dX: the MMA reads dy's tf32 part straight from the stage; this thread
-      // writes the rest of its dy row (A_lo) into tensor memory.
-      {
-        const uint32_t acol = tmem + lane_base + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + LO_COLS);
+    };
+    // Every row worker takes the same path through the named barriers below
+    // (the channel switches depend only on the CTA and the tile index), also
+    // after a wait has run out: a warp that failed skips the work, not the
+    // barriers.
+    bool ok = true;
+    int seg = 0;
+    for (int i = 0; i < n_it; ++i) {
+      const int s = i % BWD_STAGES, a = i % A_SLOTS;
+      if (ok) {
+        if (i >= A_SLOTS) ok = mbar_wait_bounded(adone(a), ((i / A_SLOTS) - 1) & 1, err, DEVERR_TC_CONVERT);
+        if (ok) ok = mbar_wait_bounded(full(s), (i / BWD_STAGES) & 1, err, DEVERR_TIMEOUT_FULL);
+        ok = __all_sync(0xffffffffu, ok);  // each warp arrives as one, so it decides as one
+      }
+      if (ok) {
+        const unsigned char* st = sm + s * BG::STAGE;
+        const unsigned char* dy128 = st + 128u * row;
+        const unsigned char* dy64 = st + GG::BOX64 + 64u * row;
+        const unsigned char* x128 = st + BG::TILE + 128u * row;
+        const unsigned char* x64 = st + BG::TILE + GG::BOX64 + 64u * row;
+        // dX: the MMA reads dy's tf32 part straight from the stage; this thread
+        // writes the rest of its half of the dy row (A_lo) into tensor memory.
+        {
+          float lo[4 * CH];
 #pragma unroll
-        for (int u = 0; u < L / 8; ++u) {
-          float lo[8];
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int c = 2 * u + hh;
-            const float4 q = (c < 8) ? *reinterpret_cast<const float4*>(dy128 + ((16u * c) ^ xm128))
-                                     : *reinterpret_cast<const float4*>(dy64 + ((16u * (c - 8)) ^ xm64));
-            lo[4 * hh] = bwd_tf32_rest(q.x);
-            lo[4 * hh + 1] = bwd_tf32_rest(q.y);
-            lo[4 * hh + 2] = bwd_tf32_rest(q.z);
-            lo[4 * hh + 3] = bwd_tf32_rest(q.w);
+          for (int u = 0; u < CH; ++u) {
+            const int c = half * CH + u;
+            const uint32_t off = (c < GG::C128) ? sw128_off(row, c) : GG::BOX64 + sw64_off(row, c - GG::C128);
+            const float4 q = *reinterpret_cast<const float4*>(st + off);
+            lo[4 * u] = bwd_tf32_rest(q.x);
+            lo[4 * u + 1] = bwd_tf32_rest(q.y);
+            lo[4 * u + 2] = bwd_tf32_rest(q.z);
+            lo[4 * u + 3] = bwd_tf32_rest(q.w);
           }
-          tmem_st8(acol + 8u * u, lo);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(aready(a));
-      }
-      // dK: the x row as packed pairs in registers, dy streamed from shared memory.
-      ok = mbar_wait_bounded(fullX(sx), (i / XS) & 1, err, DEVERR_TIMEOUT_FULL);
-      if (!__all_sync(0xffffffffu, ok)) {
-        ok = false;
-        break;
-      }
-      uint64_t XP[L + 1];
-      {
-        const unsigned char* x128 = sm + BG::OFF_X + sx * BG::TILE + 128u * row;
-        const unsigned char* x64 = sm + BG::OFF_X + sx * BG::TILE + GG::BOX64 + 64u * row;
-        float x[L];
+          const uint32_t acol =
+              tmem + lane_base + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + LO_COLS + half * 4 * CH);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float4 q = *reinterpret_cast<const float4*>(x128 + ((16u * c) ^ xm128));
-          x[4 * c] = q.x;
-          x[4 * c + 1] = q.y;
-          x[4 * c + 2] = q.z;
-          x[4 * c + 3] = q.w;
+          for (int u = 0; u < CH / 2; ++u) tmem_st8(acol + 8u * u, lo + 8 * u);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(aready(a));
         }
+        // dK: the x row in registers, dy[t] streamed from shared memory.
+        {
+          float x[L];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float4 q = *reinterpret_cast<const float4*>(x64 + ((16u * c) ^ xm64));
-          x[32 + 4 * c] = q.x;
-          x[32 + 4 * c + 1] = q.y;
-          x[32 + 4 * c + 2] = q.z;
-          x[32 + 4 * c + 3] = q.w;
+          for (int c = 0; c < 8; ++c) {
+            const float4 q = *reinterpret_cast<const float4*>(x128 + ((16u * c) ^ xm128));
+            x[4 * c] = q.x;
+            x[4 * c + 1] = q.y;
+            x[4 * c + 2] = q.z;
+            x[4 * c + 3] = q.w;
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float4 q = *reinterpret_cast<const float4*>(x64 + ((16u * c) ^ xm64));
+            x[32 + 4 * c] = q.x;
+            x[32 + 4 * c + 1] = q.y;
+            x[32 + 4 * c + 2] = q.z;
+            x[32 + 4 * c + 3] = q.w;
+          }
+          // XP[q] = (X[k], X[k + 1]), k = K0 + 2q, with X[n] = x[n - 1 + half] on
+          // [0, 49) and 0 elsewhere (half 1's copy of the row is shifted by one).
+          using P = BwdPairs<K>;
+          auto xz = [&](int n) { return (n >= 0 && n < L) ? x[n] : 0.f; };  // compile-time n
+          uint64_t XP[P::NQ];
+#pragma unroll
+          for (int q = 0; q < P::NQ; ++q) {
+            const int k = P::K0 + 2 * q;
+            const float e0 = (k >= 0 && k <= L) ? (half ? xz(k) : xz(k - 1)) : 0.f;
+            const float e1 = (k + 1 >= 0 && k + 1 <= L) ? (half ? xz(k + 1) : xz(k)) : 0.f;
+            XP[q] = bwd_pack(e0, e1);
+          }
+          bwd_dk_row2<K>(dy128, dy64, xm128, xm64, XP, acc);
         }
-        // The x rows are in registers: the x slot can be refilled.
+        // The stage is read: order the reads before the next TMA write, release it.
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(xfree(sx));
-        auto xz = [&](int n) { return (n >= 0 && n < L) ? x[n] : 0.f; };  // compile-time n
-#pragma unroll
-        for (int q = 0; q <= L; ++q) XP[q] = bwd_pack(xz(q - 1), xz(q));
+        if (lane == 0) mbar_arrive(sfree(s));
       }
-      bwd_dk_row<K>(dy128, dy64, xm128, xm64, XP, acc, acc_odd);
-      // The dy tile is read: order the reads before the next TMA write, release it.
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dfree(sd));
-    }
-    // ---------------- dK: sum the CTA's rows in a fixed order ----------------
-    // The scratch below overwrites the dy ring, which the last tiles' MMAs may
-    // still read: wait for the last MMA group (groups complete in issue order).
-    if (ok && n_it > 0)
-      ok = mbar_wait_bounded(mfree((n_it - 1) % DS), ((n_it - 1) / DS) & 1, err, DEVERR_TC_CONVERT);
-    if (!named_barrier_or(2, BWD_ROWS, !ok)) {
-      // Both groups are done with every tile and every load has been consumed:
-      // reuse the dy ring as [K][256] scratch.
-      float* red = reinterpret_cast<float*>(sm + BG::OFF_DY);
-#pragma unroll
-      for (int p = 0; p < TP::NP; ++p) {
-        float lo, hi;
-        bwd_unpack(acc[p], lo, hi);
-        red[(2 * p) * BWD_ROWS + ct] = lo;
-        red[(2 * p + 1) * BWD_ROWS + ct] = hi;
-      }
-      if (TP::ODD) red[(K - 1) * BWD_ROWS + ct] = acc_odd;
-      named_barrier(2, BWD_ROWS);
-      for (int j = ct; j < K; j += BWD_ROWS) {
-        float sum = 0.f;
-        for (int r = 0; r < BWD_ROWS; ++r) sum += red[j * BWD_ROWS + r];
-        if (direct) {
-          float* dst = dk_out + static_cast<size_t>(h) * K + j;
-          *dst = accumulate ? *dst + sum : sum;
-        } else {
-          dk_out[static_cast<size_t>(g) * 2 * K + j] = sum;
+      // A channel switch (helpers only): flush this channel's dK, then, once the
+      // MMAs of this tile -- and so every earlier one -- are done with the old
+      // Toeplitz operand, build the next channel's and signal the MMA issuer.
+      if (i + 1 < n_it) {
+        const BwdTile nxt = bwd_tile(sc, g, i + 1);
+        if (nxt.seg != seg) {
+          if (ok) {
+            flush(seg);
+            ok = mbar_wait_bounded(mfree(s), (i / BWD_STAGES) & 1, err, DEVERR_TC_CONVERT);
+          }
+          if (named_barrier_or(2, BWD_ROWS, !ok)) ok = false;
+          if (ok) {
+            bwd_build_toeplitz<K>(sm + BG::OFF_B, taps, nxt.ch, ct, BWD_ROWS);
+            fence_proxy_async_smem();
+          }
+          if (named_barrier_or(2, BWD_ROWS, !ok)) ok = false;
+          if (ok && ct == 0) mbar_arrive(tready);
+          seg = nxt.seg;
         }
       }
-      if (!direct && ct == 0) {
-        group_of[2 * g] = h;
-        group_of[2 * g + 1] = -1;
+    }
+    // ---------------- dK of the last (or only) segment ----------------
+    if (!named_barrier_or(2, BWD_ROWS, !ok)) {
+      flush(seg);
+      if (sc.direct) {
+        named_barrier(2, BWD_ROWS);
+        const float* red = reinterpret_cast<const float*>(sm + BG::OFF_RED);
+        const int h = first.ch;
+        for (int j = ct; j < K; j += BWD_ROWS) {
+          const float sum = ((red[j] + red[L + j]) + red[2 * L + j]) + red[3 * L + j];
+          float* dst = dk + static_cast<size_t>(h) * K + j;
+          *dst = accumulate ? *dst + sum : sum;
+        }
       }
     }
   } else {
@@ -475,16 +544,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const int et = static_cast<int>(threadIdx.x) - BWD_EPI0;  // 0..127
     const int quad = warp & 3;
     const int r = 32 * quad + lane;
-    unsigned char* ob = sm + BG::OFF_OUT;
-    const uint32_t os = base + static_cast<uint32_t>(BG::OFF_OUT);
     for (int j = 0; j < n_it; ++j) {
-      const int d = j % ACC_SLOTS;
-      if (et == 0) bulk_wait_read<0>();  // the previous store has read the staging tile
+      const int d = j % ACC_SLOTS, o = j % OUT_SLOTS;
+      if (et == 0) bulk_wait_read<OUT_SLOTS - 1>();
       const bool okw = mbar_wait_bounded(mdone(d), (j / ACC_SLOTS) & 1, err, DEVERR_TC_EPILOGUE);
       if (named_barrier_or(1, 128, !okw)) break;
       tc_fence_after();
       const uint32_t ta = tmem + (static_cast<uint32_t>(32 * quad) << 16) +
                           static_cast<uint32_t>(D_COL0 + d * D_SLOT_COLS);
+      unsigned char* ob = sm + BG::OFF_OUT + o * BG::TILE;
+      // D[:, t] + D[:, N + t], sixteen columns at a time.
 #pragma unroll
       for (int cc = 0; cc < N / 16; ++cc) {
         float v0[16], v1[16];
@@ -506,9 +575,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       fence_proxy_async_smem();
       named_barrier(1, 128);
       if (et == 0) {
-        const int b0 = ((g + j * G) / H) * M;
-        tma_store_3d(&tm_dx128, os, 0, h, b0);
-        tma_store_3d(&tm_dx64, os + GG::BOX64, GG::S64, h, b0);
+        const BwdTile t = bwd_tile(sc, g, j);
+        const uint32_t os = base + static_cast<uint32_t>(BG::OFF_OUT + o * BG::TILE);
+        tma_store_3d(&tm_dx128, os, 0, t.ch, t.blk * M);
+        tma_store_3d(&tm_dx64, os + GG::BOX64, GG::S64, t.ch, t.blk * M);
         bulk_commit();
       }
     }
@@ -520,6 +590,28 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
+}
+
+// dk[h][j] (=, or += when accumulate) the channel's partials in a fixed order:
+// its kp primaries' four quadrants, then its helper segment's four.
+template <int DUMMY = 0>
+__global__ void __launch_bounds__(256) bwd_dk_reduce_kernel(const float* __restrict__ part, float* __restrict__ dk,
+                                                            const BwdSched sc, int K, int accumulate) {
+  const int idx = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+  if (idx >= sc.H * K) return;
+  const int h = idx / K;
+  const int j = idx - h * K;
+  float sum = 0.f;
+  for (int r = 0; r < sc.kp; ++r) {
+    const float* p = part + static_cast<size_t>(h + r * sc.H) * 4 * K + j;
+    sum += ((p[0] + p[K]) + p[2 * K]) + p[3 * K];
+  }
+  if (sc.E > 0) {
+    const int slot = sc.kp * sc.H + (h % sc.E) * sc.m + h / sc.E;
+    const float* p = part + static_cast<size_t>(slot) * 4 * K + j;
+    sum += ((p[0] + p[K]) + p[2 * K]) + p[3 * K];
+  }
+  dk[idx] = accumulate ? dk[idx] + sum : sum;
 }
 
 }  // namespace tc

@@ -38,5 +38,13 @@ const void* bwd_kernel_k1_24(int K) {
 
 size_t bwd_smem_bytes() { return BwdGeo::SMEM; }
 
+int bwd_threads() { return BWD_LAUNCH_THREADS; }
+
+void bwd_dk_reduce(const float* part, float* dk, const BwdSched& sc, int K, int accumulate, void* stream) {
+  const int n = sc.H * K;
+  bwd_dk_reduce_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(part, dk, sc, K,
+                                                                                         accumulate);
+}
+
 }  // namespace tc
 }  // namespace pt

@@ -43,14 +43,36 @@ def _sm_count(dev) -> int:
     return torch.cuda.get_device_properties(dev).multi_processor_count
 
 
+def tensor_schedule(B, H, sm):
+    """The host's schedule of the tensor-core fused kernel (None: it does not apply):
+    kp = floor(min(tiles, SMs) / H) primary CTAs per channel; the SMs left over
+    become helpers taking every channel's tail blocks when that shortens the
+    busiest CTA (a channel switch counted as one tile) by >= 3 % and no helper
+    owns more than 4 channels; otherwise the plain grid of kp*H CTAs, which must
+    keep >= 3/4 of min(tiles, SMs) busy."""
+    nblk = -(-B // 128)
+    gmax = min(nblk * H, sm)
+    kp = gmax // H
+    if kp < 1:
+        return None
+    plain = -(-nblk // kp)
+    E = sm - kp * H
+    if E >= 1 and nblk >= 2 and -(-H // E) <= 4:
+        m = -(-H // E)
+        best, best_p = plain, 0
+        for P in range(1, nblk):
+            cost = max(-(-P // kp), m * (nblk - P) + (m - 1))
+            if cost < best:
+                best, best_p = cost, P
+        if best_p > 0 and 100 * best <= 97 * plain:
+            return {"kp": kp, "E": E, "m": m, "P": best_p, "tiles": best}
+    if 4 * kp * H < 3 * gmax:
+        return None
+    return {"kp": kp, "E": 0, "m": 0, "P": nblk, "tiles": plain}
+
+
 def _expect_tensor_fused(B, H, L, K, sm) -> bool:
-    """The host rule: 32 < L <= 48 with L % 4 == 0, any K <= 48, and a grid of
-    whole channels (a multiple of H) that keeps at least 3/4 of min(tiles, SMs) busy."""
-    if not _fusable_layout(L, K):
-        return False
-    gmax = min(-(-B // 128) * H, sm)
-    G = (gmax // H) * H
-    return G >= 1 and 4 * G >= 3 * gmax
+    return _fusable_layout(L, K) and tensor_schedule(B, H, sm) is not None
 
 
 def _expect_kind(B, H, L, K, sm) -> str:
@@ -89,6 +111,11 @@ SHAPES = [
     (5000, 74, 48, 32),   # 2 CTAs per channel
     (64, 1, 48, 3),
     (700, 128, 48, 5),    # K not among the CUDA-core kernels' specialisations
+    (4096, 128, 48, 48),  # plain grid: one CTA per channel (7 channels per helper is too many)
+    (4096, 100, 48, 7),   # helpers (48) with up to three channels each
+    (3000, 96, 48, 40),   # helpers (52) with two channels each; no plain grid at H = 96
+    (3000, 64, 48, 24),   # two primaries per channel plus helpers
+    (5000, 100, 44, 11),  # 44-column rows, helpers
     (300, 128, 48, 47),   # odd K, the largest register spill
     (250, 128, 48, 1),
     (1000, 128, 44, 44),  # 44-column rows in the 48-column layout
@@ -177,7 +204,20 @@ def test_forcing_a_tensor_engine_keeps_the_cuda_core_fusion_off(cuda_device):
     assert ops.backward_kind(300, 96, 48, 24) == "ffma_fused"
 
 
-@pytest.mark.parametrize("H", [128, 64])
+@pytest.mark.parametrize("B,H", [(16384, 128), (16384, 64), (16384, 96)])
+def test_fused_schedule_grid(cuda_device, B, H):
+    sm = _sm_count(cuda_device)
+    sc = tensor_schedule(B, H, sm)
+    if sm == 148:
+        expect = {128: {"kp": 1, "E": 0}, 64: {"kp": 2, "E": 20, "m": 4}, 96: {"kp": 1, "E": 52, "m": 2}}[H]
+        assert all(sc[k] == v for k, v in expect.items()), sc
+    assert ops.backward_kind(B, H, 48, 48) == "tensor_fused"
+    info = ops.kernel_info("bwd_fused", B, H, 48, 48)
+    assert info["grid"] == (sm if sc["E"] else sc["kp"] * H)
+    assert info["threads_per_block"] == 512 and info["local_memory_bytes"] == 0
+
+
+@pytest.mark.parametrize("H", [128, 64, 96])
 def test_fused_backward_accumulate_and_determinism(cuda_device, H):
     dev = cuda_device
     B, L, K = 3000, 48, 48
