@@ -43,7 +43,7 @@
 //                channel switch, flush dK and rebuild the Toeplitz operand
 //   warps 12-15  dX epilogue: TMEM -> staging -> TMA store
 // After the set-up the CTA's 512 x 128 registers are rebalanced with
-// setmaxnreg (warpgroup 0: 72, row workers: 168, epilogue: 104; no region
+// setmaxnreg (warpgroup 0: 72, row workers: 160, epilogue: 120; no region
 // spills).  The host launches the kernel only where the compiled function
 // starts with 128 registers per thread, the split's budget.  Every wait is
 // bounded; on expiry the kernel records a bit in the device error word, drains
@@ -66,8 +66,8 @@ constexpr int BWD_ROW0 = 128;         // first row-worker thread (warp 4)
 constexpr int BWD_ROWS = 256;         // row workers
 constexpr int BWD_EPI0 = 384;         // first epilogue thread (warp 12)
 constexpr int BWD_REG_CTRL = 72;
-constexpr int BWD_REG_ROWS = 168;
-constexpr int BWD_REG_EPI = 104;
+constexpr int BWD_REG_ROWS = 160;
+constexpr int BWD_REG_EPI = 120;
 static_assert(128 * BWD_REG_CTRL + BWD_ROWS * BWD_REG_ROWS + 128 * BWD_REG_EPI <= BWD_THREADS * BWD_LAUNCH_REGS,
               "the register split must fit the registers the CTA is launched with");
 
@@ -428,101 +428,106 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     // after a wait has run out: a warp that failed skips the work, not the
     // barriers.
     bool ok = true;
+    // Tiles [seg_begin, seg_end) belong to one channel: a primary has one
+    // segment, a helper one per channel it owns (tp tiles each).
+    const bool helper = g >= sc.kp * sc.H;
+    const int tp = sc.nblk - sc.P;
     int seg = 0;
-    for (int i = 0; i < n_it; ++i) {
-      const int s = i % BWD_STAGES, a = i % A_SLOTS;
-      if (ok) {
-        if (i >= A_SLOTS) ok = mbar_wait_bounded(adone(a), ((i / A_SLOTS) - 1) & 1, err, DEVERR_TC_CONVERT);
-        if (ok) ok = mbar_wait_bounded(full(s), (i / BWD_STAGES) & 1, err, DEVERR_TIMEOUT_FULL);
-        ok = __all_sync(0xffffffffu, ok);  // each warp arrives as one, so it decides as one
-      }
-      if (ok) {
-        const unsigned char* st = sm + s * BG::STAGE;
-        const unsigned char* dy128 = st + 128u * row;
-        const unsigned char* dy64 = st + GG::BOX64 + 64u * row;
-        const unsigned char* x128 = st + BG::TILE + 128u * row;
-        const unsigned char* x64 = st + BG::TILE + GG::BOX64 + 64u * row;
-        // dX: the MMA reads dy's tf32 part straight from the stage; this thread
-        // writes the rest of its half of the dy row (A_lo) into tensor memory.
-        {
-          float lo[4 * CH];
-#pragma unroll
-          for (int u = 0; u < CH; ++u) {
-            const int c = half * CH + u;
-            const uint32_t off = (c < GG::C128) ? sw128_off(row, c) : GG::BOX64 + sw64_off(row, c - GG::C128);
-            const float4 q = *reinterpret_cast<const float4*>(st + off);
-            lo[4 * u] = bwd_tf32_rest(q.x);
-            lo[4 * u + 1] = bwd_tf32_rest(q.y);
-            lo[4 * u + 2] = bwd_tf32_rest(q.z);
-            lo[4 * u + 3] = bwd_tf32_rest(q.w);
+    for (int i = 0;;) {
+      const int seg_end = helper ? min(n_it, (seg + 1) * tp) : n_it;
+      for (; i < seg_end; ++i) {
+        const int s = i % BWD_STAGES, a = i % A_SLOTS;
+        if (ok) {
+          if (i >= A_SLOTS) ok = mbar_wait_bounded(adone(a), ((i / A_SLOTS) - 1) & 1, err, DEVERR_TC_CONVERT);
+          if (ok) ok = mbar_wait_bounded(full(s), (i / BWD_STAGES) & 1, err, DEVERR_TIMEOUT_FULL);
+          ok = __all_sync(0xffffffffu, ok);  // each warp arrives as one, so it decides as one
+        }
+        if (ok) {
+          const unsigned char* st = sm + s * BG::STAGE;
+          const unsigned char* dy128 = st + 128u * row;
+          const unsigned char* dy64 = st + GG::BOX64 + 64u * row;
+          const unsigned char* x128 = st + BG::TILE + 128u * row;
+          const unsigned char* x64 = st + BG::TILE + GG::BOX64 + 64u * row;
+          // dX: the MMA reads dy's tf32 part straight from the stage; this thread
+          // writes the rest of its half of the dy row (A_lo) into tensor memory.
+          {
+            float lo[4 * CH];
+  #pragma unroll
+            for (int u = 0; u < CH; ++u) {
+              const int c = half * CH + u;
+              const uint32_t off = (c < GG::C128) ? sw128_off(row, c) : GG::BOX64 + sw64_off(row, c - GG::C128);
+              const float4 q = *reinterpret_cast<const float4*>(st + off);
+              lo[4 * u] = bwd_tf32_rest(q.x);
+              lo[4 * u + 1] = bwd_tf32_rest(q.y);
+              lo[4 * u + 2] = bwd_tf32_rest(q.z);
+              lo[4 * u + 3] = bwd_tf32_rest(q.w);
+            }
+            const uint32_t acol =
+                tmem + lane_base + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + LO_COLS + half * 4 * CH);
+  #pragma unroll
+            for (int u = 0; u < CH / 2; ++u) tmem_st8(acol + 8u * u, lo + 8 * u);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(aready(a));
           }
-          const uint32_t acol =
-              tmem + lane_base + static_cast<uint32_t>(A_COL0 + a * A_SLOT_COLS + LO_COLS + half * 4 * CH);
-#pragma unroll
-          for (int u = 0; u < CH / 2; ++u) tmem_st8(acol + 8u * u, lo + 8 * u);
-          tmem_wait_st();
-          tc_fence_before();
+          // dK: the x row in registers, dy[t] streamed from shared memory.
+          {
+            float x[L];
+  #pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const float4 q = *reinterpret_cast<const float4*>(x128 + ((16u * c) ^ xm128));
+              x[4 * c] = q.x;
+              x[4 * c + 1] = q.y;
+              x[4 * c + 2] = q.z;
+              x[4 * c + 3] = q.w;
+            }
+  #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const float4 q = *reinterpret_cast<const float4*>(x64 + ((16u * c) ^ xm64));
+              x[32 + 4 * c] = q.x;
+              x[32 + 4 * c + 1] = q.y;
+              x[32 + 4 * c + 2] = q.z;
+              x[32 + 4 * c + 3] = q.w;
+            }
+            // XP[q] = (X[k], X[k + 1]), k = K0 + 2q, with X[n] = x[n - 1 + half] on
+            // [0, 49) and 0 elsewhere (half 1's copy of the row is shifted by one).
+            using P = BwdPairs<K>;
+            auto xz = [&](int n) { return (n >= 0 && n < L) ? x[n] : 0.f; };  // compile-time n
+            uint64_t XP[P::NQ];
+  #pragma unroll
+            for (int q = 0; q < P::NQ; ++q) {
+              const int k = P::K0 + 2 * q;
+              const float e0 = (k >= 0 && k <= L) ? (half ? xz(k) : xz(k - 1)) : 0.f;
+              const float e1 = (k + 1 >= 0 && k + 1 <= L) ? (half ? xz(k + 1) : xz(k)) : 0.f;
+              XP[q] = bwd_pack(e0, e1);
+            }
+            bwd_dk_row2<K>(dy128, dy64, xm128, xm64, XP, acc);
+          }
+          // The stage is read: order the reads before the next TMA write, release it.
+          fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(aready(a));
+          if (lane == 0) mbar_arrive(sfree(s));
         }
-        // dK: the x row in registers, dy[t] streamed from shared memory.
-        {
-          float x[L];
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const float4 q = *reinterpret_cast<const float4*>(x128 + ((16u * c) ^ xm128));
-            x[4 * c] = q.x;
-            x[4 * c + 1] = q.y;
-            x[4 * c + 2] = q.z;
-            x[4 * c + 3] = q.w;
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const float4 q = *reinterpret_cast<const float4*>(x64 + ((16u * c) ^ xm64));
-            x[32 + 4 * c] = q.x;
-            x[32 + 4 * c + 1] = q.y;
-            x[32 + 4 * c + 2] = q.z;
-            x[32 + 4 * c + 3] = q.w;
-          }
-          // XP[q] = (X[k], X[k + 1]), k = K0 + 2q, with X[n] = x[n - 1 + half] on
-          // [0, 49) and 0 elsewhere (half 1's copy of the row is shifted by one).
-          using P = BwdPairs<K>;
-          auto xz = [&](int n) { return (n >= 0 && n < L) ? x[n] : 0.f; };  // compile-time n
-          uint64_t XP[P::NQ];
-#pragma unroll
-          for (int q = 0; q < P::NQ; ++q) {
-            const int k = P::K0 + 2 * q;
-            const float e0 = (k >= 0 && k <= L) ? (half ? xz(k) : xz(k - 1)) : 0.f;
-            const float e1 = (k + 1 >= 0 && k + 1 <= L) ? (half ? xz(k + 1) : xz(k)) : 0.f;
-            XP[q] = bwd_pack(e0, e1);
-          }
-          bwd_dk_row2<K>(dy128, dy64, xm128, xm64, XP, acc);
-        }
-        // The stage is read: order the reads before the next TMA write, release it.
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sfree(s));
       }
+      if (i >= n_it) break;
       // A channel switch (helpers only): flush this channel's dK, then, once the
-      // MMAs of this tile -- and so every earlier one -- are done with the old
-      // Toeplitz operand, build the next channel's and signal the MMA issuer.
-      if (i + 1 < n_it) {
-        const BwdTile nxt = bwd_tile(sc, g, i + 1);
-        if (nxt.seg != seg) {
-          if (ok) {
-            flush(seg);
-            ok = mbar_wait_bounded(mfree(s), (i / BWD_STAGES) & 1, err, DEVERR_TC_CONVERT);
-          }
-          if (named_barrier_or(2, BWD_ROWS, !ok)) ok = false;
-          if (ok) {
-            bwd_build_toeplitz<K>(sm + BG::OFF_B, taps, nxt.ch, ct, BWD_ROWS);
-            fence_proxy_async_smem();
-          }
-          if (named_barrier_or(2, BWD_ROWS, !ok)) ok = false;
-          if (ok && ct == 0) mbar_arrive(tready);
-          seg = nxt.seg;
-        }
+      // MMAs of the segment's last tile -- and so every earlier one -- are done
+      // with the old Toeplitz operand, build the next channel's and signal the
+      // MMA issuer.
+      const int sl = (i - 1) % BWD_STAGES;
+      if (ok) {
+        flush(seg);
+        ok = mbar_wait_bounded(mfree(sl), ((i - 1) / BWD_STAGES) & 1, err, DEVERR_TC_CONVERT);
       }
+      if (named_barrier_or(2, BWD_ROWS, !ok)) ok = false;
+      if (ok) {
+        bwd_build_toeplitz<K>(sm + BG::OFF_B, taps, bwd_tile(sc, g, i).ch, ct, BWD_ROWS);
+        fence_proxy_async_smem();
+      }
+      if (named_barrier_or(2, BWD_ROWS, !ok)) ok = false;
+      if (ok && ct == 0) mbar_arrive(tready);
+      ++seg;
     }
     // ---------------- dK of the last (or only) segment ----------------
     if (!named_barrier_or(2, BWD_ROWS, !ok)) {
@@ -550,28 +555,27 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const bool okw = mbar_wait_bounded(mdone(d), (j / ACC_SLOTS) & 1, err, DEVERR_TC_EPILOGUE);
       if (named_barrier_or(1, 128, !okw)) break;
       tc_fence_after();
+      // The whole accumulator row in registers, then release the accumulator
+      // to the MMAs before the sums and the staging stores.
+      float accd[2 * N];
       const uint32_t ta = tmem + (static_cast<uint32_t>(32 * quad) << 16) +
                           static_cast<uint32_t>(D_COL0 + d * D_SLOT_COLS);
-      unsigned char* ob = sm + BG::OFF_OUT + o * BG::TILE;
-      // D[:, t] + D[:, N + t], sixteen columns at a time.
 #pragma unroll
-      for (int cc = 0; cc < N / 16; ++cc) {
-        float v0[16], v1[16];
-        tmem_ld16(ta + 16u * cc, v0);
-        tmem_ld16(ta + static_cast<uint32_t>(N) + 16u * cc, v1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int c = 4 * cc + q;  // 16-byte chunk of the row
-          const float4 y = make_float4(v0[4 * q] + v1[4 * q], v0[4 * q + 1] + v1[4 * q + 1],
-                                       v0[4 * q + 2] + v1[4 * q + 2], v0[4 * q + 3] + v1[4 * q + 3]);
-          const uint32_t off = (c < GG::C128) ? sw128_off(r, c) : GG::BOX64 + sw64_off(r, c - GG::C128);
-          *reinterpret_cast<float4*>(ob + off) = y;
-        }
-      }
+      for (int u = 0; u < 2 * N / 16; ++u) tmem_ld16(ta + 16u * u, accd + 16 * u);
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(accfree(d));
+      unsigned char* ob = sm + BG::OFF_OUT + o * BG::TILE;
+      // D[:, t] + D[:, N + t]
+#pragma unroll
+      for (int c = 0; c < GG::C128 + GG::C64; ++c) {
+        const float4 y = make_float4(accd[4 * c] + accd[N + 4 * c], accd[4 * c + 1] + accd[N + 4 * c + 1],
+                                     accd[4 * c + 2] + accd[N + 4 * c + 2],
+                                     accd[4 * c + 3] + accd[N + 4 * c + 3]);
+        const uint32_t off = (c < GG::C128) ? sw128_off(r, c) : GG::BOX64 + sw64_off(r, c - GG::C128);
+        *reinterpret_cast<float4*>(ob + off) = y;
+      }
       fence_proxy_async_smem();
       named_barrier(1, 128);
       if (et == 0) {
