@@ -204,7 +204,9 @@ PT_API int pt_set_engine(int path, int engine);
  * entry per path, indexed by PT_PATH_FWD / PT_PATH_DX / PT_PATH_DK:
  * rows_per_tile 0 takes the frozen PathTile table for that path (the other
  * three fields are then ignored), else the same ranges as pt_set_config;
- * engine -1 takes the frozen engine, else PT_ENGINE_*.  The *_ex entry points
+ * engine -1 takes the frozen engine, else PT_ENGINE_*; bwd_kernel and
+ * helper_channels select pt_dx_dk's kernel and the tensor-core fused kernel's
+ * schedule (-1: frozen).  The *_ex entry points
  * below behave exactly like their plain counterparts, with `opts` in place of
  * the process-wide overrides for the duration of the call (NULL: the
  * process-wide state).  Invalid options give PT_ERR_ARGS (0 for the size
@@ -218,7 +220,17 @@ typedef struct pt_launch_opts {
   int ctas_per_sm[3];
   int threads_per_row[3];
   int engine[3];
+  int bwd_kernel;       /* pt_dx_dk: PT_BWD_* (PT_BWD_FROZEN: the frozen per-class choice) */
+  int helper_channels;  /* tensor-core fused kernel: most channels one helper CTA may own
+                           (0: no helper CTAs; -1: the frozen per-class limit) */
 } pt_launch_opts;
+
+/* Backward kernels pt_dx_dk may run (pt_launch_opts.bwd_kernel). */
+#define PT_BWD_FROZEN (-1)        /* the frozen per-class choice */
+#define PT_BWD_SEPARATE 0         /* pt_dx then pt_dk */
+#define PT_BWD_TENSOR_FUSED 1     /* the tensor-core fused kernel where it applies, else separate */
+#define PT_BWD_FFMA_FUSED 2       /* the CUDA-core fused kernel where it applies, else separate */
+#define PT_BWD_ANY_FUSED 3        /* tensor-core fused, else CUDA-core fused, else separate */
 
 PT_API int pt_fwd_ex(const float* x, const float* k, float* y, int B, int H, int L, int K,
                      const pt_launch_opts* opts, void* stream);

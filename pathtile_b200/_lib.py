@@ -35,6 +35,13 @@ PT_PATH_BWD_FUSED = 3  # pt_kernel_info only
 PT_ENGINE_FFMA = 0
 PT_ENGINE_TENSOR = 1
 
+# pt_launch_opts.bwd_kernel: the kernel pt_dx_dk runs.
+PT_BWD_FROZEN = -1
+PT_BWD_SEPARATE = 0
+PT_BWD_TENSOR_FUSED = 1
+PT_BWD_FFMA_FUSED = 2
+PT_BWD_ANY_FUSED = 3
+
 PT_MAX_L = 48
 PT_MAX_K = 48
 
@@ -51,6 +58,8 @@ class LaunchOpts(ctypes.Structure):
         ("ctas_per_sm", ctypes.c_int * 3),
         ("threads_per_row", ctypes.c_int * 3),
         ("engine", ctypes.c_int * 3),
+        ("bwd_kernel", ctypes.c_int),
+        ("helper_channels", ctypes.c_int),
     ]
 
     @classmethod
@@ -58,6 +67,8 @@ class LaunchOpts(ctypes.Structure):
         o = cls()
         for p in range(3):
             o.engine[p] = -1
+        o.bwd_kernel = PT_BWD_FROZEN
+        o.helper_channels = -1
         return o
 
 

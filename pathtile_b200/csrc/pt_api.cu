@@ -61,6 +61,8 @@ struct Opts {
   pt::LaunchCfg cfg[3] = {};
   bool has_cfg[3] = {false, false, false};
   int engine[3] = {-1, -1, -1};  // -1: the frozen table decides
+  int bwd_kernel = -1;           // PT_BWD_*; -1: the frozen table decides
+  int helper_channels = -1;      // -1: the frozen table decides
 };
 Opts g_opts;
 thread_local const Opts* t_opts = nullptr;
@@ -566,23 +568,31 @@ int launch_tensor_dk(const Plan& p, const float* dy, const float* x, float* dk, 
   return PT_OK;
 }
 
+// pt_dx_dk's kernel choice at a shape: the caller's, else the frozen table's.
+pt::BwdChoice bwd_choice(int L, int K) {
+  const Opts& o = opts();
+  pt::BwdChoice c = pt::kFrozenBwd[intensity_class(L, K)];
+  if (o.bwd_kernel >= 0) c.kernel = o.bwd_kernel;
+  if (o.helper_channels >= 0) c.helper_channels = o.helper_channels;
+  return c;
+}
+
 // Work schedule of the tensor-core fused backward on `sms` SMs (pt::tc::BwdSched):
 // kp = floor(min(tiles, sms) / H) primary CTAs per channel; the E = sms - kp*H
 // SMs left over become helpers that take every channel's tail blocks when that
 // shortens the busiest CTA by at least 3 % (a helper's channel switch counted
 // as one tile; P chosen to balance primaries and helpers) and no helper owns
-// more than kMaxHelperChannels channels.  Otherwise the plain grid of kp*H
+// more than max_helper_channels channels (the frozen per-class limit, or the
+// caller's).  Otherwise the plain grid of kp*H
 // CTAs, which must keep at least 3/4 of min(tiles, SMs) busy.  A channel switch
 // drains the helper's MMA pipeline while the Toeplitz operand is rebuilt (the
 // shared memory holds one), so many switches cost more than the extra SMs
 // give: measured at B = 16384, L = K = 48, helpers made H = 64 (4 channels per
 // helper) 7 % faster and H = 96 (2 per helper; no plain grid) 24 % faster than
 // the separate kernels, but H = 128 (7 per helper) 6 % slower than the plain
-// grid, and 11 % slower at K = 3.
+// grid, and 11 % slower at K = 3; the frozen table holds the limit per class.
 // Returns the grid size, or 0 where the kernel does not apply.
-constexpr int kMaxHelperChannels = 4;
-
-int fused_schedule(int B, int H, int sms, pt::tc::BwdSched& sc) {
+int fused_schedule(int B, int H, int sms, int max_helper_channels, pt::tc::BwdSched& sc) {
   const int nblk = (B + pt::tc::kRowsPerTile - 1) / pt::tc::kRowsPerTile;
   const long long tiles = static_cast<long long>(nblk) * H;
   const int gmax = static_cast<int>(tiles < sms ? tiles : sms);
@@ -591,7 +601,7 @@ int fused_schedule(int B, int H, int sms, pt::tc::BwdSched& sc) {
   const int plain = (nblk + kp - 1) / kp;  // tiles of the busiest CTA in the plain grid
   const int E = sms - kp * H;
   int best_cost = plain, best_p = 0;
-  if (E >= 1 && nblk >= 2 && (H + E - 1) / E <= kMaxHelperChannels) {
+  if (E >= 1 && nblk >= 2 && (H + E - 1) / E <= max_helper_channels) {
     const int m = (H + E - 1) / E;
     for (int P = 1; P < nblk; ++P) {
       const int prim = (P + kp - 1) / kp;
@@ -624,7 +634,7 @@ bool plan_fused(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   if (dx_engine >= 0 && dx_engine != PT_ENGINE_TENSOR) return false;
   if (static_cast<long long>(pt::tc::bwd_smem()) > di.max_smem) return false;
   pt::tc::BwdSched sc{};
-  const int G = fused_schedule(B, H, di.sm_count, sc);
+  const int G = fused_schedule(B, H, di.sm_count, bwd_choice(L, K).helper_channels, sc);
   if (G < 1) return false;
   if (ensure_smem_attr(di, func, pt::tc::bwd_smem()) != PT_OK) return false;
   // The kernel rebalances registers between its warpgroups (setmaxnreg), which
@@ -711,7 +721,8 @@ size_t dk_ws_bytes(const Plan& p);
 bool plan_bwd_rows(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
   const Opts& o = opts();
   if (o.engine[PT_PATH_DX] == PT_ENGINE_TENSOR || o.engine[PT_PATH_DK] == PT_ENGINE_TENSOR) return false;
-  if (intensity_class(L, K) == 2 && engine_for(PT_PATH_DX, B, H, L, K, di.sm_count) == PT_ENGINE_TENSOR)
+  if (bwd_choice(L, K).kernel == PT_BWD_ANY_FUSED && intensity_class(L, K) == 2 &&
+      engine_for(PT_PATH_DX, B, H, L, K, di.sm_count) == PT_ENGINE_TENSOR)
     return false;
   const pt::Entry* e = find_entry(L, K);
   if (!e) return false;
@@ -719,6 +730,15 @@ bool plan_bwd_rows(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
         (e->loader == pt::LOAD_BULK1D && (static_cast<long long>(H) * L) % 4 == 0)))
     return false;
   return plan_exact(kPathBwdRows, B, H, L, K, di, *e, p) == PT_OK;
+}
+
+// The kernel pt_dx_dk runs at a shape (filling p): 1 the tensor-core fused
+// kernel, 2 the CUDA-core fused kernel, 0 pt_dx then pt_dk.
+int plan_backward(int B, int H, int L, int K, DeviceInfo& di, Plan& p) {
+  const int kind = bwd_choice(L, K).kernel;
+  if ((kind == PT_BWD_TENSOR_FUSED || kind == PT_BWD_ANY_FUSED) && plan_fused(B, H, L, K, di, p)) return 1;
+  if ((kind == PT_BWD_FFMA_FUSED || kind == PT_BWD_ANY_FUSED) && plan_bwd_rows(B, H, L, K, di, p)) return 2;
+  return 0;
 }
 
 int launch_bwd_rows(Plan& p, DeviceInfo& di, const float* dy, const float* x, const float* k, float* dx,
@@ -811,6 +831,10 @@ bool cfg_valid(int rows_per_tile, int stages, int ctas_per_sm, int threads_per_r
 // Validated copy of a caller's per-call options (null: nothing to copy).
 bool to_opts(const pt_launch_opts* o, Opts& out) {
   if (!o) return true;
+  if (o->bwd_kernel < PT_BWD_FROZEN || o->bwd_kernel > PT_BWD_ANY_FUSED) return false;
+  if (o->helper_channels < -1 || o->helper_channels > 1024) return false;
+  out.bwd_kernel = o->bwd_kernel;
+  out.helper_channels = o->helper_channels;
   for (int p = 0; p < 3; ++p) {
     if (o->engine[p] != -1 && o->engine[p] != PT_ENGINE_FFMA && o->engine[p] != PT_ENGINE_TENSOR) return false;
     out.engine[p] = o->engine[p];
@@ -938,8 +962,7 @@ int pt_dx_dk_fused(int B, int H, int L, int K) {
   DeviceInfo* di = nullptr;
   if (current_device(di) != PT_OK) return 0;
   Plan p;
-  if (plan_fused(B, H, L, K, *di, p)) return 1;
-  return plan_bwd_rows(B, H, L, K, *di, p) ? 2 : 0;
+  return plan_backward(B, H, L, K, *di, p);
 }
 
 size_t pt_dx_dk_workspace_bytes(int B, int H, int L, int K) {
@@ -947,8 +970,9 @@ size_t pt_dx_dk_workspace_bytes(int B, int H, int L, int K) {
   DeviceInfo* di = nullptr;
   if (current_device(di) != PT_OK) return 0;
   Plan p;
-  if (plan_fused(B, H, L, K, *di, p)) return fused_ws_bytes(p);
-  if (plan_bwd_rows(B, H, L, K, *di, p)) return dk_ws_bytes(p);
+  const int kind = plan_backward(B, H, L, K, *di, p);
+  if (kind == 1) return fused_ws_bytes(p);
+  if (kind == 2) return dk_ws_bytes(p);
   return pt_dk_workspace_bytes(B, H, L, K);
 }
 
@@ -964,7 +988,8 @@ int pt_dx_dk(const float* dy, const float* x, const float* k, float* dx, float* 
   DeviceInfo* di = nullptr;
   if ((rc = current_device(di)) != PT_OK) return rc;
   Plan p;
-  if (plan_fused(B, H, L, K, *di, p)) {
+  const int kind = plan_backward(B, H, L, K, *di, p);
+  if (kind == 1) {
     const size_t need = fused_ws_bytes(p);
     if (need > 0) {
       if (!ws || ws_bytes < need) return PT_ERR_WORKSPACE;
@@ -972,7 +997,7 @@ int pt_dx_dk(const float* dy, const float* x, const float* k, float* dx, float* 
     }
     return launch_fused(p, dy, x, k, dx, dk, mode, ws, di->err, static_cast<cudaStream_t>(stream_v));
   }
-  if (plan_bwd_rows(B, H, L, K, *di, p))
+  if (kind == 2)
     return launch_bwd_rows(p, *di, dy, x, k, dx, dk, mode, ws, ws_bytes, static_cast<cudaStream_t>(stream_v));
   if ((rc = pt_dx(dy, k, dx, B, H, L, K, stream_v)) != PT_OK) return rc;
   return pt_dk(dy, x, dk, B, H, L, K, mode, ws, ws_bytes, stream_v);
@@ -1067,7 +1092,7 @@ int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n) {
   if (rc != PT_OK) return rc;
   Plan p;
   if (path == PT_PATH_BWD_FUSED) {
-    if (!plan_fused(B, H, L, K, *di, p) && !plan_bwd_rows(B, H, L, K, *di, p)) return PT_ERR_UNSUPPORTED;
+    if (plan_backward(B, H, L, K, *di, p) == 0) return PT_ERR_UNSUPPORTED;
   } else if ((rc = plan(path, B, H, L, K, *di, p)) != PT_OK) {
     return rc;
   }

@@ -33,6 +33,18 @@ constexpr int kFrozenEngine[3][3] = {
     {0, 0, 0},  // DK: light, medium, heavy
 };
 
+// kFrozenBwd[class]: the kernel pt_dx_dk runs (PT_BWD_*) and the most channels
+// a helper CTA of the tensor-core fused kernel may own (0: no helpers).
+struct BwdChoice {
+  int kernel;
+  int helper_channels;
+};
+constexpr BwdChoice kFrozenBwd[3] = {
+    {3, 4},  // light
+    {3, 4},  // medium
+    {3, 4},  // heavy
+};
+
 constexpr const char* kFrozenCfgSource = "B200 sweep of preset pathtile-train (2 trials x 3 visits), global policy per path";
 
 }  // namespace pt

@@ -29,6 +29,16 @@ Modes:
              --engines, the engine table of an engine sweep goes into it too)
   regret     score the frozen policy on a held-out sweep against its per-shape oracle
   engines    engine sweep of one preset -> <out>/engines.csv, engine_policy.json
+  backward   backward-kernel sweep of one preset -> <out>/backward.csv; selects
+             the backward policy (backward_policy.json, --write-header puts it
+             into the header) or, with --bwd-policy, scores a frozen one
+
+The backward axis is the kernel pt_dx_dk runs -- dX then dK, the tensor-core
+fused kernel (with or without helper CTAs for the tail blocks: the most
+channels one helper may own), or the CUDA-core fused kernel -- frozen per
+intensity class as a policy (kernel mode, helper limit) with the same rule:
+the policy with the minimum summed latency over the class's tuning shapes,
+ties to the smaller policy.
 """
 from __future__ import annotations
 
@@ -389,6 +399,103 @@ def engine_regret(rows: list[dict], engines: dict[str, dict[str, str]]) -> list[
     return out
 
 
+# ---------------------------------------------------------------------------
+# Backward-kernel axis (pt_launch_opts.bwd_kernel / helper_channels)
+# ---------------------------------------------------------------------------
+BWD_KINDS = ("separate", "tensor_fused", "ffma_fused")
+HELPER_LIMITS = (0, 2, 4, 8)
+# Candidate policies (bwd_kernel, helper_channels): PT_BWD_SEPARATE,
+# PT_BWD_TENSOR_FUSED, PT_BWD_FFMA_FUSED, PT_BWD_ANY_FUSED.
+BWD_POLICIES = ([(0, 0)] + [(1, h) for h in HELPER_LIMITS] + [(2, 0)] + [(3, h) for h in HELPER_LIMITS])
+
+
+def bwd_policy_id(pol: tuple[int, int]) -> str:
+    return f"k{pol[0]}h{pol[1]}"
+
+
+def _bwd_rows_by_shape(rows: list[dict]) -> dict[str, dict]:
+    """config_id -> {"class": ..., "time": {policy: ms}} from backward-sweep rows
+    (one row per measured variant, listing the policies that run it)."""
+    shapes: dict[str, dict] = {}
+    for r in rows:
+        d = shapes.setdefault(r["config_id"], {"class": _class_of(r), "time": {}})
+        for pid in str(r["policies"]).split(";"):
+            if pid:
+                d["time"][pid] = float(r["mean_ms"])
+    return shapes
+
+
+def select_backward(rows: list[dict]) -> dict[str, tuple[int, int]]:
+    """Per intensity class, the policy with the minimum summed latency over the
+    class's shapes (ties to the smaller policy); policies missing any of the
+    class's shapes are not eligible; a class without shapes inherits from the
+    nearest class that has some (medium first)."""
+    shapes = _bwd_rows_by_shape(rows)
+    chosen: dict[str, tuple[int, int]] = {}
+    for cls in CLASSES:
+        members = [d for d in shapes.values() if d["class"] == cls]
+        if not members:
+            continue
+        totals = []
+        for pol in BWD_POLICIES:
+            pid = bwd_policy_id(pol)
+            if all(pid in d["time"] for d in members):
+                totals.append((sum(d["time"][pid] for d in members), pol))
+        if totals:
+            chosen[cls] = min(totals)[1]
+    for cls in CLASSES:
+        if cls not in chosen:
+            for alt in ("medium", "heavy", "light"):
+                if alt in chosen:
+                    chosen[cls] = chosen[alt]
+                    break
+    if not chosen:
+        raise ValueError("no backward-sweep rows to select from")
+    return chosen
+
+
+def backward_regret(rows: list[dict], policy: dict[str, tuple[int, int]]) -> list[dict]:
+    """Per shape: backward time of the frozen policy, of the per-shape best
+    variant, and of dX then dK."""
+    out = []
+    for cid, d in sorted(_bwd_rows_by_shape(rows).items()):
+        pid = bwd_policy_id(policy[d["class"]])
+        if pid not in d["time"]:
+            continue
+        frozen = d["time"][pid]
+        best = min(d["time"].values())
+        sep = d["time"].get(bwd_policy_id((0, 0)))
+        out.append({"config_id": cid, "class": d["class"], "frozen_ms": frozen, "best_ms": best,
+                    "separate_ms": sep, "regret_pct": 100.0 * (frozen / best - 1.0),
+                    "gain_vs_separate_pct": (100.0 * (sep / frozen - 1.0)) if sep else None})
+    return out
+
+
+def apply_backward_to_header(text: str, policy: dict[str, tuple[int, int]]) -> str:
+    """Rewrite only the kFrozenBwd table of an existing frozen-config header."""
+    start = text.index("constexpr BwdChoice kFrozenBwd[3] = {")
+    end = text.index("};", start) + 2
+    rows = ["constexpr BwdChoice kFrozenBwd[3] = {"]
+    for cls in CLASSES:
+        rows.append("    {%d, %d},  // %s" % (policy[cls][0], policy[cls][1], cls))
+    rows.append("};")
+    return text[:start] + "\n".join(rows) + text[end:]
+
+
+def _header_backward_block(text: str | None) -> list[str]:
+    """The kFrozenBwd block of an existing header (kept when the launch table is
+    rewritten), or the default: any fused kernel, helpers owning <= 4 channels."""
+    if text and "constexpr BwdChoice kFrozenBwd[3] = {" in text:
+        start = text.index("// kFrozenBwd[class]:")
+        end = text.index("};", text.index("constexpr BwdChoice kFrozenBwd[3] = {")) + 2
+        return text[start:end].split("\n")
+    return ["// kFrozenBwd[class]: the kernel pt_dx_dk runs (PT_BWD_*) and the most channels",
+            "// a helper CTA of the tensor-core fused kernel may own (0: no helpers).",
+            "struct BwdChoice {", "  int kernel;", "  int helper_channels;", "};",
+            "constexpr BwdChoice kFrozenBwd[3] = {", "    {3, 4},  // light", "    {3, 4},  // medium",
+            "    {3, 4},  // heavy", "};"]
+
+
 def render_header(policy: dict[str, dict[str, tuple[int, int, int]]], source: str,
                   engines: dict[str, dict[str, str]] | None = None) -> str:
     lines = [
@@ -425,7 +532,9 @@ def render_header(policy: dict[str, dict[str, tuple[int, int, int]]], source: st
     for p, name in zip(PATHS, ("FWD", "DX", "DK")):
         cells = ", ".join(str(ENGINES.index(engines[p][c]) if engines else 0) for c in CLASSES)
         lines.append(f"    {{{cells}}},  // {name}: light, medium, heavy")
-    lines += ["};", "", f'constexpr const char* kFrozenCfgSource = "{source}";', "", "}  // namespace pt", ""]
+    lines += ["};", ""]
+    lines += _header_backward_block(HEADER.read_text() if HEADER.exists() else None)
+    lines += ["", f'constexpr const char* kFrozenCfgSource = "{source}";', "", "}  // namespace pt", ""]
     return "\n".join(lines)
 
 
@@ -637,6 +746,74 @@ def run_engine_sweep(cases: list[ShapeCase], warmup: int, runs: int, seed: int, 
     return rows
 
 
+def run_backward_sweep(cases: list[ShapeCase], warmup: int, runs: int, seed: int, out: Path,
+                       reps: int = 3) -> list[dict]:
+    """Per shape: every distinct backward variant the candidate policies lead
+    to (kernel kind and grid, as the library reports them for that policy) is
+    checked against dX then dK on the same inputs and timed (per-launch CUDA
+    events, visits alternating between variants; figure = median over visits of
+    the per-visit mean)."""
+    import torch
+
+    from . import _lib, ops
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    out.mkdir(parents=True, exist_ok=True)
+    stream = torch.cuda.current_stream()
+    rows = []
+    for case in cases:
+        B, H, L, K = case.B, case.H, case.L, case.K
+        sd = case_seed(seed, case)
+        x, k, dy = _make_inputs(case, sd, B, dev)
+        variants: dict[tuple, tuple] = {}
+        for pol in BWD_POLICIES:
+            o = _lib.LaunchOpts.frozen()
+            o.bwd_kernel, o.helper_channels = pol
+            kind = ops.backward_kind(B, H, L, K, opts=o)
+            grid = ops.kernel_info("bwd_fused", B, H, L, K, opts=o)["grid"] if kind != "separate" else 0
+            variants.setdefault((kind, grid), (o, []))[1].append(bwd_policy_id(pol))
+        sep = _lib.LaunchOpts.frozen()
+        sep.bwd_kernel = _lib.PT_BWD_SEPARATE
+        gk0 = torch.empty_like(k)
+        gx0 = ops.dx_dk(dy, x, k, gk0, opts=sep)
+        gx, gk = torch.empty_like(x), torch.empty_like(k)
+        err = {}
+        for key, (o, _) in variants.items():
+            ops.dx_dk(dy, x, k, gk, gx=gx, opts=o)
+            err[key] = max(float((gx - gx0).abs().max() / gx0.abs().max().clamp_min(1e-30)),
+                           float((gk - gk0).abs().max() / gk0.abs().max().clamp_min(1e-30)))
+        assert ops.device_error() == 0, f"{case.config_id}: a kernel wait expired"
+        keys = [kk for kk in variants if err[kk] <= 1e-4]
+        visits: dict[tuple, list[float]] = {}
+        for rep in range(reps):
+            for key in (keys if rep % 2 == 0 else list(reversed(keys))):
+                o = variants[key][0]
+                for _ in range(warmup):
+                    ops.dx_dk(dy, x, k, gk, gx=gx, opts=o)
+                ev = []
+                for _ in range(runs):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record(stream)
+                    ops.dx_dk(dy, x, k, gk, gx=gx, opts=o)
+                    b.record(stream)
+                    ev.append((a, b))
+                torch.cuda.synchronize()
+                visits.setdefault(key, []).append(statistics.mean(a.elapsed_time(b) for a, b in ev))
+        for key, (o, pids) in variants.items():
+            rows.append({"config_id": case.config_id, "B": B, "H": H, "L": L, "K": K,
+                         "class": intensity_class(L, K), "variant": key[0], "grid": key[1],
+                         "policies": ";".join(pids), "max_norm_err": err[key], "valid": err[key] <= 1e-4,
+                         "mean_ms": statistics.median(visits[key]) if key in visits else float("nan"),
+                         "visits": len(visits.get(key, []))})
+        print(json.dumps({"config_id": case.config_id,
+                          **{f"{kk[0]}@{kk[1]}": round(statistics.median(v), 4) for kk, v in visits.items()}}),
+              flush=True)
+        del x, k, dy, gx, gx0
+        torch.cuda.empty_cache()
+    _write_csv(out / "backward.csv", rows)
+    return rows
+
+
 def apply_engines_to_header(text: str, engines: dict[str, dict[str, str]]) -> str:
     """Rewrite only the kFrozenEngine table of an existing frozen-config header."""
     start = text.index("constexpr int kFrozenEngine[3][3] = {")
@@ -684,7 +861,8 @@ def aggregate_trials(root: Path) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--mode", choices=("run", "aggregate", "regret", "engines", "baselines"), required=True)
+    ap.add_argument("--mode", choices=("run", "aggregate", "regret", "engines", "baselines", "backward"),
+                    required=True)
     ap.add_argument("--preset", default="pathtile-train", choices=sorted(PRESETS))
     ap.add_argument("--out", type=Path, required=True, help="results directory of this preset")
     ap.add_argument("--trial", type=int, default=1)
@@ -697,6 +875,7 @@ def main() -> None:
     ap.add_argument("--per-class", action="store_true", help="aggregate: select per intensity class")
     ap.add_argument("--policy", type=Path, help="regret: frozen_config.json to score")
     ap.add_argument("--engines", type=Path, help="aggregate: engine_policy.json to include in the header")
+    ap.add_argument("--bwd-policy", type=Path, help="backward: backward_policy.json to score instead of selecting")
     ap.add_argument("--train-csv", type=Path, help="baselines: candidate summary of the tuning shapes")
     ap.add_argument("--eval-csv", type=Path, help="baselines: candidate summary of the shapes to score "
                     "(default: aggregate the trials under --out)")
@@ -709,6 +888,31 @@ def main() -> None:
         _write_csv(args.out / "selector_baselines_per_shape.csv", rows)
         (args.out / "selector_baselines_summary.json").write_text(json.dumps(summary, indent=1))
         print(json.dumps(summary, indent=1))
+        return
+    if args.mode == "backward":
+        rows = [r for r in run_backward_sweep(cases_for_preset(args.preset), args.warmup, args.runs, args.seed,
+                                              args.out, reps=args.reps) if r["valid"]]
+        if args.bwd_policy:
+            pol = {c: tuple(v) for c, v in json.loads(args.bwd_policy.read_text())["policy"].items()}
+        else:
+            pol = select_backward(rows)
+        reg = backward_regret(rows, pol)
+        gains = [r["gain_vs_separate_pct"] for r in reg if r["gain_vs_separate_pct"] is not None]
+        doc = {"policy": {c: list(v) for c, v in pol.items()},
+               "policy_meaning": "[bwd_kernel (0 separate, 1 tensor-core fused, 2 CUDA-core fused, 3 any fused), "
+                                 "most channels per helper CTA (0: none)]",
+               "preset": args.preset, "selected_here": args.bwd_policy is None,
+               "shapes": len(reg),
+               "regret_pct_mean": statistics.mean(r["regret_pct"] for r in reg) if reg else None,
+               "regret_pct_max": max(r["regret_pct"] for r in reg) if reg else None,
+               "within_2pct": sum(r["regret_pct"] <= 2.0 for r in reg),
+               "gain_vs_separate_pct_mean": statistics.mean(gains) if gains else None}
+        _write_csv(args.out / "backward_regret.csv", reg)
+        (args.out / ("backward_policy.json" if args.bwd_policy is None else "backward_scored.json")).write_text(
+            json.dumps(doc, indent=1))
+        print(json.dumps(doc, indent=1))
+        if args.write_header and args.bwd_policy is None:
+            HEADER.write_text(apply_backward_to_header(HEADER.read_text(), pol))
         return
     if args.mode == "engines":
         rows = run_engine_sweep(cases_for_preset(args.preset), args.warmup, args.runs, args.seed, args.out,

@@ -104,6 +104,12 @@ def test_per_call_options_validation_and_effect(native_lib):
     assert native_lib.pt_dx_ex(FAKE, FAKE, FAKE, 2, 4, 16, 8, pe, NULL) == _lib.PT_ERR_ARGS
     out = (ctypes.c_int * 7)()
     assert native_lib.pt_config_ex(0, 16, 4, 16, 8, out, 7, pe) == _lib.PT_ERR_ARGS
+    bk = _lib.LaunchOpts.frozen()
+    bk.bwd_kernel = 4
+    pk = ctypes.cast(ctypes.pointer(bk), ctypes.c_void_p)
+    assert native_lib.pt_dx_dk_ex(FAKE, FAKE, FAKE, FAKE, FAKE, 2, 4, 16, 8, 1, NULL, 0, pk, NULL) == _lib.PT_ERR_ARGS
+    bk.bwd_kernel, bk.helper_channels = _lib.PT_BWD_SEPARATE, -2
+    assert native_lib.pt_dx_dk_ex(FAKE, FAKE, FAKE, FAKE, FAKE, 2, 4, 16, 8, 1, NULL, 0, pk, NULL) == _lib.PT_ERR_ARGS
 
 
 def test_runtime_launch_options_map_reference_arguments():

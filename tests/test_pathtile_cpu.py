@@ -238,3 +238,48 @@ def test_host_cpu_mask_and_numa_binding_restore(monkeypatch):
     with host.near_device(0) as cpus:
         assert cpus == [] and os.sched_getaffinity(0) == before
     assert os.sched_getaffinity(0) == before
+
+
+# ---------------- backward-kernel axis ----------------
+def _bwd_row(cid, L, K, variant, policies, ms):
+    return {"config_id": cid, "L": L, "K": K, "variant": variant, "policies": ";".join(policies), "mean_ms": ms}
+
+
+def test_backward_policy_selection_and_regret():
+    from pathtile_b200 import pathtile as pt
+
+    sep, tf0, tf4, ff = "k0h0", "k1h0", "k1h4", "k2h0"
+    any0, any4 = "k3h0", "k3h4"
+    rows = [
+        # heavy shape A: tensor fused best with helpers
+        _bwd_row("A", 48, 48, "separate", [sep, ff], 3.0),
+        _bwd_row("A", 48, 48, "tensor_fused", [tf0, any0], 2.0),
+        _bwd_row("A", 48, 48, "tensor_fused", ["k1h2", tf4, "k1h8", "k3h2", any4, "k3h8"], 1.5),
+        # heavy shape B: helpers slower
+        _bwd_row("B", 48, 48, "separate", [sep, ff], 3.0),
+        _bwd_row("B", 48, 48, "tensor_fused", [tf0, any0, "k1h2", "k3h2"], 2.0),
+        _bwd_row("B", 48, 48, "tensor_fused", [tf4, "k1h8", any4, "k3h8"], 2.2),
+        # light shape: only the CUDA-core fused kernel or separate
+        _bwd_row("C", 16, 4, "separate", [sep, tf0, "k1h2", tf4, "k1h8"], 1.0),
+        _bwd_row("C", 16, 4, "ffma_fused", [ff, any0, "k3h2", any4, "k3h8"], 0.7),
+    ]
+    pol = pt.select_backward(rows)
+    # heavy: totals k1h2/k3h2 = 1.5 + 2.0 = 3.5 (the smallest; ties -> smaller tuple k1h2)
+    assert pol["heavy"] == (1, 2)
+    # light: any-fused policies 0.7; the smallest tuple among them is (2, 0)
+    assert pol["light"] == (2, 0)
+    assert pol["medium"] == pol["heavy"]  # no medium shape: inherits
+    reg = {r["config_id"]: r for r in pt.backward_regret(rows, pol)}
+    assert reg["A"]["regret_pct"] == 0.0 and reg["B"]["regret_pct"] == 0.0
+    assert abs(reg["C"]["gain_vs_separate_pct"] - 100 * (1.0 / 0.7 - 1)) < 1e-9
+
+
+def test_backward_header_rewrite_keeps_the_rest():
+    from pathtile_b200 import pathtile as pt
+
+    text = pt.HEADER.read_text()
+    new = pt.apply_backward_to_header(text, {"light": (2, 0), "medium": (3, 4), "heavy": (1, 0)})
+    assert "    {2, 0},  // light" in new and "    {1, 0},  // heavy" in new
+    assert new.replace("{2, 0},  // light", "").count("kFrozenCfg[3][3]") == text.count("kFrozenCfg[3][3]")
+    # The full header renderer keeps the backward table of the existing header.
+    assert "kFrozenBwd" in pt.render_header({p: {c: (128, 3, 2, 1) for c in pt.CLASSES} for p in pt.PATHS}, "x")
