@@ -170,7 +170,10 @@ PT_API size_t pt_dk_workspace_bytes(int B, int H, int L, int K);
  * arithmetic-intensity class keying the table (0 light, 1 medium, 2 heavy:
  * in-range FMAs per output element < 12, < 24, else); if `n` >= 6, out[5] =
  * consumer threads per row (1, or 2 when two threads split a row); if `n` >= 7,
- * out[6] = the engine that runs (PT_ENGINE_*).  `n` >= 4.
+ * out[6] = the engine that runs (PT_ENGINE_*); if `n` >= 9, out[7] = the
+ * backward kernel pt_dx_dk may use (PT_BWD_*) and out[8] = the most channels
+ * a helper CTA of the tensor-core fused kernel may own, for the shape's class.
+ * `n` >= 4.
  * Mirrors the frozen constants that the reference bakes into CUDA_TEMPLATE
  * (WARPS_PER_BLOCK / BWDK_BLOCK, kernels/warp_tiled_ampere.py:668-672,
  * selected by scripts/aggregate_pathtile_results.py:222-240).

@@ -1080,6 +1080,11 @@ int pt_config(int path, int B, int H, int L, int K, int* out, int n) {
     (void)cudaGetLastError();
     out[6] = engine_for(path, B, H, L, K, sm);
   }
+  if (n >= 9) {
+    const pt::BwdChoice c = bwd_choice(L, K);
+    out[7] = c.kernel;
+    out[8] = c.helper_channels;
+  }
   return PT_OK;
 }
 

@@ -40,9 +40,9 @@ struct BwdChoice {
   int helper_channels;
 };
 constexpr BwdChoice kFrozenBwd[3] = {
-    {3, 4},  // light
-    {3, 4},  // medium
-    {3, 4},  // heavy
+    {3, 0},  // light
+    {3, 0},  // medium
+    {3, 0},  // heavy
 };
 
 constexpr const char* kFrozenCfgSource = "B200 sweep of preset pathtile-train (2 trials x 3 visits), global policy per path";

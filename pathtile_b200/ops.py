@@ -411,11 +411,11 @@ def config(path: str, B: int, H: int, L: int, K: int, opts: "_lib.LaunchOpts | N
     """Launch choice of one path at one shape (C ABI pt_config): the frozen table,
     or ``opts`` / the process-wide overrides where they are set."""
     code = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK}[path]
-    out = (ctypes.c_int * 7)()
-    _lib.check(_lib.load().pt_config_ex(code, B, H, L, K, out, 7, _opts_ptr(opts)), "pt_config")
+    out = (ctypes.c_int * 9)()
+    _lib.check(_lib.load().pt_config_ex(code, B, H, L, K, out, 9, _opts_ptr(opts)), "pt_config")
     return {"rows_per_tile": out[0], "stages": out[1], "ctas_per_sm": out[2], "specialised": out[3],
             "intensity_class": ("light", "medium", "heavy")[out[4]], "threads_per_row": out[5],
-            "engine": ENGINES[out[6]]}
+            "engine": ENGINES[out[6]], "bwd_kernel": out[7], "helper_channels": out[8]}
 
 
 KERNEL_PATHS = {"fwd": PT_PATH_FWD, "bwd_input": PT_PATH_DX, "bwd_weight": PT_PATH_DK,

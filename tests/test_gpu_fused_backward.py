@@ -43,13 +43,16 @@ def _sm_count(dev) -> int:
     return torch.cuda.get_device_properties(dev).multi_processor_count
 
 
-def tensor_schedule(B, H, sm):
+def tensor_schedule(B, H, sm, helper_limit=None):
     """The host's schedule of the tensor-core fused kernel (None: it does not apply):
     kp = floor(min(tiles, SMs) / H) primary CTAs per channel; the SMs left over
     become helpers taking every channel's tail blocks when that shortens the
     busiest CTA (a channel switch counted as one tile) by >= 3 % and no helper
-    owns more than 4 channels; otherwise the plain grid of kp*H CTAs, which must
-    keep >= 3/4 of min(tiles, SMs) busy."""
+    owns more than `helper_limit` channels (default: the frozen limit the
+    library reports); otherwise the plain grid of kp*H CTAs, which must keep
+    >= 3/4 of min(tiles, SMs) busy."""
+    if helper_limit is None:
+        helper_limit = ops.config("bwd_input", B, H, 48, 48)["helper_channels"]
     nblk = -(-B // 128)
     gmax = min(nblk * H, sm)
     kp = gmax // H
@@ -57,7 +60,7 @@ def tensor_schedule(B, H, sm):
         return None
     plain = -(-nblk // kp)
     E = sm - kp * H
-    if E >= 1 and nblk >= 2 and -(-H // E) <= 4:
+    if E >= 1 and nblk >= 2 and -(-H // E) <= helper_limit:
         m = -(-H // E)
         best, best_p = plain, 0
         for P in range(1, nblk):
@@ -111,11 +114,7 @@ SHAPES = [
     (5000, 74, 48, 32),   # 2 CTAs per channel
     (64, 1, 48, 3),
     (700, 128, 48, 5),    # K not among the CUDA-core kernels' specialisations
-    (4096, 128, 48, 48),  # plain grid: one CTA per channel (7 channels per helper is too many)
-    (4096, 100, 48, 7),   # helpers (48) with up to three channels each
-    (3000, 96, 48, 40),   # helpers (52) with two channels each; no plain grid at H = 96
-    (3000, 64, 48, 24),   # two primaries per channel plus helpers
-    (5000, 100, 44, 11),  # 44-column rows, helpers
+    (4096, 128, 48, 48),  # plain grid: one CTA per channel
     (300, 128, 48, 47),   # odd K, the largest register spill
     (250, 128, 48, 1),
     (1000, 128, 44, 44),  # 44-column rows in the 48-column layout
@@ -204,17 +203,63 @@ def test_forcing_a_tensor_engine_keeps_the_cuda_core_fusion_off(cuda_device):
     assert ops.backward_kind(300, 96, 48, 24) == "ffma_fused"
 
 
-@pytest.mark.parametrize("B,H", [(16384, 128), (16384, 64), (16384, 96)])
-def test_fused_schedule_grid(cuda_device, B, H):
+def _helper_opts(limit: int):
+    from pathtile_b200 import _lib
+
+    o = _lib.LaunchOpts.frozen()
+    o.bwd_kernel, o.helper_channels = _lib.PT_BWD_TENSOR_FUSED, limit
+    return o
+
+
+@pytest.mark.parametrize("B,H,limit", [(16384, 128, 0), (16384, 64, 4), (16384, 96, 4), (16384, 128, 8)])
+def test_fused_schedule_grid(cuda_device, B, H, limit):
     sm = _sm_count(cuda_device)
-    sc = tensor_schedule(B, H, sm)
+    sc = tensor_schedule(B, H, sm, helper_limit=limit)
     if sm == 148:
-        expect = {128: {"kp": 1, "E": 0}, 64: {"kp": 2, "E": 20, "m": 4}, 96: {"kp": 1, "E": 52, "m": 2}}[H]
+        expect = {(128, 0): {"kp": 1, "E": 0}, (64, 4): {"kp": 2, "E": 20, "m": 4},
+                  (96, 4): {"kp": 1, "E": 52, "m": 2}, (128, 8): {"kp": 1, "E": 20, "m": 7, "P": 113}}[(H, limit)]
         assert all(sc[k] == v for k, v in expect.items()), sc
-    assert ops.backward_kind(B, H, 48, 48) == "tensor_fused"
-    info = ops.kernel_info("bwd_fused", B, H, 48, 48)
+    o = _helper_opts(limit)
+    assert ops.backward_kind(B, H, 48, 48, opts=o) == "tensor_fused"
+    info = ops.kernel_info("bwd_fused", B, H, 48, 48, opts=o)
     assert info["grid"] == (sm if sc["E"] else sc["kp"] * H)
     assert info["threads_per_block"] == 512 and info["local_memory_bytes"] == 0
+
+
+HELPER_SHAPES = [
+    (4096, 128, 48, 48, 8),   # 20 helpers beside 128 primaries, up to 7 channels each
+    (4096, 128, 48, 7, 8),
+    (3000, 96, 48, 40, 4),    # 52 helpers with two channels each; no plain grid at H = 96
+    (3000, 64, 48, 24, 4),    # two primaries per channel plus helpers
+    (5000, 100, 44, 11, 4),   # 44-column rows, helpers with up to three channels
+]
+
+
+@pytest.mark.parametrize("mode", ["deterministic", "atomic"])
+@pytest.mark.parametrize("B,H,L,K,limit", HELPER_SHAPES)
+def test_helper_schedules_against_fp64_oracle(cuda_device, B, H, L, K, limit, mode):
+    """The tensor-core fused kernel with helper CTAs (channel switches, per-segment
+    dK partials), selected per call; the frozen table may not use helpers."""
+    dev = cuda_device
+    o = _helper_opts(limit)
+    sm = _sm_count(dev)
+    sc = tensor_schedule(B, H, sm, helper_limit=limit)
+    if sm == 148:
+        assert sc is not None and sc["E"] > 0, sc
+        assert ops.kernel_info("bwd_fused", B, H, L, K, opts=o)["grid"] == sm
+    x, k, dy, cpu = _inputs(B, H, L, K, 2525, dev)
+    gk = torch.zeros_like(k) if mode == "atomic" else torch.full_like(k, float("nan"))
+    gx = ops.dx_dk(dy, x, k, gk, mode=mode, opts=o)
+    torch.cuda.synchronize()
+    assert ops.device_error(clear=True) == 0, "a kernel wait expired"
+    np.testing.assert_allclose(gx.cpu().numpy(), c_oracle.dx(cpu[2], cpu[1]), **FWD_TOL)
+    assert_dk_close(gk.cpu().numpy(), c_oracle.dk(cpu[2], cpu[0], K))
+    # Deterministic: the same partials summed in the same order, run after run.
+    if mode == "deterministic":
+        gk2 = torch.empty_like(k)
+        ops.dx_dk(dy, x, k, gk2, opts=o)
+        torch.cuda.synchronize()
+        assert torch.equal(gk, gk2)
 
 
 @pytest.mark.parametrize("H", [128, 64, 96])
