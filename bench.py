@@ -292,18 +292,27 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     stream = torch.cuda.current_stream(dev)
 
     fused = args.backward == "fused"
+    # N > 1: dK summed over the ranks through the peers' exchange buffers (inside
+    # the fused backward kernel where it applies), or by an NCCL all-reduce.
+    exchange = None
+    if dist is not None and args.collective == "fused":
+        from pathtile_b200.distributed import PeerExchange, dx_dk_allreduce, peer_fused
 
-    def compute():
+        exchange = PeerExchange(H, K, dev)
+
+    def compute(nccl: bool = False):
         ops.fwd(x, k, y)
-        if fused:
+        if exchange is not None and not nccl:
+            dx_dk_allreduce(dy, x, k, gk, exchange, gx=gx)
+        elif fused:
             ops.dx_dk(dy, x, k, gk, gx=gx, mode="deterministic")
         else:
             ops.dx(dy, k, gx)
             ops.dk(dy, x, gk, mode="deterministic")
 
-    def step():
-        compute()
-        if dist is not None:
+    def step(nccl: bool = False):
+        compute(nccl)
+        if dist is not None and (exchange is None or nccl):
             dist.all_reduce(gk)
 
     for _ in range(args.warmup):
@@ -321,7 +330,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s_ev.record(stream)
         for _ in range(args.steps):
-            if dist is None:
+            if dist is None or exchange is not None:
                 step()
                 continue
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
@@ -336,12 +345,32 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         step_ms = s_ev.elapsed_time(e_ev) / args.steps
     split = None
     if dist is not None:
+        if exchange is not None:
+            # The same step with the NCCL all-reduce after the backward, for comparison.
+            for _ in range(args.warmup):
+                step(nccl=True)
+            torch.cuda.synchronize()
+            dist.barrier()
+            for _ in range(args.steps):
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                ev[0].record(stream)
+                compute(nccl=True)
+                ev[1].record(stream)
+                dist.all_reduce(gk)
+                ev[2].record(stream)
+                marks.append(ev)
+            torch.cuda.synchronize()
+        nccl_step = statistics.mean(a.elapsed_time(c) for a, _, c in marks)
         comp = statistics.mean(a.elapsed_time(b) for a, b, _ in marks)
         red = statistics.mean(b.elapsed_time(c) for _, b, c in marks)
-        t = torch.tensor([step_ms, comp, red], device=dev, dtype=torch.float64)
+        t = torch.tensor([step_ms, comp, red, nccl_step], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_ms, comp, red = map(float, t.tolist())
-        split = {"compute_ms": comp, "allreduce_ms": red}
+        step_ms, comp, red, nccl_step = map(float, t.tolist())
+        split = {"collective": ("dK summed inside the backward kernel through the peers' memory (NVLink)"
+                                if exchange is not None and peer_fused(B, H, L, K) else
+                                "peer-memory sum kernel after the backward" if exchange is not None else
+                                "NCCL all_reduce after the backward"),
+                 "nccl_variant": {"step_ms": nccl_step, "compute_ms": comp, "allreduce_ms": red}}
 
     # Per-phase times under the reference protocol, each phase timed separately.
     # Outputs exist already; the dK workspace is allocated by a call outside the
@@ -377,6 +406,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     if args.no_e2e:
         err = ops.device_error()
+        if exchange is not None:
+            exchange.close()
         if rank == 0:
             print(json.dumps({"profile_run": True, "B": B, "ms_per_step": step_ms, "phase_ms": phase_ms,
                               "device_error_word": err}), flush=True)
@@ -417,6 +448,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     h2d, d2h = pipe.bytes_per_call(B)
     err = ops.device_error()
     numa.close()
+    if exchange is not None:
+        exchange.close()
 
     if rank != 0:
         return None
@@ -464,7 +497,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "config": {
             "workload": "primary: B=16384 per GPU, H=128, L=48, K=48 (N=8: batch-sharded x[131072,128,48])",
             "B_per_gpu": B, "global_batch": B * world, "H": H, "L": L, "K": K,
-            "parallelism": f"dp{world}" + (" + NCCL all_reduce(dK)" if world > 1 else ""),
+            "parallelism": f"dp{world}" + ((" + dK summed over NVLink peer memory" if exchange is not None
+                                             else " + NCCL all_reduce(dK)") if world > 1 else ""),
             "dk_mode": "deterministic",
             "backward": ("fused dX+dK kernel (ops.dx_dk)" if fused_on else "dX then dK"),
             "engines": engines,
@@ -709,6 +743,8 @@ def main() -> None:
                     help="backward of the step: ops.dx_dk (one fused kernel where it applies) or dX then dK")
     ap.add_argument("--engine", choices=("frozen", "ffma", "tensor"), default="frozen",
                     help="kernels to run: the frozen per-shape table (default), or force one engine")
+    ap.add_argument("--collective", choices=("fused", "nccl"), default="fused",
+                    help="N > 1: sum dK through the peers' memory inside the backward (default) or NCCL all_reduce")
     ap.add_argument("--workload", choices=("primary", "s4-train"), default="primary",
                     help="s4-train: time the S4ConvD training step instead (single GPU)")
     args = ap.parse_args()

@@ -269,12 +269,54 @@ PT_API int pt_kernel_info(int path, int B, int H, int L, int K, int* out, int n)
  * consumer waited for a tile, bit 1 the producer waited for an in-flight copy
  * to drain, bit 2 the producer waited for consumers to finish a stage; the
  * tensor-core kernels add bit 3 (converter waits), bit 4 (MMA issuer waits) and
- * bit 5 (epilogue waits).  Reads (and
+ * bit 5 (epilogue waits); bit 6 a peer's dK row never arrived (pt_dx_dk_allreduce).  Reads (and
  * with clear != 0, resets) the word of the current device; synchronises the
  * device.  The reference has no device-side error channel (its kernels return
  * silently on L > 48, kernels/warp_tiled_ampere.py:390).
  */
 PT_API int pt_device_error(unsigned int* out, int clear);
+
+/*
+ * Data-parallel step on the GPUs of one node: each rank has dK of its batch
+ * shard; these entry points sum dK over the ranks through the other GPUs'
+ * memory (NVLink / NVSwitch), the counterpart of the step's NCCL all-reduce
+ * (the reference is single-GPU; no counterpart there).  Each rank owns an
+ * exchange buffer of pt_peer_buffer_bytes(world, H, K) (pt_peer_alloc: device
+ * memory, zeroed) and maps every other rank's (pt_ipc_export on the owner,
+ * pt_ipc_import on the others, the 64-byte handles exchanged by the caller,
+ * e.g. torch.distributed).  pt_peer_group lists the buffers as mapped in this
+ * process (bufs[rank] = the own one) and an epoch that the caller increases by
+ * one for every call, identically on all ranks, starting at 1.  Every rank must
+ * make the same calls in the same order; a rank whose peers do not arrive within
+ * 2 s sets bit 6 (value 64) of the device error word and leaves dk unsummed.
+ *
+ * pt_dx_dk_allreduce: pt_dx_dk (deterministic: dk = dK) with dk summed over the
+ * ranks; where the tensor-core fused kernel runs with one CTA per channel
+ * (pt_dx_dk_allreduce_fused = 1), the CTA that computed a channel's row sends
+ * it to every rank and sums the ranks' rows in its epilogue -- no separate
+ * collective; otherwise pt_dx_dk then pt_allreduce_peer.  pt_allreduce_peer:
+ * dk[H][K] summed over the ranks in place.  Sums run in rank order on every
+ * rank, so all ranks hold the same bits.
+ */
+#define PT_MAX_PEERS 8
+#define PT_IPC_HANDLE_BYTES 64
+typedef struct pt_peer_group {
+  int rank;
+  int world;
+  void* bufs[PT_MAX_PEERS];
+  unsigned int epoch;
+} pt_peer_group;
+
+PT_API size_t pt_peer_buffer_bytes(int world, int H, int K);
+PT_API int pt_peer_alloc(size_t bytes, void** ptr);
+PT_API int pt_peer_free(void* ptr);
+PT_API int pt_ipc_export(const void* ptr, void* handle);
+PT_API int pt_ipc_import(const void* handle, void** ptr);
+PT_API int pt_ipc_close(void* ptr);
+PT_API int pt_dx_dk_allreduce(const float* dy, const float* x, const float* k, float* dx, float* dk, int B, int H,
+                              int L, int K, void* ws, size_t ws_bytes, const pt_peer_group* grp, void* stream);
+PT_API int pt_dx_dk_allreduce_fused(int B, int H, int L, int K);
+PT_API int pt_allreduce_peer(float* dk, int H, int K, const pt_peer_group* grp, void* stream);
 
 /*
  * Self-test of the device-side wait limit (test use): launches one warp that

@@ -44,6 +44,8 @@ PT_BWD_ANY_FUSED = 3
 
 PT_MAX_L = 48
 PT_MAX_K = 48
+PT_MAX_PEERS = 8
+PT_IPC_HANDLE_BYTES = 64
 
 
 class LaunchOpts(ctypes.Structure):
@@ -70,6 +72,18 @@ class LaunchOpts(ctypes.Structure):
         o.bwd_kernel = PT_BWD_FROZEN
         o.helper_channels = -1
         return o
+
+
+class PeerGroup(ctypes.Structure):
+    """``pt_peer_group``: this rank, the number of ranks, every rank's exchange
+    buffer as mapped into this process, and the call's epoch."""
+
+    _fields_ = [
+        ("rank", ctypes.c_int),
+        ("world", ctypes.c_int),
+        ("bufs", ctypes.c_void_p * PT_MAX_PEERS),
+        ("epoch", ctypes.c_uint),
+    ]
 
 
 # Every symbol include/pathtile_b200.h declares, with (restype, argtypes).
@@ -107,6 +121,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_kernel_info_ex": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int), _c_int,
                                    _vp]),
     "pt_selftest_wait_timeout": (_c_int, [ctypes.c_ulonglong, _vp, _vp]),
+    "pt_peer_buffer_bytes": (_c_size, [_c_int, _c_int, _c_int]),
+    "pt_peer_alloc": (_c_int, [_c_size, ctypes.POINTER(ctypes.c_void_p)]),
+    "pt_peer_free": (_c_int, [_vp]),
+    "pt_ipc_export": (_c_int, [_vp, _vp]),
+    "pt_ipc_import": (_c_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "pt_ipc_close": (_c_int, [_vp]),
+    "pt_dx_dk_allreduce": (_c_int, [_fp, _fp, _fp, _fp, _fp, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp,
+                                    _vp]),
+    "pt_dx_dk_allreduce_fused": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
+    "pt_allreduce_peer": (_c_int, [_fp, _c_int, _c_int, _vp, _vp]),
 }
 
 _lock = threading.Lock()

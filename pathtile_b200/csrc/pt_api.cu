@@ -15,6 +15,7 @@
 #include "pt_cl.h"
 #include "pt_frozen_config.h"
 #include "pt_kernels.cuh"
+#include "pt_peer.cuh"
 #include "pt_registry.h"
 #include "pt_tc.h"
 
@@ -682,7 +683,7 @@ size_t fused_ws_bytes(const Plan& p) {
 }
 
 int launch_fused(const Plan& p, const float* dy, const float* x, const float* k, float* dx, float* dk,
-                 int mode, void* ws, unsigned* err, cudaStream_t stream) {
+                 int mode, void* ws, unsigned* err, cudaStream_t stream, const pt::PeerArgs* peers = nullptr) {
   const pt::TileGeom& g = p.g;
   CUtensorMap dy128, dy64, x128, x64, dx128, dx64;
   int rc = PT_OK;
@@ -696,8 +697,11 @@ int launch_fused(const Plan& p, const float* dy, const float* x, const float* k,
   int accumulate = (mode == PT_DK_DETERMINISTIC) ? 0 : 1;  // atomic and *_ACCUMULATE add to dk
   float* part = sc.direct ? nullptr : static_cast<float*>(ws);
   int acc_k = sc.direct ? accumulate : 0;
+  pt::PeerArgs pa{};
+  pa.world = 1;
+  if (peers && sc.direct) pa = *peers;
   void* args[] = {&dy128, &dy64, &x128, &x64, &dx128, &dx64, const_cast<float**>(&k), &part, &dk,
-                  &sc, &acc_k, &err};
+                  &sc, &acc_k, &pa, &err};
   cudaError_t ce = cudaLaunchKernel(p.func, dim3(g.G), dim3(p.threads), args, p.smem, stream);
   if (ce != cudaSuccess) return cuda_fail(ce);
   if (!sc.direct) {
@@ -1223,6 +1227,131 @@ int pt_kernel_info_ex(int path, int B, int H, int L, int K, int* out, int n, con
   if (!to_opts(o, op)) return PT_ERR_ARGS;
   OptsScope scope(o ? &op : nullptr);
   return pt_kernel_info(path, B, H, L, K, out, n);
+}
+
+// ---------------- dK summed over the ranks through peer memory ----------------
+size_t pt_peer_buffer_bytes(int world, int H, int K) {
+  if (world < 1 || world > PT_MAX_PEERS || H < 1 || K < 1 || K > PT_MAX_K) return 0;
+  const size_t data = 2ull * world * H * K * sizeof(float);
+  const size_t flags = 2ull * world * H * sizeof(unsigned);
+  return (data + 255) / 256 * 256 + (flags + 255) / 256 * 256;
+}
+
+int pt_peer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return PT_ERR_ARGS;
+  *ptr = nullptr;
+  DeviceInfo* di = nullptr;
+  int rc = current_device(di);
+  if (rc != PT_OK) return rc;
+  void* p = nullptr;
+  cudaError_t ce = cudaMalloc(&p, bytes);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  if ((ce = cudaMemset(p, 0, bytes)) != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(ce);
+  }
+  *ptr = p;
+  return PT_OK;
+}
+
+int pt_peer_free(void* ptr) {
+  if (!ptr) return PT_OK;
+  const cudaError_t ce = cudaFree(ptr);
+  return ce == cudaSuccess ? PT_OK : cuda_fail(ce);
+}
+
+int pt_ipc_export(const void* ptr, void* handle) {
+  if (!ptr || !handle) return PT_ERR_ARGS;
+  cudaIpcMemHandle_t h;
+  const cudaError_t ce = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  static_assert(sizeof(h) == PT_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return PT_OK;
+}
+
+int pt_ipc_import(const void* handle, void** ptr) {
+  if (!handle || !ptr) return PT_ERR_ARGS;
+  *ptr = nullptr;
+  DeviceInfo* di = nullptr;
+  int rc = current_device(di);
+  if (rc != PT_OK) return rc;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t ce = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return ce == cudaSuccess ? PT_OK : cuda_fail(ce);
+}
+
+int pt_ipc_close(void* ptr) {
+  if (!ptr) return PT_OK;
+  const cudaError_t ce = cudaIpcCloseMemHandle(ptr);
+  return ce == cudaSuccess ? PT_OK : cuda_fail(ce);
+}
+
+namespace {
+
+int peer_args(const pt_peer_group* grp, int H, int K, pt::PeerArgs& pa) {
+  if (!grp || grp->world < 2 || grp->world > PT_MAX_PEERS || grp->rank < 0 || grp->rank >= grp->world ||
+      grp->epoch == 0)
+    return PT_ERR_ARGS;
+  const size_t data = 2ull * grp->world * H * K * sizeof(float);
+  for (int r = 0; r < grp->world; ++r) {
+    if (!grp->bufs[r] || !aligned16(grp->bufs[r])) return PT_ERR_ARGS;
+    pa.data[r] = static_cast<float*>(grp->bufs[r]);
+    pa.flags[r] = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(grp->bufs[r]) + (data + 255) / 256 * 256);
+  }
+  pa.rank = grp->rank;
+  pa.world = grp->world;
+  pa.H = H;
+  pa.K = K;
+  pa.epoch = grp->epoch;
+  return PT_OK;
+}
+
+int launch_peer_allreduce(float* dk, const pt::PeerArgs& pa, unsigned* err, cudaStream_t stream) {
+  pt::peer_allreduce_kernel<<<pa.H, 64, 0, stream>>>(dk, pa, err);
+  const cudaError_t ce = cudaGetLastError();
+  return ce == cudaSuccess ? PT_OK : cuda_fail(ce);
+}
+
+}  // namespace
+
+int pt_allreduce_peer(float* dk, int H, int K, const pt_peer_group* grp, void* stream) {
+  if (!dk || H < 1 || K < 1 || K > PT_MAX_K) return PT_ERR_ARGS;
+  pt::PeerArgs pa{};
+  int rc = peer_args(grp, H, K, pa);
+  if (rc != PT_OK) return rc;
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device(di)) != PT_OK) return rc;
+  return launch_peer_allreduce(dk, pa, di->err, static_cast<cudaStream_t>(stream));
+}
+
+int pt_dx_dk_allreduce(const float* dy, const float* x, const float* k, float* dx, float* dk, int B, int H,
+                       int L, int K, void* ws, size_t ws_bytes, const pt_peer_group* grp, void* stream_v) {
+  int rc = check_common(dy, x, k, B, H, L, K);
+  if (rc != PT_OK) return rc;
+  if (!dk || (B > 0 && !dx)) return PT_ERR_ARGS;
+  pt::PeerArgs pa{};
+  if ((rc = peer_args(grp, H, K, pa)) != PT_OK) return rc;
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device(di)) != PT_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (B > 0) {
+    Plan p;
+    if (plan_backward(B, H, L, K, *di, p) == 1 && p.sched.direct)
+      return launch_fused(p, dy, x, k, dx, dk, PT_DK_DETERMINISTIC, ws, di->err, stream, &pa);
+  }
+  if ((rc = pt_dx_dk(dy, x, k, dx, dk, B, H, L, K, PT_DK_DETERMINISTIC, ws, ws_bytes, stream_v)) != PT_OK)
+    return rc;
+  return launch_peer_allreduce(dk, pa, di->err, stream);
+}
+
+int pt_dx_dk_allreduce_fused(int B, int H, int L, int K) {
+  if (B < 1 || H < 1 || L < 1 || K < 1 || L > PT_MAX_L || K > PT_MAX_K) return 0;
+  DeviceInfo* di = nullptr;
+  if (current_device(di) != PT_OK) return 0;
+  Plan p;
+  return (plan_backward(B, H, L, K, *di, p) == 1 && p.sched.direct) ? 1 : 0;
 }
 
 int pt_selftest_wait_timeout(unsigned long long limit_ns, void* out, void* stream) {

@@ -51,6 +51,7 @@
 // undefined.
 #pragma once
 
+#include "pt_peer.cuh"
 #include "pt_tc.h"
 #include "pt_tc_kernels.cuh"
 
@@ -257,14 +258,16 @@ __device__ __forceinline__ void bwd_build_toeplitz(unsigned char* bm, const floa
 }
 
 // part: workspace of [slots][4][K] partials (unused when sc.direct); dk: written
-// directly (=, or += when accumulate != 0) when sc.direct.
+// directly (=, or += when accumulate != 0) when sc.direct -- then, with
+// pa.world > 1, as the sum over the ranks of their dK rows, exchanged through
+// the other GPUs' memory by the same CTA that computed the row (pt_peer.cuh).
 template <int K>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tm_dy128, const __grid_constant__ CUtensorMap tm_dy64,
                   const __grid_constant__ CUtensorMap tm_x128, const __grid_constant__ CUtensorMap tm_x64,
                   const __grid_constant__ CUtensorMap tm_dx128, const __grid_constant__ CUtensorMap tm_dx64,
                   const float* __restrict__ taps, float* __restrict__ part, float* __restrict__ dk,
-                  const BwdSched sc, int accumulate, unsigned* err) {
+                  const BwdSched sc, int accumulate, const PeerArgs pa, unsigned* err) {
   using GG = Geo<3>;
   using BG = BwdGeo;
   constexpr int N = GG::N;
@@ -536,9 +539,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         named_barrier(2, BWD_ROWS);
         const float* red = reinterpret_cast<const float*>(sm + BG::OFF_RED);
         const int h = first.ch;
-        for (int j = ct; j < K; j += BWD_ROWS) {
-          const float sum = ((red[j] + red[L + j]) + red[2 * L + j]) + red[3 * L + j];
-          float* dst = dk + static_cast<size_t>(h) * K + j;
+        float sum = 0.f;
+        if (ct < K) sum = ((red[ct] + red[L + ct]) + red[2 * L + ct]) + red[3 * L + ct];
+        // Data-parallel step: the channel's dK summed over the ranks right here.
+        bool write = true;
+        if (pa.world > 1) write = peer_sum_row(pa, h, ct, BWD_ROWS, 2, sum, sum, err);
+        if (write && ct < K) {
+          float* dst = dk + static_cast<size_t>(h) * K + ct;
           *dst = accumulate ? *dst + sum : sum;
         }
       }

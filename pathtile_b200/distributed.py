@@ -3,10 +3,13 @@
 The reference is single-GPU; on an 8xB200 box the batch dimension shards
 naturally: FWD and dX are independent per (b, h) sequence and need no
 communication, and dK is a sum over b, so each rank computes dK of its batch
-slice and one all-reduce (sum) of the [H, K] filter gradient -- 24,576 bytes
-at H=128, K=48 -- combines them.  One process per GPU, ``torch.distributed``
-over NCCL (NVLink / NVSwitch) for that all-reduce; each rank reads only its
-own HBM.
+slice and the [H, K] filter gradients -- 24,576 bytes at H=128, K=48 -- are
+summed over the ranks.  One process per GPU with ``torch.distributed`` for the
+plumbing.  The sum runs either as an NCCL all-reduce after the backward, or
+(``PeerExchange``) inside the backward kernel itself: the CTA that computed a
+channel's dK row stores it into every other GPU's exchange buffer over NVLink
+and adds the ranks' rows (pt_dx_dk_allreduce).  Each rank reads only its own
+HBM; the exchange writes into the peers' buffers.
 
 Batch split: rank r of n owns rows [b0, b1) with the first ``B % n`` ranks
 holding one extra batch (``shard_range``); uneven splits are allowed, a rank
@@ -14,12 +17,13 @@ may own zero batches.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 
 ComputeFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], tuple[torch.Tensor, torch.Tensor, torch.Tensor]]
 
@@ -52,14 +56,114 @@ def allreduce_dk(gk: torch.Tensor, group=None) -> torch.Tensor:
 
 
 def data_parallel_step(x_local: torch.Tensor, k: torch.Tensor, dy_local: torch.Tensor,
-                       compute: ComputeFn | None = None, group=None):
+                       compute: ComputeFn | None = None, group=None, exchange: "PeerExchange | None" = None):
     """One training-path step on this rank's batch shard.
 
-    Returns (y_local, dx_local, dk) where dk is already summed over all ranks.
-    ``compute`` defaults to the native GPU kernels; it is injectable so the
-    sharding and reduction logic can be exercised on CPU ranks.
+    Returns (y_local, dx_local, dk) where dk is already summed over all ranks:
+    through ``exchange`` (peer memory, inside the backward kernel where it
+    applies) when given, else by an NCCL all-reduce.  ``compute`` defaults to
+    the native GPU kernels; it is injectable so the sharding and reduction logic
+    can be exercised on CPU ranks.
     """
+    if exchange is not None and compute is None:
+        y = ops.fwd(x_local, k)
+        gk = torch.empty_like(k)
+        gx = dx_dk_allreduce(dy_local, x_local, k, gk, exchange)
+        return y, gx, gk
     fn = compute or native_compute
     y, gx, gk = fn(x_local, k, dy_local)
     allreduce_dk(gk, group)
     return y, gx, gk
+
+
+class PeerExchange:
+    """Exchange buffers for summing dK over the ranks through peer memory.
+
+    Every rank allocates one buffer on its GPU (``pt_peer_alloc``, zeroed),
+    exports its CUDA IPC handle, gathers the others' over ``torch.distributed``
+    and maps them; ``group()`` returns the ``pt_peer_group`` of the next call
+    (the epoch advances by one per call on every rank).  Collective: every rank
+    of the process group constructs it, in the same order.  ``close()`` unmaps
+    the peers' buffers and frees the own one once every rank is done with it.
+    """
+
+    def __init__(self, H: int, K: int, device: torch.device, group=None) -> None:
+        self.lib = _lib.load()
+        self.group_ = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if not 2 <= self.world <= _lib.PT_MAX_PEERS:
+            raise ValueError(f"peer exchange needs 2..{_lib.PT_MAX_PEERS} ranks, got {self.world}")
+        self.H, self.K, self.device = H, K, device
+        self.nbytes = int(self.lib.pt_peer_buffer_bytes(self.world, H, K))
+        self._own = ctypes.c_void_p()
+        self._imported: list[ctypes.c_void_p] = []
+        with torch.cuda.device(device):
+            _lib.check(self.lib.pt_peer_alloc(self.nbytes, ctypes.byref(self._own)), "pt_peer_alloc")
+            handle = ctypes.create_string_buffer(_lib.PT_IPC_HANDLE_BYTES)
+            _lib.check(self.lib.pt_ipc_export(self._own, handle), "pt_ipc_export")
+            handles: list = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            bufs = (ctypes.c_void_p * _lib.PT_MAX_PEERS)()
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bufs[r] = self._own.value
+                    continue
+                ptr = ctypes.c_void_p()
+                hb = ctypes.create_string_buffer(bytes(h), _lib.PT_IPC_HANDLE_BYTES)
+                _lib.check(self.lib.pt_ipc_import(hb, ctypes.byref(ptr)), "pt_ipc_import")
+                self._imported.append(ptr)
+                bufs[r] = ptr.value
+        self._grp = _lib.PeerGroup(self.rank, self.world, bufs, 0)
+        dist.barrier(group=group)
+
+    def group(self) -> ctypes.c_void_p:
+        """The pt_peer_group of the next call (advances the epoch)."""
+        self._grp.epoch += 1
+        return ctypes.cast(ctypes.pointer(self._grp), ctypes.c_void_p)
+
+    def close(self) -> None:
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group_)
+        with torch.cuda.device(self.device):
+            for ptr in self._imported:
+                self.lib.pt_ipc_close(ptr)
+            dist.barrier(group=self.group_)
+            self.lib.pt_peer_free(self._own)
+        self._own = None
+
+
+def dx_dk_allreduce(dy: torch.Tensor, x: torch.Tensor, k: torch.Tensor, gk: torch.Tensor, exchange: PeerExchange,
+                    gx: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """dX of this shard into gx and dK summed over the ranks into gk (deterministic:
+    gk = the sum), the sum done through the peers' exchange buffers -- inside the
+    fused backward kernel where it runs with one CTA per channel."""
+    B, H, L, K = ops.check_shapes(x, k)
+    if tuple(dy.shape) != (B, H, L) or tuple(gk.shape) != (H, K):
+        raise ValueError("gy must be shaped like x and gk like k")
+    if (H, K) != (exchange.H, exchange.K):
+        raise ValueError("the exchange was built for another [H, K]")
+    if gx is None:
+        gx = torch.empty_like(dy, memory_format=torch.contiguous_format)
+    for t, n in ((dy, "gy"), (x, "x"), (k, "k"), (gk, "gk"), (gx, "gx")):
+        ops._ensure_cuda_f32(t, n)
+        ops._ensure_raw(t, n)
+    lib = _lib.load()
+    dev = x.device
+    with torch.cuda.device(dev):
+        ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
+        need = int(lib.pt_dx_dk_workspace_bytes(B, H, L, K)) if B > 0 else 0
+        if need > 0:
+            ws = workspace if workspace is not None else ops.WORKSPACES.get(dev, need)
+            ws_ptr, ws_bytes = ops._ptr(ws), ws.numel() * ws.element_size()
+        st = lib.pt_dx_dk_allreduce(ops._ptr(dy), ops._ptr(x), ops._ptr(k), ops._ptr(gx), ops._ptr(gk), B, H, L, K,
+                                    ws_ptr, ws_bytes, exchange.group(), ops._stream(dev))
+    _lib.check(st, "pt_dx_dk_allreduce")
+    return gx
+
+
+def peer_fused(B: int, H: int, L: int, K: int) -> bool:
+    """True when dx_dk_allreduce sums dK inside the backward kernel at this shape."""
+    return bool(_lib.load().pt_dx_dk_allreduce_fused(B, H, L, K))

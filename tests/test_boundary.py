@@ -121,6 +121,22 @@ def test_runtime_launch_options_map_reference_arguments():
     assert list(f.rows_per_tile) == [0, 0, 0]  # all frozen
 
 
+def test_peer_exchange_argument_checks(native_lib):
+    assert native_lib.pt_peer_buffer_bytes(0, 128, 48) == 0
+    assert native_lib.pt_peer_buffer_bytes(9, 128, 48) == 0
+    assert native_lib.pt_peer_buffer_bytes(2, 128, 48) == 2 * 2 * 128 * 48 * 4 + 2 * 2 * 128 * 4
+    grp = _lib.PeerGroup(0, 2, (ctypes.c_void_p * _lib.PT_MAX_PEERS)(0x10000, 0x20000), 0)
+    pg = ctypes.cast(ctypes.pointer(grp), ctypes.c_void_p)
+    # epoch 0 and a missing group are rejected before any CUDA call
+    assert native_lib.pt_dx_dk_allreduce(FAKE, FAKE, FAKE, FAKE, FAKE, 2, 4, 16, 8, NULL, 0, pg, NULL) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_dx_dk_allreduce(FAKE, FAKE, FAKE, FAKE, FAKE, 2, 4, 16, 8, NULL, 0, NULL, NULL) == _lib.PT_ERR_ARGS
+    grp.epoch, grp.world = 1, 1
+    assert native_lib.pt_allreduce_peer(FAKE, 4, 8, pg, NULL) == _lib.PT_ERR_ARGS
+    grp.world, grp.rank = 2, 2
+    assert native_lib.pt_allreduce_peer(FAKE, 4, 8, pg, NULL) == _lib.PT_ERR_ARGS
+    assert native_lib.pt_peer_alloc(0, ctypes.byref(ctypes.c_void_p())) == _lib.PT_ERR_ARGS
+
+
 def test_wait_selftest_argument_checks(native_lib):
     assert native_lib.pt_selftest_wait_timeout(0, FAKE, NULL) == _lib.PT_ERR_ARGS
     assert native_lib.pt_selftest_wait_timeout(2_000_000_000, FAKE, NULL) == _lib.PT_ERR_ARGS

@@ -69,3 +69,70 @@ def test_two_rank_batch_sharding_matches_oracle(tmp_path, shape):
     scale = float(np.abs(ref).max())
     for r in range(2):
         np.testing.assert_allclose(np.load(tmp_path / f"r{r}_gk.npy"), ref, rtol=1e-4, atol=1e-4 * scale)
+
+
+def _rank_main_peer(rank: int, world: int, port: int, out_dir: str, shape, calls: int) -> None:
+    """The sharded step with dK summed through the peers' exchange buffers,
+    `calls` times in a row (the epochs alternate the exchange slots)."""
+    import sys
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    ex = None
+    try:
+        from oracle import reference_torch
+        from pathtile_b200 import ops
+        from pathtile_b200.distributed import PeerExchange, data_parallel_step, peer_fused, shard_range
+
+        B, H, L, K = shape
+        ex = PeerExchange(H, K, dev)
+        b0, b1 = shard_range(B, rank, world)
+        for call in range(calls):
+            x, k, dy = reference_torch.make_inputs(B, H, L, K, seed=100 + call)
+            y, gx, gk = data_parallel_step(x[b0:b1].to(dev), k.to(dev), dy[b0:b1].to(dev), exchange=ex)
+            torch.cuda.synchronize()
+            np.save(os.path.join(out_dir, f"c{call}_r{rank}_gx.npy"), gx.cpu().numpy())
+            np.save(os.path.join(out_dir, f"c{call}_r{rank}_gk.npy"), gk.cpu().numpy())
+        with open(os.path.join(out_dir, f"r{rank}_info.txt"), "w") as f:
+            f.write(f"{int(peer_fused(b1 - b0, H, L, K))} {ops.device_error()}")
+    finally:
+        if ex is not None:
+            ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("shape,fused", [((2048, 128, 48, 48), 1), ((301, 64, 37, 13), 0)])
+def test_two_rank_peer_memory_dk_sum_matches_oracle(tmp_path, shape, fused):
+    """dK summed over the ranks inside the fused backward kernel (one CTA per
+    channel) or by the standalone peer kernel after the backward: every rank gets
+    the same bits, equal to the full-batch FP64 dK within 1e-4, on four calls in
+    a row."""
+    import torch.multiprocessing as mp
+
+    from oracle import c_oracle, reference_torch
+
+    calls = 4
+    mp.spawn(_rank_main_peer, args=(2, _free_port(), str(tmp_path), shape, calls), nprocs=2, join=True)
+    B, H, L, K = shape
+    for r in range(2):
+        kind, err = (int(v) for v in (tmp_path / f"r{r}_info.txt").read_text().split())
+        assert err == 0
+        if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+            assert kind == fused
+    for call in range(calls):
+        x, k, dy = reference_torch.make_inputs(B, H, L, K, seed=100 + call)
+        gx = np.concatenate([np.load(tmp_path / f"c{call}_r{r}_gx.npy") for r in range(2)])
+        np.testing.assert_allclose(gx, c_oracle.dx(dy, k), rtol=1e-5, atol=1e-5)
+        ref = c_oracle.dk(dy, x, K)
+        scale = float(np.abs(ref).max())
+        gk0 = np.load(tmp_path / f"c{call}_r0_gk.npy")
+        gk1 = np.load(tmp_path / f"c{call}_r1_gk.npy")
+        assert np.array_equal(gk0, gk1)  # rank-ordered sum: the same bits on every rank
+        np.testing.assert_allclose(gk0, ref, rtol=1e-4, atol=1e-4 * scale)
