@@ -295,10 +295,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     # N > 1: dK summed over the ranks through the peers' exchange buffers (inside
     # the fused backward kernel where it applies), or by an NCCL all-reduce.
     exchange = None
+    exchange_note = None
     if dist is not None and args.collective == "fused":
-        from pathtile_b200.distributed import PeerExchange, dx_dk_allreduce, peer_fused
+        from pathtile_b200.distributed import PeerExchange, PeerExchangeUnavailable, dx_dk_allreduce, peer_fused
 
-        exchange = PeerExchange(H, K, dev)
+        try:
+            exchange = PeerExchange(H, K, dev)
+        except PeerExchangeUnavailable as exc:  # every rank falls back alike
+            exchange_note = f"peer exchange unavailable ({exc}); NCCL all_reduce used"
 
     def compute(nccl: bool = False):
         ops.fwd(x, k, y)
@@ -369,7 +373,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         split = {"collective": ("dK summed inside the backward kernel through the peers' memory (NVLink)"
                                 if exchange is not None and peer_fused(B, H, L, K) else
                                 "peer-memory sum kernel after the backward" if exchange is not None else
-                                "NCCL all_reduce after the backward"),
+                                exchange_note or "NCCL all_reduce after the backward"),
                  "nccl_variant": {"step_ms": nccl_step, "compute_ms": comp, "allreduce_ms": red}}
 
     # Per-phase times under the reference protocol, each phase timed separately.

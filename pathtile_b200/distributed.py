@@ -76,6 +76,11 @@ def data_parallel_step(x_local: torch.Tensor, k: torch.Tensor, dy_local: torch.T
     return y, gx, gk
 
 
+class PeerExchangeUnavailable(RuntimeError):
+    """Some rank could not allocate, export or map an exchange buffer (raised on
+    every rank alike)."""
+
+
 class PeerExchange:
     """Exchange buffers for summing dK over the ranks through peer memory.
 
@@ -98,24 +103,43 @@ class PeerExchange:
         self.nbytes = int(self.lib.pt_peer_buffer_bytes(self.world, H, K))
         self._own = ctypes.c_void_p()
         self._imported: list[ctypes.c_void_p] = []
+        bufs = (ctypes.c_void_p * _lib.PT_MAX_PEERS)()
+        failure = ""
         with torch.cuda.device(device):
-            _lib.check(self.lib.pt_peer_alloc(self.nbytes, ctypes.byref(self._own)), "pt_peer_alloc")
+            # Every rank takes part in the same collectives whatever fails locally;
+            # the outcome is agreed on with one all-reduce, so either every rank
+            # has the exchange or every rank raises PeerExchangeUnavailable.
             handle = ctypes.create_string_buffer(_lib.PT_IPC_HANDLE_BYTES)
-            _lib.check(self.lib.pt_ipc_export(self._own, handle), "pt_ipc_export")
+            st = self.lib.pt_peer_alloc(self.nbytes, ctypes.byref(self._own))
+            if st == _lib.PT_OK:
+                st = self.lib.pt_ipc_export(self._own, handle)
+            if st != _lib.PT_OK:
+                failure = f"rank {self.rank}: exchange buffer: {_lib.status_string(st)}"
             handles: list = [None] * self.world
-            dist.all_gather_object(handles, handle.raw, group=group)
-            bufs = (ctypes.c_void_p * _lib.PT_MAX_PEERS)()
+            dist.all_gather_object(handles, handle.raw if not failure else None, group=group)
             for r, h in enumerate(handles):
+                if failure:
+                    break
                 if r == self.rank:
                     bufs[r] = self._own.value
                     continue
+                if h is None:
+                    failure = f"rank {r} has no exchange buffer"
+                    break
                 ptr = ctypes.c_void_p()
                 hb = ctypes.create_string_buffer(bytes(h), _lib.PT_IPC_HANDLE_BYTES)
-                _lib.check(self.lib.pt_ipc_import(hb, ctypes.byref(ptr)), "pt_ipc_import")
+                st = self.lib.pt_ipc_import(hb, ctypes.byref(ptr))
+                if st != _lib.PT_OK:
+                    failure = f"rank {self.rank} cannot map rank {r}'s buffer: {_lib.status_string(st)}"
+                    break
                 self._imported.append(ptr)
                 bufs[r] = ptr.value
+            ok = torch.tensor([0 if failure else 1], device=device, dtype=torch.int32)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            if int(ok.item()) == 0:
+                self.close()
+                raise PeerExchangeUnavailable(failure or "another rank could not set up its exchange")
         self._grp = _lib.PeerGroup(self.rank, self.world, bufs, 0)
-        dist.barrier(group=group)
 
     def group(self) -> ctypes.c_void_p:
         """The pt_peer_group of the next call (advances the epoch)."""
@@ -123,6 +147,8 @@ class PeerExchange:
         return ctypes.cast(ctypes.pointer(self._grp), ctypes.c_void_p)
 
     def close(self) -> None:
+        """Collective: unmap the peers' buffers, then free the own one once every
+        rank has unmapped it."""
         if self._own is None:
             return
         torch.cuda.synchronize(self.device)
@@ -130,8 +156,10 @@ class PeerExchange:
         with torch.cuda.device(self.device):
             for ptr in self._imported:
                 self.lib.pt_ipc_close(ptr)
+            self._imported = []
             dist.barrier(group=self.group_)
-            self.lib.pt_peer_free(self._own)
+            if self._own.value:
+                self.lib.pt_peer_free(self._own)
         self._own = None
 
 
