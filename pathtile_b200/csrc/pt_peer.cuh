@@ -45,12 +45,20 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   return v;
 }
 
+struct PeerSum {
+  float sum;  // the rank-ordered sum (threads j < K)
+  int ok;     // 0: a peer's row did not arrive in time
+};
+
 // Threads [0, nthr) of the CTA (named barrier `bar`; nthr >= max(K, W), a
 // multiple of 32) exchange row c: thread j < K brings value v of tap j and gets
-// the rank-ordered sum in `out`.  Returns false (for every participating thread)
-// when a peer's row did not arrive in time.
-__device__ __forceinline__ bool peer_sum_row(const PeerArgs& pa, int c, int tid, int nthr, int bar, float v,
-                                             float& out, unsigned* err) {
+// the rank-ordered sum back.  ok is 0 (for every participating thread) when a
+// peer's row did not arrive in time.  Not inlined: it runs once per CTA, after
+// the kernel's main loop, and inlined its addressing and waits raise the
+// register demand of the loop's own role enough to spill.  `pa` refers to a
+// __grid_constant__ kernel parameter, so passing its address copies nothing.
+static __device__ __noinline__ PeerSum peer_sum_row(const PeerArgs& pa, int c, int tid, int nthr, int bar, float v,
+                                                    unsigned* err) {
   const int par = static_cast<int>(pa.epoch & 1u);
   const size_t row = static_cast<size_t>(par * pa.world + pa.rank) * pa.H + c;
   if (tid < pa.K) {
@@ -73,29 +81,26 @@ __device__ __forceinline__ bool peer_sum_row(const PeerArgs& pa, int c, int tid,
       }
     }
   }
-  ok = !named_barrier_or(bar, nthr, !ok);
-  if (ok && tid < pa.K) {
+  PeerSum res{0.f, !named_barrier_or(bar, nthr, !ok)};
+  if (res.ok && tid < pa.K) {
     __threadfence_system();
     const float* mine = pa.data[pa.rank];
-    float s = 0.f;
     for (int r = 0; r < pa.world; ++r)
-      s += __ldcg(mine + (static_cast<size_t>(par * pa.world + r) * pa.H + c) * pa.K + tid);
-    out = s;
+      res.sum += __ldcg(mine + (static_cast<size_t>(par * pa.world + r) * pa.H + c) * pa.K + tid);
   }
-  return ok;
+  return res;
 }
 
 #ifdef PT_KERNELS_IMPL
 // In-place sum over the ranks of dk[H][K]: one CTA per row, one thread per tap
 // (blockDim.x = K rounded up to 32, at least W).
-__global__ void __launch_bounds__(64) peer_allreduce_kernel(float* __restrict__ dk, const PeerArgs pa,
+__global__ void __launch_bounds__(64) peer_allreduce_kernel(float* __restrict__ dk, const __grid_constant__ PeerArgs pa,
                                                             unsigned* err) {
   const int c = static_cast<int>(blockIdx.x);
   const int tid = static_cast<int>(threadIdx.x);
   const float v = (tid < pa.K) ? dk[static_cast<size_t>(c) * pa.K + tid] : 0.f;
-  float out = 0.f;
-  if (peer_sum_row(pa, c, tid, static_cast<int>(blockDim.x), 1, v, out, err) && tid < pa.K)
-    dk[static_cast<size_t>(c) * pa.K + tid] = out;
+  const PeerSum r = peer_sum_row(pa, c, tid, static_cast<int>(blockDim.x), 1, v, err);
+  if (r.ok && tid < pa.K) dk[static_cast<size_t>(c) * pa.K + tid] = r.sum;
 }
 #endif  // PT_KERNELS_IMPL
 

@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                   const __grid_constant__ CUtensorMap tm_x128, const __grid_constant__ CUtensorMap tm_x64,
                   const __grid_constant__ CUtensorMap tm_dx128, const __grid_constant__ CUtensorMap tm_dx64,
                   const float* __restrict__ taps, float* __restrict__ part, float* __restrict__ dk,
-                  const BwdSched sc, int accumulate, const PeerArgs pa, unsigned* err) {
+                  const BwdSched sc, int accumulate, const __grid_constant__ PeerArgs pa, unsigned* err) {
   using GG = Geo<3>;
   using BG = BwdGeo;
   constexpr int N = GG::N;
@@ -543,7 +543,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         if (ct < K) sum = ((red[ct] + red[L + ct]) + red[2 * L + ct]) + red[3 * L + ct];
         // Data-parallel step: the channel's dK summed over the ranks right here.
         bool write = true;
-        if (pa.world > 1) write = peer_sum_row(pa, h, ct, BWD_ROWS, 2, sum, sum, err);
+        if (pa.world > 1) {
+          const PeerSum r = peer_sum_row(pa, h, ct, BWD_ROWS, 2, sum, err);
+          write = r.ok;
+          sum = r.sum;
+        }
         if (write && ct < K) {
           float* dst = dk + static_cast<size_t>(h) * K + ct;
           *dst = accumulate ? *dst + sum : sum;
