@@ -5,8 +5,9 @@
 A step is one FWD + dX + dK pass (dK deterministic two-pass, written, not
 accumulated, so no zero-fill exists) over one batch of the primary workload,
 B=16384 per GPU, H=128, L=48, K=48 (weak scaling: at N=8 the job is the
-batch-sharded x[131072,128,48] configuration; for N>1 each step also
-all-reduces dK[128,48] over NCCL).  Inputs are resident in HBM and each of
+batch-sharded x[131072,128,48] configuration; for N>1 each step also sums
+dK[128,48] over the ranks, through NVLink peer memory inside the backward
+kernel, or with the NCCL all-reduce that is timed beside it).  Inputs are resident in HBM and each of
 x, dy, y, dX is 402 MB, larger than the 126 MB L2, so no L2 flush is needed.
 
 Printed (rank 0, one JSON line): ``value`` = whole-job effective GB/s of
@@ -15,13 +16,15 @@ phases -- over the device-timed step (CUDA events, max over ranks; the step's
 backward is one fused kernel, which moves fewer bytes than the formula
 credits, see ``step_moved_bytes``); ``aggregate_ms`` = the sum of the three
 phases timed separately under the reference's protocol (each phase: 3 trials
-of 50 untimed + 100 timed launches, median of the trial means; outputs and the
+of 50 untimed + 100 timed launches, mean of the trial means; outputs and the
 dK workspace allocated before timing); ``roofline`` for the dominant kernel of
-the step; ``cpu_baseline`` = the reference's PyTorch CPU path timed on this
+the step, its duration taken inside the timed steps (CUDA events between the
+step's kernels, on the launching stream); ``cpu_baseline`` = the reference's PyTorch CPU path timed on this
 host under the reference's protocol (1-GPU runs only); ``e2e`` = the same pass
 through the host-buffer API (pinned host tensors, copies inside the timed
 region); ``clocks`` sampled by NVML during the timed region (and per phase).
-For N > 1, ``compute_ms`` and ``allreduce_ms`` split the step (max over ranks).
+For N > 1, ``step_split`` gives the NCCL variant's ``compute_ms`` and
+``allreduce_ms`` (max over ranks).
 
 ``--impl reference`` times the reference's own CPU implementation (its PyTorch
 path F.pad + grouped conv1d with autograd, restated in oracle/) on this host's
@@ -304,8 +307,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         except PeerExchangeUnavailable as exc:  # every rank falls back alike
             exchange_note = f"peer exchange unavailable ({exc}); NCCL all_reduce used"
 
-    def compute(nccl: bool = False):
+    def compute(nccl: bool = False, mid=None):
         ops.fwd(x, k, y)
+        if mid is not None:  # between the FWD and the backward: splits the step per kernel
+            mid.record(stream)
         if exchange is not None and not nccl:
             dx_dk_allreduce(dy, x, k, gk, exchange, gx=gx)
         elif fused:
@@ -314,8 +319,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             ops.dx(dy, k, gx)
             ops.dk(dy, x, gk, mode="deterministic")
 
-    def step(nccl: bool = False):
-        compute(nccl)
+    def step(nccl: bool = False, mid=None):
+        compute(nccl, mid)
         if dist is not None and (exchange is None or nccl):
             dist.all_reduce(gk)
 
@@ -324,9 +329,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
-    # For N > 1, events around each step's compute and its all-reduce split the
-    # step; they are recorded on the launching stream and add no device work.
+    # Events between the kernels of each timed step give every kernel's device
+    # time inside the timed region (the roofline figure below); for N > 1 with
+    # NCCL they also split off the all-reduce.  They are recorded on the
+    # launching stream and add no device work.
     marks = []
+    in_step = []  # per step: (step start, after FWD, after the backward)
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
         if dist is not None:
@@ -334,19 +342,21 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s_ev.record(stream)
         for _ in range(args.steps):
-            if dist is None or exchange is not None:
-                step()
-                continue
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
             ev[0].record(stream)
-            compute()
+            compute(mid=ev[3])
             ev[1].record(stream)
-            dist.all_reduce(gk)
+            if dist is not None and exchange is None:
+                dist.all_reduce(gk)
             ev[2].record(stream)
-            marks.append(ev)
+            in_step.append((ev[0], ev[3], ev[1]))
+            if dist is not None and exchange is None:
+                marks.append(ev[:3])
         e_ev.record(stream)
         e_ev.synchronize()
         step_ms = s_ev.elapsed_time(e_ev) / args.steps
+    step_fwd_ms = statistics.mean(a.elapsed_time(m) for a, m, _ in in_step)
+    step_bwd_ms = statistics.mean(m.elapsed_time(b) for _, m, b in in_step)
     split = None
     if dist is not None:
         if exchange is not None:
@@ -367,9 +377,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         nccl_step = statistics.mean(a.elapsed_time(c) for a, _, c in marks)
         comp = statistics.mean(a.elapsed_time(b) for a, b, _ in marks)
         red = statistics.mean(b.elapsed_time(c) for _, b, c in marks)
-        t = torch.tensor([step_ms, comp, red, nccl_step], device=dev, dtype=torch.float64)
+        t = torch.tensor([step_ms, comp, red, nccl_step, step_fwd_ms, step_bwd_ms], device=dev,
+                         dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_ms, comp, red, nccl_step = map(float, t.tolist())
+        step_ms, comp, red, nccl_step, step_fwd_ms, step_bwd_ms = map(float, t.tolist())
         split = {"collective": ("dK summed inside the backward kernel through the peers' memory (NVLink)"
                                 if exchange is not None and peer_fused(B, H, L, K) else
                                 "peer-memory sum kernel after the backward" if exchange is not None else
@@ -463,13 +474,22 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     total_bytes = 3 * pb * world
     fused_on = fused and ops.fused_backward(B, H, L, K)
     step_kernels = ("fwd", "bwd_fused") if fused_on else ("fwd", "bwd_input", "bwd_weight")
-    dominant = max(step_kernels, key=phase_ms.get)
     # Algorithmic bytes of a launch: FWD / dX / dK move two activations + k; the
     # fused backward reads dy and x, writes dx, reads k and writes dK.
     kernel_bytes = {p: pb for p in ("fwd", "bwd_input", "bwd_weight")}
     kernel_bytes["bwd_fused"] = (3 * B * H * L + 2 * H * K) * 4
     step_moved = kernel_bytes["fwd"] + (kernel_bytes["bwd_fused"] if fused_on else 2 * pb)
-    achieved = kernel_bytes[dominant] / (phase_ms[dominant] / 1e3) / 1e9
+    # The dominant kernel's duration inside the timed steps (events between the
+    # step's two kernels); with dX then dK the backward is two launches, and the
+    # separately timed phases stand in.
+    if fused_on:
+        in_step_ms = {"fwd": step_fwd_ms, "bwd_fused": step_bwd_ms}
+        dominant = max(step_kernels, key=in_step_ms.get)
+        dominant_ms, measured_in = in_step_ms[dominant], f"the {args.steps} timed steps (CUDA events between the step's kernels)"
+    else:
+        dominant = max(step_kernels, key=phase_ms.get)
+        dominant_ms, measured_in = phase_ms[dominant], "its phase loop (reference protocol)"
+    achieved = kernel_bytes[dominant] / (dominant_ms / 1e3) / 1e9
     sm_mhz = clocks.summary()["sm_mhz"] or 1965.0
     fma_peak = runtime.fp32_fma_peak_tflops(torch.cuda.get_device_properties(dev).multi_processor_count,
                                             float(sm_mhz))
@@ -531,6 +551,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "frac": achieved / hbm,
             "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured" else "fallback",
             "algorithmic_bytes_per_launch": kernel_bytes[dominant],
+            "kernel_ms": dominant_ms,
+            "measured_in": measured_in,
+            "in_step_ms": {"fwd": step_fwd_ms, "backward": step_bwd_ms},
             "traffic": (traffic or {}).get(dominant),
             "fp32_fma_peak_tflops_at_sampled_clock": fma_peak,
         },
