@@ -113,25 +113,30 @@ def _rank_main_peer(rank: int, world: int, port: int, out_dir: str, shape, calls
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("shape,fused", [((2048, 128, 48, 48), 1), ((301, 64, 37, 13), 0)])
+@pytest.mark.parametrize("shape,fused", [((2048, 128, 48, 48), 1), ((301, 64, 37, 13), 0), ("mixed", None)])
 def test_peer_memory_dk_sum_matches_oracle(tmp_path, shape, fused):
     """dK summed over every visible GPU's rank inside the fused backward kernel (one CTA per
     channel) or by the standalone peer kernel after the backward: every rank gets
     the same bits, equal to the full-batch FP64 dK within 1e-4, on four calls in
-    a row."""
+    a row.  "mixed": at H = 64 a shard of 128 rows runs the fused kernel with one
+    CTA per channel and a shard of 129 rows needs two CTAs per channel, so with
+    B = 128 * world + 1 rank 0 takes the separate path (backward, then the peer
+    kernel) while the others sum inside the backward kernel, through the same slots."""
     import torch.multiprocessing as mp
 
     from oracle import c_oracle, reference_torch
 
     calls = 4
     world = _peer_world()
+    if shape == "mixed":
+        shape = (128 * world + 1, 64, 48, 48)
     mp.spawn(_rank_main_peer, args=(world, _free_port(), str(tmp_path), shape, calls), nprocs=world, join=True)
     B, H, L, K = shape
     for r in range(world):
         kind, err = (int(v) for v in (tmp_path / f"r{r}_info.txt").read_text().split())
         assert err == 0
         if torch.cuda.get_device_properties(0).multi_processor_count == 148:
-            assert kind == fused
+            assert kind == (fused if fused is not None else int(r > 0))
     for call in range(calls):
         x, k, dy = reference_torch.make_inputs(B, H, L, K, seed=100 + call)
         gx = np.concatenate([np.load(tmp_path / f"c{call}_r{r}_gx.npy") for r in range(world)])
